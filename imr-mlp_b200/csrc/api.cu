@@ -1,0 +1,728 @@
+// api.cu -- C ABI implementation (include/mtpb200.h): context lifetime,
+// validation, uploads and the EFS pipeline.
+#include "context.hpp"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <exception>
+#include <new>
+#include <string>
+#include <vector>
+
+using namespace mtpb;
+
+namespace mtpb {
+static thread_local std::string g_last_error;
+
+int fail(int status, const std::string &msg)
+{
+    g_last_error = msg;
+    return status;
+}
+
+int cuda_fail(cudaError_t e, const char *where)
+{
+    g_last_error = std::string(where) + ": " + cudaGetErrorString(e);
+    return e == cudaErrorMemoryAllocation ? MTPB_ERR_MEMORY : MTPB_ERR_CUDA;
+}
+} // namespace mtpb
+
+
+
+namespace mtpb {
+
+int set_device(mtpb_context *c)
+{
+    CUDA_TRY(cudaSetDevice(c->device), "cudaSetDevice");
+    return MTPB_OK;
+}
+
+static bool copy_model(const mtpb_model_view *v, ModelHost &m, std::string *err)
+{
+    if (!v) {
+        *err = "model view is NULL";
+        return false;
+    }
+    if (v->species_count <= 0 || v->radial_func_count <= 0 || v->rb_size <= 0 ||
+        v->alpha_index_basic_count <= 0 || v->alpha_index_times_count < 0 ||
+        v->alpha_scalar_moments < 0 || v->alpha_moments_count <= 0) {
+        *err = "model counts must be positive";
+        return false;
+    }
+    if (!v->min_dist || !v->max_dist || !v->alpha_index_basic || !v->alpha_moment_mapping ||
+        !v->radial_coeffs || !v->species_coeffs || !v->moment_coeffs ||
+        (v->alpha_index_times_count > 0 && !v->alpha_index_times)) {
+        *err = "model view has a NULL array";
+        return false;
+    }
+    m.K = v->species_count;
+    m.mu = v->radial_func_count;
+    m.R = v->rb_size;
+    m.split = v->radial_basis_split ? 1 : 0;
+    m.M = v->alpha_moments_count;
+    m.scaling = v->scaling;
+    const int pairs = m.split ? m.K * m.K : 1;
+    m.min_dist.assign(v->min_dist, v->min_dist + pairs);
+    m.max_dist.assign(v->max_dist, v->max_dist + pairs);
+    m.basic.assign(v->alpha_index_basic, v->alpha_index_basic + 4 * v->alpha_index_basic_count);
+    if (v->alpha_index_times_count > 0)
+        m.times.assign(v->alpha_index_times, v->alpha_index_times + 4 * v->alpha_index_times_count);
+    m.mapping.assign(v->alpha_moment_mapping, v->alpha_moment_mapping + v->alpha_scalar_moments);
+    m.radial.assign(v->radial_coeffs, v->radial_coeffs + m.K * m.K * m.mu * m.R);
+    m.species.assign(v->species_coeffs, v->species_coeffs + m.K);
+    m.moment.assign(v->moment_coeffs, v->moment_coeffs + v->alpha_scalar_moments);
+    return true;
+}
+
+static int upload_model(mtpb_context *c)
+{
+    const ModelHost &m = c->model;
+    const int KK = m.K * m.K;
+    std::vector<PairParams> pp(KK);
+    for (int p = 0; p < KK; ++p) {
+        const double rmin = m.pair_min(p), rmax = m.pair_max(p);
+        pp[p] = {rmax + rmin, rmax - rmin, 2.0 / (rmax - rmin), rmax};
+    }
+    c->d_radial = c->arena.get<double>("model_radial", m.radial.size());
+    c->d_species = c->arena.get<double>("model_species", m.K);
+    c->d_pairs = c->arena.get<PairParams>("model_pairs", KK);
+    c->d_recs = c->arena.get<DagRec>("model_dag", c->plan.recs.size());
+    std::vector<int> row0(c->plan.phase_rows.size() + 1, 0);
+    for (size_t i = 0; i < c->plan.phase_rows.size(); ++i)
+        row0[i + 1] = row0[i] + c->plan.phase_rows[i];
+    c->d_phase_row0 = c->arena.get<int>("model_dag_row0", row0.size());
+    if (!c->d_radial || !c->d_species || !c->d_pairs || !c->d_recs || !c->d_phase_row0)
+        return fail(MTPB_ERR_MEMORY, "device allocation for the model failed");
+    CUDA_TRY(cudaMemcpyAsync(c->d_radial, m.radial.data(), sizeof(double) * m.radial.size(),
+                             cudaMemcpyHostToDevice, c->stream),
+             "upload radial");
+    CUDA_TRY(cudaMemcpyAsync(c->d_species, m.species.data(), sizeof(double) * m.K,
+                             cudaMemcpyHostToDevice, c->stream),
+             "upload species");
+    CUDA_TRY(cudaMemcpyAsync(c->d_pairs, pp.data(), sizeof(PairParams) * KK,
+                             cudaMemcpyHostToDevice, c->stream),
+             "upload pairs");
+    CUDA_TRY(cudaMemcpyAsync(c->d_recs, c->plan.recs.data(), sizeof(DagRec) * c->plan.recs.size(),
+                             cudaMemcpyHostToDevice, c->stream),
+             "upload graph");
+    CUDA_TRY(cudaMemcpyAsync(c->d_phase_row0, row0.data(), sizeof(int) * row0.size(),
+                             cudaMemcpyHostToDevice, c->stream),
+             "upload graph phases");
+    CUDA_TRY(cudaStreamSynchronize(c->stream), "model upload");
+    return MTPB_OK;
+}
+
+EdgeArgs edge_args(const mtpb_context *c, int ncenter, const int *types, const int *offsets,
+                   const int *nbr, const double *rx, const double *ry, const double *rz)
+{
+    EdgeArgs a{};
+    a.natoms = ncenter;
+    a.npad = c->npad;
+    a.types = types;
+    a.offsets = offsets;
+    a.nbr = nbr;
+    a.rx = rx;
+    a.ry = ry;
+    a.rz = rz;
+    a.group_maxdeg = c->d_group_maxdeg;
+    a.K = c->model.K;
+    a.R = c->model.R;
+    a.mu_total = c->model.mu;
+    a.scaling = c->model.scaling;
+    a.radial = c->d_radial;
+    a.pairs = c->d_pairs;
+    return a;
+}
+
+// forward moments -> graph -> reverse moments for ncenter centres.
+int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offsets,
+                const int *nbr, const double *rx, const double *ry, const double *rz,
+                double *site_energy, double *dx, double *dy, double *dz)
+{
+    c->npad = ((ncenter + 31) / 32) * 32;
+    c->d_group_maxdeg = c->arena.get<int>("group_maxdeg", c->npad / 32 + 1);
+    double *basic = c->arena.get<double>("basic", (size_t)c->nslot * c->npad + 1);
+    double *adjoint = c->arena.get<double>("adjoint", (size_t)c->nslot * c->npad + 1);
+    if (!c->d_group_maxdeg || !basic || !adjoint)
+        return fail(MTPB_ERR_MEMORY, "device allocation for moments failed");
+    CUDA_TRY(launch_group_maxdeg(ncenter, offsets, c->d_group_maxdeg, c->stream), "group_maxdeg");
+    c->launches++;
+    EdgeArgs a = edge_args(c, ncenter, types, offsets, nbr, rx, ry, rz);
+    CUDA_TRY(cudaEventRecord(c->ev[1], c->stream), "event");
+    CUDA_TRY(launch_moments_fwd(c->shape, a, basic, c->stream), "moments forward");
+    c->launches++;
+    CUDA_TRY(cudaEventRecord(c->ev[2], c->stream), "event");
+    CUDA_TRY(launch_dag(c->plan, c->d_recs, c->d_phase_row0, c->nslot, ncenter, c->npad, types,
+                        c->d_species, basic, adjoint, site_energy, c->stream),
+             "moment graph");
+    c->launches++;
+    CUDA_TRY(cudaEventRecord(c->ev[3], c->stream), "event");
+    CUDA_TRY(launch_moments_rev(c->shape, a, adjoint, dx, dy, dz, c->stream), "moments reverse");
+    c->launches++;
+    CUDA_TRY(cudaEventRecord(c->ev[4], c->stream), "event");
+    return MTPB_OK;
+}
+
+static int check_structures(const mtpb_context *c, const mtpb_structures *in)
+{
+    if (!in)
+        return fail(MTPB_ERR_ARGUMENT, "structures is NULL");
+    if (in->n_structures < 0)
+        return fail(MTPB_ERR_ARGUMENT, "n_structures must be >= 0");
+    if (in->n_structures > 0 && (!in->atom_offsets || !in->cells))
+        return fail(MTPB_ERR_ARGUMENT, "atom_offsets and cells are required");
+    return MTPB_OK;
+}
+
+} // namespace mtpb
+
+// ============================================================================
+extern "C" {
+
+const char *mtpb_last_error(void) { return mtpb::g_last_error.c_str(); }
+
+int mtpb_abi_version(void) { return MTPB_ABI_VERSION; }
+
+int mtpb_device_count(int *count)
+{
+    if (!count)
+        return fail(MTPB_ERR_ARGUMENT, "count is NULL");
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        *count = 0;
+        return cuda_fail(e, "cudaGetDeviceCount");
+    }
+    *count = n;
+    return MTPB_OK;
+}
+
+int mtpb_create(int device, const mtpb_model_view *view, mtpb_context **out)
+{
+    if (!out)
+        return fail(MTPB_ERR_ARGUMENT, "ctx output pointer is NULL");
+    *out = nullptr;
+    mtpb_context *c = nullptr;
+    try {
+        c = new mtpb_context();
+    } catch (const std::bad_alloc &) {
+        return fail(MTPB_ERR_MEMORY, "host allocation failed");
+    }
+    std::string err;
+    int rc = MTPB_OK;
+    do {
+        if (!copy_model(view, c->model, &err) || !validate_model(c->model, &err)) {
+            rc = fail(MTPB_ERR_ARGUMENT, err);
+            break;
+        }
+        c->shape = select_shape(c->model, &err);
+        if (c->shape < 0) {
+            rc = fail(MTPB_ERR_UNSUPPORTED, err);
+            break;
+        }
+        c->nslot = shape_desc(c->shape).nslot;
+        if (!build_slot_map(c->model, c->shape, c->slot_of_basic, &err) ||
+            !build_dag_plan(c->model, c->shape, c->slot_of_basic, c->plan, &err)) {
+            rc = fail(MTPB_ERR_UNSUPPORTED, err);
+            break;
+        }
+        int ndev = 0;
+        cudaError_t e = cudaGetDeviceCount(&ndev);
+        if (e != cudaSuccess || ndev == 0) {
+            cudaGetLastError();
+            rc = fail(MTPB_ERR_CUDA, std::string("no CUDA device available: ") +
+                                         cudaGetErrorString(e));
+            break;
+        }
+        if (device < 0 || device >= ndev) {
+            rc = fail(MTPB_ERR_ARGUMENT, "device index out of range");
+            break;
+        }
+        c->device = device;
+        if ((rc = set_device(c)) != MTPB_OK)
+            break;
+        cudaDeviceProp prop;
+        if ((e = cudaGetDeviceProperties(&prop, device)) != cudaSuccess) {
+            rc = cuda_fail(e, "cudaGetDeviceProperties");
+            break;
+        }
+        if (prop.major < 10) {
+            rc = fail(MTPB_ERR_UNSUPPORTED, "this library is built for sm_100a (B200) devices");
+            break;
+        }
+        if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess) {
+            rc = cuda_fail(e, "cudaStreamCreate");
+            break;
+        }
+        for (auto &ev : c->ev)
+            if ((e = cudaEventCreate(&ev)) != cudaSuccess) {
+                rc = cuda_fail(e, "cudaEventCreate");
+                break;
+            }
+        if (rc != MTPB_OK)
+            break;
+        rc = upload_model(c);
+    } while (false);
+    if (rc != MTPB_OK) {
+        mtpb_destroy(c);
+        return rc;
+    }
+    *out = c;
+    return MTPB_OK;
+}
+
+int mtpb_destroy(mtpb_context *c)
+{
+    if (!c)
+        return MTPB_OK;
+    if (c->stream) {
+        cudaSetDevice(c->device);
+        cudaStreamSynchronize(c->stream);
+    }
+    c->arena.release();
+    for (auto &ev : c->ev)
+        if (ev)
+            cudaEventDestroy(ev);
+    if (c->stream)
+        cudaStreamDestroy(c->stream);
+    delete c;
+    return MTPB_OK;
+}
+
+int mtpb_update_coefficients(mtpb_context *c, const double *radial, const double *species,
+                             const double *moment)
+{
+    if (!c || !radial || !species || !moment)
+        return fail(MTPB_ERR_ARGUMENT, "NULL argument");
+    ModelHost m = c->model;
+    std::copy(radial, radial + m.radial.size(), m.radial.begin());
+    std::copy(species, species + m.K, m.species.begin());
+    std::copy(moment, moment + m.S(), m.moment.begin());
+    std::string err;
+    if (!validate_model(m, &err))
+        return fail(MTPB_ERR_ARGUMENT, err);
+    DagPlan plan;
+    if (!build_dag_plan(m, c->shape, c->slot_of_basic, plan, &err))
+        return fail(MTPB_ERR_UNSUPPORTED, err);
+    int rc = set_device(c);
+    if (rc)
+        return rc;
+    CUDA_TRY(cudaStreamSynchronize(c->stream), "sync");
+    c->model = std::move(m);
+    c->plan = std::move(plan);
+    c->have_efs = false;
+    return upload_model(c);
+}
+
+int mtpb_cutoff(const mtpb_context *c, double *cutoff)
+{
+    if (!c || !cutoff)
+        return fail(MTPB_ERR_ARGUMENT, "NULL argument");
+    *cutoff = c->model.cutoff();
+    return MTPB_OK;
+}
+
+int mtpb_set_skin(mtpb_context *c, double skin)
+{
+    if (!c || !(skin >= 0) || !std::isfinite(skin))
+        return fail(MTPB_ERR_ARGUMENT, "skin must be a finite non-negative number");
+    c->skin = skin;
+    c->have_list = false;
+    return MTPB_OK;
+}
+
+int mtpb_build_neighbors(mtpb_context *c, const mtpb_structures *in, int memory)
+{
+    if (!c)
+        return fail(MTPB_ERR_ARGUMENT, "ctx is NULL");
+    int rc = check_structures(c, in);
+    if (rc)
+        return rc;
+    if ((rc = set_device(c)))
+        return rc;
+    const int S = in->n_structures;
+    const bool dev = memory == MTPB_MEMORY_DEVICE;
+    c->have_list = false;
+    c->have_efs = false;
+    // host copies of the (small) per-structure arrays
+    c->h_atom_offsets.assign(S + 1, 0);
+    c->h_cells.assign(9 * (size_t)S, 0.0);
+    std::vector<int> pbc(3 * (size_t)S, 1);
+    if (S > 0) {
+        if (dev) {
+            CUDA_TRY(cudaMemcpy(c->h_atom_offsets.data(), in->atom_offsets, sizeof(int) * (S + 1),
+                                cudaMemcpyDeviceToHost),
+                     "read atom_offsets");
+            CUDA_TRY(cudaMemcpy(c->h_cells.data(), in->cells, sizeof(double) * 9 * S,
+                                cudaMemcpyDeviceToHost),
+                     "read cells");
+            if (in->pbc)
+                CUDA_TRY(cudaMemcpy(pbc.data(), in->pbc, sizeof(int) * 3 * S,
+                                    cudaMemcpyDeviceToHost),
+                         "read pbc");
+        } else {
+            std::copy(in->atom_offsets, in->atom_offsets + S + 1, c->h_atom_offsets.begin());
+            std::copy(in->cells, in->cells + 9 * (size_t)S, c->h_cells.begin());
+            if (in->pbc)
+                std::copy(in->pbc, in->pbc + 3 * (size_t)S, pbc.begin());
+        }
+    }
+    if (c->h_atom_offsets[0] != 0)
+        return fail(MTPB_ERR_ARGUMENT, "atom_offsets[0] must be 0");
+    for (int s = 0; s < S; ++s)
+        if (c->h_atom_offsets[s + 1] < c->h_atom_offsets[s])
+            return fail(MTPB_ERR_ARGUMENT, "atom_offsets must be non-decreasing");
+    const int N = c->h_atom_offsets[S];
+    if (N > 0 && (!in->positions || !in->types))
+        return fail(MTPB_ERR_ARGUMENT, "positions and types are required");
+    const double cut = c->model.cutoff() + c->skin;
+    std::vector<NbStruct> ns(S);
+    int cells = 0;
+    for (int s = 0; s < S; ++s) {
+        std::string err;
+        if (!prepare_struct(&c->h_cells[9 * (size_t)s], &pbc[3 * (size_t)s], cut, ns[s], &err))
+            return fail(MTPB_ERR_UNSUPPORTED, "structure " + std::to_string(s) + ": " + err);
+        ns[s].cell0 = cells;
+        const long nc = (long)ns[s].ncell[0] * ns[s].ncell[1] * ns[s].ncell[2];
+        if (cells + nc > (1L << 30))
+            return fail(MTPB_ERR_UNSUPPORTED, "too many neighbour cells");
+        cells += (int)nc;
+    }
+    // device inputs
+    int *d_aoff = c->arena.get<int>("in_atom_offsets", S + 1);
+    NbStruct *d_ns = c->arena.get<NbStruct>("in_nbstructs", S + 1);
+    if (!d_aoff || !d_ns)
+        return fail(MTPB_ERR_MEMORY, "device allocation failed");
+    CUDA_TRY(cudaMemcpyAsync(d_aoff, c->h_atom_offsets.data(), sizeof(int) * (S + 1),
+                             cudaMemcpyHostToDevice, c->stream),
+             "upload offsets");
+    if (S > 0)
+        CUDA_TRY(cudaMemcpyAsync(d_ns, ns.data(), sizeof(NbStruct) * S, cudaMemcpyHostToDevice,
+                                 c->stream),
+                 "upload structs");
+    const double *d_pos = in->positions;
+    const int *d_types = in->types;
+    if (!dev && N > 0) {
+        double *p = c->arena.get<double>("in_positions", 3 * (size_t)N);
+        int *t = c->arena.get<int>("in_types", N);
+        if (!p || !t)
+            return fail(MTPB_ERR_MEMORY, "device allocation failed");
+        CUDA_TRY(cudaMemcpyAsync(p, in->positions, sizeof(double) * 3 * N, cudaMemcpyHostToDevice,
+                                 c->stream),
+                 "upload positions");
+        CUDA_TRY(cudaMemcpyAsync(t, in->types, sizeof(int) * N, cudaMemcpyHostToDevice, c->stream),
+                 "upload types");
+        d_pos = p;
+        d_types = t;
+    } else if (dev && N > 0) {
+        // keep a private copy of the types: the caller's buffer is borrowed
+        int *t = c->arena.get<int>("in_types", N);
+        if (!t)
+            return fail(MTPB_ERR_MEMORY, "device allocation failed");
+        CUDA_TRY(cudaMemcpyAsync(t, in->types, sizeof(int) * N, cudaMemcpyDeviceToDevice,
+                                 c->stream),
+                 "copy types");
+        d_types = t;
+    }
+    // host-side type check (small cost relative to the build)
+    {
+        std::vector<int> ht(N);
+        if (N > 0)
+            CUDA_TRY(cudaMemcpyAsync(ht.data(), d_types, sizeof(int) * N, cudaMemcpyDeviceToHost,
+                                     c->stream),
+                     "read types");
+        CUDA_TRY(cudaStreamSynchronize(c->stream), "sync");
+        for (int i = 0; i < N; ++i)
+            if (ht[i] < 0 || ht[i] >= c->model.K)
+                return fail(MTPB_ERR_ARGUMENT, "atom " + std::to_string(i) +
+                                                   " has a species index outside 0..K-1");
+    }
+    NbBuildInput bi;
+    bi.nstruct = S;
+    bi.natoms = N;
+    bi.total_cells = cells;
+    bi.atom_offsets = d_aoff;
+    bi.structs = d_ns;
+    bi.positions = d_pos;
+    CUDA_TRY(cudaEventRecord(c->ev[0], c->stream), "event");
+    NbResult res;
+    cudaError_t e = build_neighbors(bi, c->arena, res, c->stream);
+    if (e != cudaSuccess)
+        return cuda_fail(e, "neighbour build");
+    c->nb = res;
+    c->nedges = res.nedges;
+    c->natoms = N;
+    c->ntotal = N;
+    c->nstruct = S;
+    c->d_types = d_types;
+    c->d_offsets = res.offsets;
+    // reduction segments: <= 1024 atoms of one structure each
+    std::vector<int> sb, se, s0(S + 1, 0);
+    for (int s = 0; s < S; ++s) {
+        s0[s] = (int)sb.size();
+        const int a0 = c->h_atom_offsets[s], a1 = c->h_atom_offsets[s + 1];
+        if (a0 == a1) {
+            sb.push_back(a0);
+            se.push_back(a1);
+        }
+        for (int a = a0; a < a1; a += 1024) {
+            sb.push_back(a);
+            se.push_back(std::min(a + 1024, a1));
+        }
+    }
+    s0[S] = (int)sb.size();
+    c->nseg = (int)sb.size();
+    c->d_seg_begin = c->arena.get<int>("seg_begin", sb.size() + 1);
+    c->d_seg_end = c->arena.get<int>("seg_end", se.size() + 1);
+    c->d_struct_seg0 = c->arena.get<int>("struct_seg0", S + 1);
+    if (!c->d_seg_begin || !c->d_seg_end || !c->d_struct_seg0)
+        return fail(MTPB_ERR_MEMORY, "device allocation failed");
+    if (!sb.empty()) {
+        CUDA_TRY(cudaMemcpyAsync(c->d_seg_begin, sb.data(), sizeof(int) * sb.size(),
+                                 cudaMemcpyHostToDevice, c->stream),
+                 "upload segments");
+        CUDA_TRY(cudaMemcpyAsync(c->d_seg_end, se.data(), sizeof(int) * se.size(),
+                                 cudaMemcpyHostToDevice, c->stream),
+                 "upload segments");
+    }
+    CUDA_TRY(cudaMemcpyAsync(c->d_struct_seg0, s0.data(), sizeof(int) * (S + 1),
+                             cudaMemcpyHostToDevice, c->stream),
+             "upload segments");
+    CUDA_TRY(cudaStreamSynchronize(c->stream), "neighbour build");
+    c->have_list = true;
+    c->nb_built_this_call = true;
+    return MTPB_OK;
+}
+
+int mtpb_neighbor_count(const mtpb_context *c, long *n)
+{
+    if (!c || !n)
+        return fail(MTPB_ERR_ARGUMENT, "NULL argument");
+    if (!c->have_list)
+        return fail(MTPB_ERR_STATE, "no neighbour list has been built");
+    *n = c->nedges;
+    return MTPB_OK;
+}
+
+int mtpb_get_neighbors(const mtpb_context *c, int *offsets, int *nbr, double *rij, int *shift)
+{
+    if (!c)
+        return fail(MTPB_ERR_ARGUMENT, "ctx is NULL");
+    if (!c->have_list)
+        return fail(MTPB_ERR_STATE, "no neighbour list has been built");
+    CUDA_TRY(cudaSetDevice(c->device), "cudaSetDevice");
+    const long E = c->nedges;
+    if (offsets)
+        CUDA_TRY(cudaMemcpy(offsets, c->nb.offsets, sizeof(int) * (c->natoms + 1),
+                            cudaMemcpyDeviceToHost),
+                 "copy offsets");
+    if (nbr && E)
+        CUDA_TRY(cudaMemcpy(nbr, c->nb.nbr, sizeof(int) * E, cudaMemcpyDeviceToHost), "copy nbr");
+    if (shift && E)
+        CUDA_TRY(cudaMemcpy(shift, c->nb.shift, sizeof(int) * E, cudaMemcpyDeviceToHost),
+                 "copy shift");
+    if (rij && E) {
+        std::vector<double> x(E), y(E), z(E);
+        CUDA_TRY(cudaMemcpy(x.data(), c->nb.rx, sizeof(double) * E, cudaMemcpyDeviceToHost), "rx");
+        CUDA_TRY(cudaMemcpy(y.data(), c->nb.ry, sizeof(double) * E, cudaMemcpyDeviceToHost), "ry");
+        CUDA_TRY(cudaMemcpy(z.data(), c->nb.rz, sizeof(double) * E, cudaMemcpyDeviceToHost), "rz");
+        for (long e = 0; e < E; ++e) {
+            rij[3 * e] = x[e];
+            rij[3 * e + 1] = y[e];
+            rij[3 * e + 2] = z[e];
+        }
+    }
+    return MTPB_OK;
+}
+
+int mtpb_efs_compute(mtpb_context *c, int memory, const mtpb_efs_output *out)
+{
+    if (!c)
+        return fail(MTPB_ERR_ARGUMENT, "ctx is NULL");
+    if (!c->have_list)
+        return fail(MTPB_ERR_STATE, "build the neighbour list first (mtpb_build_neighbors)");
+    int rc = set_device(c);
+    if (rc)
+        return rc;
+    const bool dev = memory == MTPB_MEMORY_DEVICE;
+    const int N = c->natoms, S = c->nstruct;
+    const long E = c->nedges;
+    c->launches = 0;
+    if (!c->nb_built_this_call)
+        CUDA_TRY(cudaEventRecord(c->ev[0], c->stream), "event");
+    double *site_energy = c->arena.get<double>("site_energy", N + 1);
+    double *dx = c->arena.get<double>("dx", E + 1), *dy = c->arena.get<double>("dy", E + 1),
+           *dz = c->arena.get<double>("dz", E + 1);
+    double *forces = (dev && out && out->forces) ? out->forces
+                                                 : c->arena.get<double>("forces", 3 * (size_t)N + 1);
+    double *avir = c->arena.get<double>("atom_virial", 9 * (size_t)N + 1);
+    double *partials = c->arena.get<double>("partials", 10 * (size_t)c->nseg + 10);
+    double *energy = (dev && out && out->energy) ? out->energy
+                                                 : c->arena.get<double>("energy", S + 1);
+    double *stress = (dev && out && out->stress) ? out->stress
+                                                 : c->arena.get<double>("stress", 9 * (size_t)S + 9);
+    if (!site_energy || !dx || !dy || !dz || !forces || !avir || !partials || !energy || !stress)
+        return fail(MTPB_ERR_MEMORY, "device allocation failed");
+    rc = run_moments(c, N, c->d_types, c->nb.offsets, c->nb.nbr, c->nb.rx, c->nb.ry, c->nb.rz,
+                     site_energy, dx, dy, dz);
+    if (rc)
+        return rc;
+    CUDA_TRY(launch_force_gather(N, N, c->nb.offsets, c->nb.in_offsets, c->nb.in_edges, dx, dy, dz,
+                                 c->nb.rx, c->nb.ry, c->nb.rz, forces, avir, 0, c->stream),
+             "force gather");
+    CUDA_TRY(launch_segment_reduce(c->nseg, c->d_seg_begin, c->d_seg_end, site_energy, avir, N,
+                                   partials, c->stream),
+             "segment reduce");
+    CUDA_TRY(launch_struct_reduce(S, c->d_struct_seg0, partials, energy, stress, c->stream),
+             "structure reduce");
+    c->launches += 3;
+    CUDA_TRY(cudaEventRecord(c->ev[5], c->stream), "event");
+    c->ev_valid = true;
+    c->nb_built_this_call = false;
+    if (out) {
+        const cudaMemcpyKind k = dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+        if (out->energy && !dev)
+            CUDA_TRY(cudaMemcpyAsync(out->energy, energy, sizeof(double) * S, k, c->stream), "copy");
+        if (out->forces && !dev)
+            CUDA_TRY(cudaMemcpyAsync(out->forces, forces, sizeof(double) * 3 * N, k, c->stream),
+                     "copy");
+        if (out->stress && !dev)
+            CUDA_TRY(cudaMemcpyAsync(out->stress, stress, sizeof(double) * 9 * S, k, c->stream),
+                     "copy");
+        if (out->site_energy && N)
+            CUDA_TRY(cudaMemcpyAsync(out->site_energy, site_energy, sizeof(double) * N, k,
+                                     c->stream),
+                     "copy");
+    }
+    if (!dev)
+        CUDA_TRY(cudaStreamSynchronize(c->stream), "EFS");
+    else
+        CUDA_TRY(cudaGetLastError(), "EFS");
+    c->have_efs = true;
+    return MTPB_OK;
+}
+
+int mtpb_efs_structures(mtpb_context *c, const mtpb_structures *in, int memory,
+                        int reuse_neighbors, const mtpb_efs_output *out)
+{
+    if (!c)
+        return fail(MTPB_ERR_ARGUMENT, "ctx is NULL");
+    int rc = check_structures(c, in);
+    if (rc)
+        return rc;
+    bool reuse = reuse_neighbors && c->have_list && in->n_structures == c->nstruct;
+    if (reuse) {
+        // the layout must be unchanged; positions are those of the build
+        if (memory != MTPB_MEMORY_DEVICE)
+            for (int s = 0; s <= in->n_structures && reuse; ++s)
+                reuse = in->atom_offsets[s] == c->h_atom_offsets[s];
+    }
+    if (!reuse) {
+        rc = mtpb_build_neighbors(c, in, memory);
+        if (rc)
+            return rc;
+    }
+    return mtpb_efs_compute(c, memory, out);
+}
+
+int mtpb_last_timings(const mtpb_context *c, double *ms)
+{
+    if (!c || !ms)
+        return fail(MTPB_ERR_ARGUMENT, "NULL argument");
+    if (!c->ev_valid)
+        return fail(MTPB_ERR_STATE, "no compute call has been timed");
+    CUDA_TRY(cudaSetDevice(c->device), "cudaSetDevice");
+    CUDA_TRY(cudaEventSynchronize(c->ev[5]), "event sync");
+    float t[5];
+    for (int i = 0; i < 5; ++i) {
+        CUDA_TRY(cudaEventElapsedTime(&t[i], c->ev[i], c->ev[i + 1]), "elapsed");
+        ms[i] = t[i];
+    }
+    return MTPB_OK;
+}
+
+int mtpb_last_launch_count(const mtpb_context *c, int *launches)
+{
+    if (!c || !launches)
+        return fail(MTPB_ERR_ARGUMENT, "NULL argument");
+    *launches = c->launches;
+    return MTPB_OK;
+}
+
+int mtpb_get_site_moments(const mtpb_context *c, double *basic, double *adjoint)
+{
+    if (!c)
+        return fail(MTPB_ERR_ARGUMENT, "ctx is NULL");
+    if (!c->have_efs)
+        return fail(MTPB_ERR_STATE, "no EFS result available");
+    CUDA_TRY(cudaSetDevice(c->device), "cudaSetDevice");
+    const int nb = c->model.nb();
+    const int N = c->natoms;
+    auto fetch = [&](const char *name, double *dst) -> int {
+        double *src = const_cast<DeviceArena &>(c->arena).get<double>(name, 1);
+        std::vector<double> all((size_t)c->nslot * c->npad);
+        CUDA_TRY(cudaMemcpy(all.data(), src, sizeof(double) * all.size(), cudaMemcpyDeviceToHost),
+                 "copy moments");
+        for (int i = 0; i < N; ++i)
+            for (int b = 0; b < nb; ++b)
+                dst[(size_t)i * nb + b] = all[(size_t)c->slot_of_basic[b] * c->npad + i];
+        return MTPB_OK;
+    };
+    int rc;
+    if (basic && (rc = fetch("basic", basic)))
+        return rc;
+    if (adjoint && (rc = fetch("adjoint", adjoint)))
+        return rc;
+    return MTPB_OK;
+}
+
+int mtpb_get_edge_derivatives(const mtpb_context *c, double *dedr)
+{
+    if (!c || !dedr)
+        return fail(MTPB_ERR_ARGUMENT, "NULL argument");
+    if (!c->have_efs)
+        return fail(MTPB_ERR_STATE, "no EFS result available");
+    CUDA_TRY(cudaSetDevice(c->device), "cudaSetDevice");
+    const long E = c->nedges;
+    DeviceArena &ar = const_cast<DeviceArena &>(c->arena);
+    std::vector<double> x(E), y(E), z(E);
+    if (E) {
+        CUDA_TRY(cudaMemcpy(x.data(), ar.get<double>("dx", 1), sizeof(double) * E,
+                            cudaMemcpyDeviceToHost),
+                 "dx");
+        CUDA_TRY(cudaMemcpy(y.data(), ar.get<double>("dy", 1), sizeof(double) * E,
+                            cudaMemcpyDeviceToHost),
+                 "dy");
+        CUDA_TRY(cudaMemcpy(z.data(), ar.get<double>("dz", 1), sizeof(double) * E,
+                            cudaMemcpyDeviceToHost),
+                 "dz");
+    }
+    for (long e = 0; e < E; ++e) {
+        dedr[3 * e] = x[e];
+        dedr[3 * e + 1] = y[e];
+        dedr[3 * e + 2] = z[e];
+    }
+    return MTPB_OK;
+}
+
+int mtpb_efs_csr(mtpb_context *c, const mtpb_csr_request *req, int memory)
+{
+    return csr_compute(c, req, memory);
+}
+
+int mtpb_efs_lammps(mtpb_context *c, const mtpb_lammps_request *req)
+{
+    return lammps_compute(c, req);
+}
+
+int mtpb_loss_grad(mtpb_context *c, const mtpb_labels *labels, const mtpb_loss_weights *w,
+                   int norm_count, int memory, double *loss, double *metrics, double *grad)
+{
+    return loss_grad_compute(c, labels, w, norm_count, memory, loss, metrics, grad);
+}
+
+} // extern "C"

@@ -1,0 +1,84 @@
+// context.hpp -- the context object behind the C ABI and the helpers
+// shared by the API translation units.
+#pragma once
+
+#include "internal.hpp"
+#include "neighbors.hpp"
+#include "plan.hpp"
+
+#include "../../include/mtpb200.h"
+
+#include <cuda_runtime.h>
+
+#include <string>
+#include <vector>
+
+namespace mtpb {
+
+// Device-resident state of the training evaluator (training.cu).
+struct TrainingState {
+    bool ready = false;
+};
+
+int fail(int status, const std::string &msg);
+int cuda_fail(cudaError_t e, const char *where);
+
+} // namespace mtpb
+
+#define CUDA_TRY(expr, where)                                                                      \
+    do {                                                                                           \
+        cudaError_t _e = (expr);                                                                   \
+        if (_e != cudaSuccess)                                                                     \
+            return ::mtpb::cuda_fail(_e, where);                                                           \
+    } while (0)
+
+struct mtpb_context {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    mtpb::ModelHost model;
+    int shape = -1;
+    int nslot = 0;
+    std::vector<int> slot_of_basic;
+    mtpb::DagPlan plan;
+    mtpb::DeviceArena arena;
+    double skin = 0.0;
+    // device model data
+    double *d_radial = nullptr, *d_species = nullptr;
+    mtpb::PairParams *d_pairs = nullptr;
+    mtpb::DagRec *d_recs = nullptr;
+    int *d_phase_row0 = nullptr;
+    // current batch (structures path)
+    int nstruct = 0, natoms = 0, ntotal = 0;
+    long nedges = 0;
+    bool have_list = false;
+    std::vector<int> h_atom_offsets;
+    std::vector<double> h_cells;
+    mtpb::NbResult nb;
+    const int *d_types = nullptr;
+    const int *d_offsets = nullptr;
+    int *d_group_maxdeg = nullptr;
+    int *d_seg_begin = nullptr, *d_seg_end = nullptr, *d_struct_seg0 = nullptr;
+    int nseg = 0;
+    int npad = 0;
+    // timings
+    cudaEvent_t ev[6] = {};
+    bool ev_valid = false;
+    bool nb_built_this_call = false;
+    int launches = 0;
+    bool have_efs = false;
+    mtpb::TrainingState train;
+};
+
+
+namespace mtpb {
+int set_device(mtpb_context *c);
+EdgeArgs edge_args(const mtpb_context *c, int ncenter, const int *types, const int *offsets,
+                   const int *nbr, const double *rx, const double *ry, const double *rz);
+int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offsets,
+                const int *nbr, const double *rx, const double *ry, const double *rz,
+                double *site_energy, double *dx, double *dy, double *dz);
+int csr_compute(mtpb_context *c, const mtpb_csr_request *req, int memory);
+int lammps_compute(mtpb_context *c, const mtpb_lammps_request *req);
+int loss_grad_compute(mtpb_context *c, const mtpb_labels *labels, const mtpb_loss_weights *w,
+                      int norm_count, int memory, double *loss, double *metrics, double *grad);
+} // namespace mtpb

@@ -1,0 +1,789 @@
+// efs.cu -- FP64 moment kernels (forward and reverse), the per-atom moment
+// graph kernel, the deterministic force gather and the energy/virial
+// reductions of the MTP energy/force/stress path.
+//
+// Reference semantics (paths relative to the reference project):
+//   forward   potentials/potential_mtp.cpp:2813-2925  (CalcSiteDescriptorsImpl)
+//   energy    potentials/potential_mtp.cpp:2959-2984  (CalcSiteEFS)
+//   reverse   potentials/potential_mtp.cpp:3292-3305, 2938-2957
+//   scatter   potentials/potential_mtp.cpp:1909-1932  (getEFS)
+//   radial    basis/basis.cpp:148-164                 (RBasis_Chebyshev::calc_der)
+//
+// The kernels use a factorised form of the same mathematics.  With
+// rhat = r/|r| and f_mu the radial functions, every basic moment is
+//   b[mu,abc] = sum_j f_mu(r_j) xhat^a yhat^b zhat^c.
+// The force on edge j needs d_j = dE/dr_j = sum a[mu,abc] grad(f_mu u_abc):
+//   d_j = rhat (V - H/r) + G/r,  with P_abc = sum_mu a f_mu,
+//   P'_abc = sum_mu a f'_mu, V = sum P' u, H = sum nu P u, G = sum P grad u,
+// each polynomial evaluated along x-chains with Horner's rule.  This replaces
+// the reference's per-edge Jacobian (nb x n_e x 3 doubles per site) by
+// registers.
+#include "internal.hpp"
+#include "shapes.cuh"
+
+#include <cstdio>
+
+namespace mtpb {
+
+constexpr int KS = 8;     // edge slots staged per chunk
+constexpr int STR = 33;   // padded row stride of the staging arrays (doubles)
+
+template <class S> struct ShapeCfg;
+template <> struct ShapeCfg<ShapeS1> { static constexpr int NW = 2; };
+template <> struct ShapeCfg<ShapeS2> { static constexpr int NW = 2; };
+template <> struct ShapeCfg<ShapeL16> { static constexpr int NW = 4; };
+template <> struct ShapeCfg<ShapeL20> { static constexpr int NW = 8; };
+template <> struct ShapeCfg<ShapeL24> { static constexpr int NW = 16; };
+template <> struct ShapeCfg<ShapePS> { static constexpr int NW = 4; };
+
+// staging arrays: 0 xhat, 1 yhat, 2 zhat, 3 1/r, 4.. f_mu, 4+NMU.. f'_mu
+template <class S, bool REV> constexpr int stage_rows()
+{
+    return REV ? 4 + 2 * S::NMU : 4 + S::NMU;
+}
+
+template <class S, bool REV> constexpr int smem_doubles(int K, int R)
+{
+    constexpr int NW = ShapeCfg<S>::NW;
+    int n = stage_rows<S, REV>() * KS * STR;
+    if (REV)
+        n += NW * 3 * KS * 32;
+    n += 4 * K * K;             // pair parameters
+    n += K * K * S::NMU * R;    // radial coefficients of the used channels
+    return n;
+}
+
+struct StageView {
+    double *st;       // [rows][KS][STR]
+    double *part;     // [NW][3][KS][32] (reverse only)
+    const PairParams *pairs;
+    const double *radial;  // [K*K][NMU][R]
+};
+
+__device__ __forceinline__ double &SV(double *st, int row, int k, int lane)
+{
+    return st[(row * KS + k) * STR + lane];
+}
+
+// Computes the per-edge quantities of one chunk of edge slots for the 32
+// atoms of this block.  Every thread of the block takes part.
+template <class S, int NW, bool REV>
+__device__ __forceinline__ void stage_chunk(const EdgeArgs &p, const StageView &v, int atom0,
+                                            int chunk)
+{
+    constexpr int NMU = S::NMU;
+    for (int item = threadIdx.x; item < 32 * KS; item += NW * 32) {
+        const int lane = item / KS;
+        const int k = item - lane * KS;
+        const int atom = atom0 + lane;
+        double xh = 0.0, yh = 0.0, zh = 0.0, rinv = 0.0;
+        double f[NMU], fp[NMU];
+#pragma unroll
+        for (int m = 0; m < NMU; ++m) {
+            f[m] = 0.0;
+            fp[m] = 0.0;
+        }
+        if (atom < p.natoms) {
+            const int e = __ldg(p.offsets + atom) + chunk * KS + k;
+            if (e < __ldg(p.offsets + atom + 1)) {
+                const double x = __ldg(p.rx + e), y = __ldg(p.ry + e), z = __ldg(p.rz + e);
+                // neighbour distance exactly as the reference list stores it:
+                // sqrt((x*x + y*y) + z*z) without contraction
+                const double r2 = __dadd_rn(__dadd_rn(__dmul_rn(x, x), __dmul_rn(y, y)),
+                                            __dmul_rn(z, z));
+                const double r = sqrt(r2);
+                const int it = __ldg(p.types + atom);
+                const int jt = __ldg(p.types + __ldg(p.nbr + e));
+                // atoms of type -1 are skipped (runtime/mtp/mlip.cpp:944, 952)
+                const int pair = (it >= 0 && jt >= 0) ? it * p.K + jt : 0;
+                const PairParams pp = v.pairs[pair];
+                // potential_mtp.cpp:2842 skips r > cutoff; mlip.cpp:966 r > 0
+                if (it >= 0 && jt >= 0 && r > 0.0 && r <= pp.rmax) {
+                    rinv = 1.0 / r;
+                    xh = x * rinv;
+                    yh = y * rinv;
+                    zh = z * rinv;
+                    // Chebyshev recurrence (basis.cpp:148-164) folded into
+                    // the channel sums f_mu = sum_xi c[pair,mu,xi] Q_xi(r)
+                    const double ksi = (2.0 * r - pp.pu) / pp.su;
+                    const double ru = r - pp.rmax;
+                    const double s = p.scaling;
+                    const double *c = v.radial + pair * NMU * p.R;
+                    double q0 = s * (ru * ru), d0 = s * (2.0 * ru);
+#pragma unroll
+                    for (int m = 0; m < NMU; ++m) {
+                        f[m] = c[m * p.R] * q0;
+                        fp[m] = c[m * p.R] * d0;
+                    }
+                    if (p.R > 1) {
+                        double q1 = s * (ksi * ru * ru);
+                        double d1 = s * (pp.mult * ru * ru + 2.0 * ksi * ru);
+#pragma unroll
+                        for (int m = 0; m < NMU; ++m) {
+                            f[m] = fma(c[m * p.R + 1], q1, f[m]);
+                            fp[m] = fma(c[m * p.R + 1], d1, fp[m]);
+                        }
+                        for (int xi = 2; xi < p.R; ++xi) {
+                            const double q2 = 2.0 * ksi * q1 - q0;
+                            const double d2 = 2.0 * (pp.mult * q1 + ksi * d1) - d0;
+#pragma unroll
+                            for (int m = 0; m < NMU; ++m) {
+                                f[m] = fma(c[m * p.R + xi], q2, f[m]);
+                                fp[m] = fma(c[m * p.R + xi], d2, fp[m]);
+                            }
+                            q0 = q1;
+                            q1 = q2;
+                            d0 = d1;
+                            d1 = d2;
+                        }
+                    }
+                }
+            }
+        }
+        SV(v.st, 0, k, lane) = xh;
+        SV(v.st, 1, k, lane) = yh;
+        SV(v.st, 2, k, lane) = zh;
+#pragma unroll
+        for (int m = 0; m < NMU; ++m)
+            SV(v.st, 4 + m, k, lane) = f[m];
+        if constexpr (REV) {
+            SV(v.st, 3, k, lane) = rinv;
+#pragma unroll
+            for (int m = 0; m < NMU; ++m)
+                SV(v.st, 4 + NMU + m, k, lane) = fp[m];
+        }
+    }
+}
+
+// accumulator offset of monomial a within a chain (sum of channel counts of
+// the lower powers)
+template <class S> constexpr int chain_acc_off(int s, int a)
+{
+    int o = 0;
+    for (int aa = 0; aa < a; ++aa)
+        o += S::cnt(aa + s);
+    return o;
+}
+
+// ----------------------------------------------------------------------------
+// Forward: basic moments of 32 atoms; warp W owns the chains of Partition.
+// ----------------------------------------------------------------------------
+template <class S, int NW, int W>
+__device__ __forceinline__ void fwd_warp(const EdgeArgs &p, const StageView &v, int atom0,
+                                         int maxdeg, double *basic)
+{
+    using P = Partition<S, NW>;
+    constexpr int NACC = P::table.nacc[W];
+    constexpr int NCHW = P::table.count[W];
+    constexpr int MAXB = P::table.maxb[W];
+    constexpr int MAXC = P::table.maxc[W];
+    constexpr int NMU = S::NMU;
+    const int lane = threadIdx.x & 31;
+    double acc[NACC > 0 ? NACC : 1];
+#pragma unroll
+    for (int i = 0; i < NACC; ++i)
+        acc[i] = 0.0;
+    const int nchunks = (maxdeg + KS - 1) / KS;
+    for (int ch = 0; ch < nchunks; ++ch) {
+        stage_chunk<S, NW, false>(p, v, atom0, ch);
+        __syncthreads();
+        const int kend = min(KS, maxdeg - ch * KS);
+        for (int k = 0; k < kend; ++k) {
+            const double xh = SV(v.st, 0, k, lane);
+            const double yh = SV(v.st, 1, k, lane);
+            const double zh = SV(v.st, 2, k, lane);
+            double f[NMU];
+#pragma unroll
+            for (int m = 0; m < NMU; ++m)
+                f[m] = SV(v.st, 4 + m, k, lane);
+            double yp[MAXB + 1], zp[MAXC + 1];
+            yp[0] = 1.0;
+            zp[0] = 1.0;
+#pragma unroll
+            for (int i = 1; i <= MAXB; ++i)
+                yp[i] = yp[i - 1] * yh;
+#pragma unroll
+            for (int i = 1; i <= MAXC; ++i)
+                zp[i] = zp[i - 1] * zh;
+            static_for<NCHW>([&](auto ii) {
+                constexpr int ci = P::table.list[W * S::NCH + decltype(ii)::value];
+                constexpr int a0 = P::table.acc0[W * S::NCH + decltype(ii)::value];
+                constexpr int b = S::chains.b[ci];
+                constexpr int c = S::chains.c[ci];
+                constexpr int L = S::chains.len[ci];
+                double u;
+                if constexpr (b == 0 && c == 0)
+                    u = 1.0;
+                else if constexpr (b == 0)
+                    u = zp[c];
+                else if constexpr (c == 0)
+                    u = yp[b];
+                else
+                    u = yp[b] * zp[c];
+                static_for<L>([&](auto ia) {
+                    constexpr int a = decltype(ia)::value;
+                    constexpr int nu = a + b + c;
+                    constexpr int off = a0 + chain_acc_off<S>(b + c, a);
+                    static_for<S::cnt(nu)>([&](auto iq) {
+                        constexpr int q = decltype(iq)::value;
+                        acc[off + q] = fma(f[S::chan(nu, q)], u, acc[off + q]);
+                    });
+                    if constexpr (a + 1 < L)
+                        u *= xh;
+                });
+            });
+        }
+        __syncthreads();
+    }
+    const int atom = atom0 + lane;
+    if (atom < p.natoms) {
+        static_for<NCHW>([&](auto ii) {
+            constexpr int ci = P::table.list[W * S::NCH + decltype(ii)::value];
+            constexpr int a0 = P::table.acc0[W * S::NCH + decltype(ii)::value];
+            constexpr int n = S::chains.nacc[ci];
+            constexpr int slot0 = S::chains.slot0[ci];
+#pragma unroll
+            for (int i = 0; i < n; ++i)
+                basic[(size_t)(slot0 + i) * p.npad + atom] = acc[a0 + i];
+        });
+    }
+}
+
+// ----------------------------------------------------------------------------
+// Reverse: per-edge dE_i/dr_ij of 32 atoms.  Each warp adds its chains'
+// share; the shares are summed in fixed warp order (deterministic).
+// ----------------------------------------------------------------------------
+template <class S, int NW, int W>
+__device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, int atom0,
+                                         int maxdeg, const double *adjoint, double *dx,
+                                         double *dy, double *dz)
+{
+    using P = Partition<S, NW>;
+    constexpr int NACC = P::table.nacc[W];
+    constexpr int NCHW = P::table.count[W];
+    constexpr int MAXB = P::table.maxb[W];
+    constexpr int MAXC = P::table.maxc[W];
+    constexpr int NMU = S::NMU;
+    const int lane = threadIdx.x & 31;
+    const int atom = atom0 + lane;
+    double adj[NACC > 0 ? NACC : 1];
+    if (atom < p.natoms) {
+        static_for<NCHW>([&](auto ii) {
+            constexpr int ci = P::table.list[W * S::NCH + decltype(ii)::value];
+            constexpr int a0 = P::table.acc0[W * S::NCH + decltype(ii)::value];
+            constexpr int n = S::chains.nacc[ci];
+            constexpr int slot0 = S::chains.slot0[ci];
+#pragma unroll
+            for (int i = 0; i < n; ++i)
+                adj[a0 + i] = __ldg(adjoint + (size_t)(slot0 + i) * p.npad + atom);
+        });
+    } else {
+#pragma unroll
+        for (int i = 0; i < NACC; ++i)
+            adj[i] = 0.0;
+    }
+    const int nchunks = (maxdeg + KS - 1) / KS;
+    for (int ch = 0; ch < nchunks; ++ch) {
+        stage_chunk<S, NW, true>(p, v, atom0, ch);
+        __syncthreads();
+        const int kend = min(KS, maxdeg - ch * KS);
+        for (int k = 0; k < kend; ++k) {
+            const double xh = SV(v.st, 0, k, lane);
+            const double yh = SV(v.st, 1, k, lane);
+            const double zh = SV(v.st, 2, k, lane);
+            const double rinv = SV(v.st, 3, k, lane);
+            double f[NMU], fp[NMU];
+#pragma unroll
+            for (int m = 0; m < NMU; ++m) {
+                f[m] = SV(v.st, 4 + m, k, lane);
+                fp[m] = SV(v.st, 4 + NMU + m, k, lane);
+            }
+            double yp[MAXB + 1], zp[MAXC + 1];
+            yp[0] = 1.0;
+            zp[0] = 1.0;
+#pragma unroll
+            for (int i = 1; i <= MAXB; ++i)
+                yp[i] = yp[i - 1] * yh;
+#pragma unroll
+            for (int i = 1; i <= MAXC; ++i)
+                zp[i] = zp[i - 1] * zh;
+            double V = 0.0, H = 0.0, Gx = 0.0, Gy = 0.0, Gz = 0.0;
+            static_for<NCHW>([&](auto ii) {
+                constexpr int ci = P::table.list[W * S::NCH + decltype(ii)::value];
+                constexpr int a0 = P::table.acc0[W * S::NCH + decltype(ii)::value];
+                constexpr int b = S::chains.b[ci];
+                constexpr int c = S::chains.c[ci];
+                constexpr int L = S::chains.len[ci];
+                double h0 = 0.0, h1 = 0.0, g0 = 0.0;
+                static_for<L>([&](auto ia) {
+                    constexpr int a = L - 1 - decltype(ia)::value;
+                    constexpr int nu = a + b + c;
+                    constexpr int off = a0 + chain_acc_off<S>(b + c, a);
+                    double Pv = adj[off] * f[S::chan(nu, 0)];
+                    double Pd = adj[off] * fp[S::chan(nu, 0)];
+                    static_for<S::cnt(nu) - 1>([&](auto iq) {
+                        constexpr int q = decltype(iq)::value + 1;
+                        Pv = fma(adj[off + q], f[S::chan(nu, q)], Pv);
+                        Pd = fma(adj[off + q], fp[S::chan(nu, q)], Pd);
+                    });
+                    if constexpr (a == L - 1) {
+                        h0 = Pv;
+                        g0 = Pd;
+                    } else {
+                        h1 = fma(h1, xh, h0);
+                        h0 = fma(h0, xh, Pv);
+                        g0 = fma(g0, xh, Pd);
+                    }
+                });
+                double q;
+                if constexpr (b == 0 && c == 0)
+                    q = 1.0;
+                else if constexpr (b == 0)
+                    q = zp[c];
+                else if constexpr (c == 0)
+                    q = yp[b];
+                else
+                    q = yp[b] * zp[c];
+                V = fma(q, g0, V);
+                Gx = fma(q, h1, Gx);
+                if constexpr (b > 0) {
+                    double qy = (c == 0) ? yp[b - 1] : yp[b - 1] * zp[c];
+                    Gy = fma(double(b) * qy, h0, Gy);
+                }
+                if constexpr (c > 0) {
+                    double qz = (b == 0) ? zp[c - 1] : yp[b] * zp[c - 1];
+                    Gz = fma(double(c) * qz, h0, Gz);
+                }
+                H = fma(q, fma(xh, h1, double(b + c) * h0), H);
+            });
+            const double t = V - H * rinv;
+            double *part = v.part + (size_t)W * 3 * KS * 32;
+            part[(0 * KS + k) * 32 + lane] = fma(xh, t, Gx * rinv);
+            part[(1 * KS + k) * 32 + lane] = fma(yh, t, Gy * rinv);
+            part[(2 * KS + k) * 32 + lane] = fma(zh, t, Gz * rinv);
+        }
+        __syncthreads();
+        // sum the warps' shares in warp order and store per edge
+        for (int item = threadIdx.x; item < 32 * KS; item += NW * 32) {
+            const int ln = item / KS;
+            const int k = item - ln * KS;
+            const int at = atom0 + ln;
+            if (k >= kend || at >= p.natoms)
+                continue;
+            const int e = __ldg(p.offsets + at) + ch * KS + k;
+            if (e >= __ldg(p.offsets + at + 1))
+                continue;
+            double sx = 0.0, sy = 0.0, sz = 0.0;
+#pragma unroll
+            for (int w = 0; w < NW; ++w) {
+                const double *pw = v.part + (size_t)w * 3 * KS * 32;
+                sx += pw[(0 * KS + k) * 32 + ln];
+                sy += pw[(1 * KS + k) * 32 + ln];
+                sz += pw[(2 * KS + k) * 32 + ln];
+            }
+            dx[e] = sx;
+            dy[e] = sy;
+            dz[e] = sz;
+        }
+        __syncthreads();
+    }
+}
+
+template <class S, bool REV>
+__global__ void __launch_bounds__(ShapeCfg<S>::NW * 32)
+    k_moments(EdgeArgs p, double *basic, const double *adjoint, double *dx, double *dy,
+              double *dz)
+{
+    constexpr int NW = ShapeCfg<S>::NW;
+    constexpr int NMU = S::NMU;
+    extern __shared__ double smem[];
+    StageView v;
+    v.st = smem;
+    double *cur = smem + stage_rows<S, REV>() * KS * STR;
+    v.part = cur;
+    if (REV)
+        cur += NW * 3 * KS * 32;
+    PairParams *pairs = reinterpret_cast<PairParams *>(cur);
+    cur += 4 * p.K * p.K;
+    double *radial = cur;
+    const int KK = p.K * p.K;
+    for (int i = threadIdx.x; i < KK; i += blockDim.x)
+        pairs[i] = p.pairs[i];
+    for (int i = threadIdx.x; i < KK * NMU * p.R; i += blockDim.x) {
+        const int pair = i / (NMU * p.R);
+        const int rem = i - pair * NMU * p.R;
+        radial[i] = p.radial[(size_t)pair * p.mu_total * p.R + rem];
+    }
+    v.pairs = pairs;
+    v.radial = radial;
+    __syncthreads();
+    const int group = blockIdx.x;
+    const int atom0 = group * 32;
+    const int maxdeg = __ldg(p.group_maxdeg + group);
+    const int warp = threadIdx.x >> 5;
+    static_for<NW>([&](auto iw) {
+        constexpr int W = decltype(iw)::value;
+        if (warp == W) {
+            if constexpr (REV)
+                rev_warp<S, NW, W>(p, v, atom0, maxdeg, adjoint, dx, dy, dz);
+            else
+                fwd_warp<S, NW, W>(p, v, atom0, maxdeg, basic);
+        }
+    });
+}
+
+template <class S, bool REV> static cudaError_t launch_shape(const EdgeArgs &a, double *basic,
+                                                             const double *adjoint, double *dx,
+                                                             double *dy, double *dz,
+                                                             cudaStream_t s)
+{
+    constexpr int NW = ShapeCfg<S>::NW;
+    const int groups = (a.natoms + 31) / 32;
+    if (groups == 0)
+        return cudaSuccess;
+    const size_t smem = sizeof(double) * smem_doubles<S, REV>(a.K, a.R);
+    auto kern = k_moments<S, REV>;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem);
+    if (err != cudaSuccess)
+        return err;
+    kern<<<groups, NW * 32, smem, s>>>(a, basic, adjoint, dx, dy, dz);
+    return cudaGetLastError();
+}
+
+template <bool REV> static cudaError_t dispatch(int shape, const EdgeArgs &a, double *basic,
+                                                const double *adjoint, double *dx, double *dy,
+                                                double *dz, cudaStream_t s)
+{
+    switch (shape) {
+    case SHAPE_S1: return launch_shape<ShapeS1, REV>(a, basic, adjoint, dx, dy, dz, s);
+    case SHAPE_S2: return launch_shape<ShapeS2, REV>(a, basic, adjoint, dx, dy, dz, s);
+    case SHAPE_L16: return launch_shape<ShapeL16, REV>(a, basic, adjoint, dx, dy, dz, s);
+    case SHAPE_L20: return launch_shape<ShapeL20, REV>(a, basic, adjoint, dx, dy, dz, s);
+    case SHAPE_L24: return launch_shape<ShapeL24, REV>(a, basic, adjoint, dx, dy, dz, s);
+    case SHAPE_PS: return launch_shape<ShapePS, REV>(a, basic, adjoint, dx, dy, dz, s);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_moments_fwd(int shape, const EdgeArgs &a, double *basic, cudaStream_t s)
+{
+    return dispatch<false>(shape, a, basic, nullptr, nullptr, nullptr, nullptr, s);
+}
+
+cudaError_t launch_moments_rev(int shape, const EdgeArgs &a, const double *adjoint, double *dx,
+                               double *dy, double *dz, cudaStream_t s)
+{
+    return dispatch<true>(shape, a, nullptr, adjoint, dx, dy, dz, s);
+}
+
+// ---- host-side shape queries ----------------------------------------------
+template <class S> static ShapeDesc make_desc()
+{
+    ShapeDesc d{};
+    d.nmu = S::NMU;
+    for (int i = 0; i < S::NMU; ++i)
+        d.numax[i] = S::numax[i];
+    d.nslot = S::NSLOT;
+    return d;
+}
+
+const ShapeDesc &shape_desc(int id)
+{
+    static const ShapeDesc descs[SHAPE_COUNT] = {make_desc<ShapeS1>(), make_desc<ShapeS2>(),
+                                                 make_desc<ShapeL16>(), make_desc<ShapeL20>(),
+                                                 make_desc<ShapeL24>(), make_desc<ShapePS>()};
+    return descs[id];
+}
+
+int shape_slot(int id, int mu, int a, int b, int c)
+{
+    switch (id) {
+    case SHAPE_S1: return ShapeS1::slot_of(mu, a, b, c);
+    case SHAPE_S2: return ShapeS2::slot_of(mu, a, b, c);
+    case SHAPE_L16: return ShapeL16::slot_of(mu, a, b, c);
+    case SHAPE_L20: return ShapeL20::slot_of(mu, a, b, c);
+    case SHAPE_L24: return ShapeL24::slot_of(mu, a, b, c);
+    case SHAPE_PS: return ShapePS::slot_of(mu, a, b, c);
+    default: return -1;
+    }
+}
+
+// ----------------------------------------------------------------------------
+// Per-32-atom-group maximum neighbour count (chunk count of the edge kernels)
+// ----------------------------------------------------------------------------
+__global__ void k_group_maxdeg(int natoms, const int *offsets, int *out)
+{
+    const int atom = blockIdx.x * blockDim.x + threadIdx.x;
+    int deg = 0;
+    if (atom < natoms)
+        deg = offsets[atom + 1] - offsets[atom];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        deg = max(deg, __shfl_xor_sync(0xffffffffu, deg, o));
+    if ((threadIdx.x & 31) == 0 && atom - (int)(threadIdx.x & 31) < natoms)
+        out[atom >> 5] = deg;
+}
+
+cudaError_t launch_group_maxdeg(int natoms, const int *offsets, int *group_maxdeg,
+                                cudaStream_t s)
+{
+    if (natoms == 0)
+        return cudaSuccess;
+    const int threads = 256;
+    const int blocks = (natoms + threads - 1) / threads;
+    k_group_maxdeg<<<blocks, threads, 0, s>>>(natoms, offsets, group_maxdeg);
+    return cudaGetLastError();
+}
+
+// ----------------------------------------------------------------------------
+// Moment graph: forward product rules, site energy, reverse adjoints.
+// One block = 16 atoms; each half-warp runs one record stream of the plan.
+// Shared memory holds one row of 16 doubles per graph value (basic moments,
+// product moments that feed later rules, their adjoints, and constants).
+//
+// Forward record:  acc = START ? 0 : acc;  acc += (c * row[s1]) * row[s2];
+//                  END: row[out] = acc (out >= 0), E += e * acc.
+// Reverse record:  acc = START ? e : acc;  acc += (c * row[s1]) * row[s2];
+//                  END: GLOBAL ? adjoint[out] = acc : row[out] = acc.
+// ----------------------------------------------------------------------------
+__global__ void __launch_bounds__(DAG_WARPS * 32)
+    k_dag(const DagRec *__restrict__ recs, const int *__restrict__ phase_row0, int n_fwd,
+          int n_rev, int nrows, int one_row, int zero_row, int nslot, int natoms, int npad,
+          const int *__restrict__ types, const double *__restrict__ species_coeffs,
+          const double *__restrict__ basic, double *__restrict__ adjoint,
+          double *__restrict__ site_energy)
+{
+    extern __shared__ double rows[];   // [nrows][16]
+    __shared__ double epart[DAG_STREAMS][DAG_ATOMS];
+    const int atom0 = blockIdx.x * DAG_ATOMS;
+    // load basic moments (kernel slot s -> row s)
+    for (int i = threadIdx.x; i < nslot * DAG_ATOMS; i += blockDim.x) {
+        const int s = i / DAG_ATOMS, a = i - s * DAG_ATOMS;
+        const int atom = atom0 + a;
+        rows[i] = atom < natoms ? basic[(size_t)s * npad + atom] : 0.0;
+    }
+    if (threadIdx.x < DAG_ATOMS) {
+        rows[one_row * DAG_ATOMS + threadIdx.x] = 1.0;
+        rows[zero_row * DAG_ATOMS + threadIdx.x] = 0.0;
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int stream = warp * 2 + (lane >> 4);
+    const int al = lane & 15;
+    double E = 0.0, acc = 0.0;
+    for (int ph = 0; ph < n_fwd; ++ph) {
+        const int r0 = phase_row0[ph], r1 = phase_row0[ph + 1];
+        for (int r = r0; r < r1; ++r) {
+            const DagRec rec = recs[(size_t)r * DAG_STREAMS + stream];
+            if (rec.flags & DAG_START)
+                acc = 0.0;
+            acc = fma(rec.c * rows[rec.s1 * DAG_ATOMS + al], rows[rec.s2 * DAG_ATOMS + al], acc);
+            if (rec.flags & DAG_END) {
+                if (rec.out >= 0)
+                    rows[rec.out * DAG_ATOMS + al] = acc;
+                E = fma(rec.e, acc, E);
+            }
+        }
+        __syncthreads();
+    }
+    epart[stream][al] = E;
+    __syncthreads();
+    if (threadIdx.x < DAG_ATOMS) {
+        const int atom = atom0 + threadIdx.x;
+        if (atom < natoms) {
+            const int t = types[atom];
+            double se = t >= 0 ? species_coeffs[t] : 0.0;
+            if (t >= 0)
+                for (int s = 0; s < DAG_STREAMS; ++s)
+                    se += epart[s][threadIdx.x];
+            site_energy[atom] = se;
+        }
+    }
+    const int atom = atom0 + al;
+    for (int ph = n_fwd; ph < n_fwd + n_rev; ++ph) {
+        const int r0 = phase_row0[ph], r1 = phase_row0[ph + 1];
+        for (int r = r0; r < r1; ++r) {
+            const DagRec rec = recs[(size_t)r * DAG_STREAMS + stream];
+            if (rec.flags & DAG_START)
+                acc = rec.e;
+            acc = fma(rec.c * rows[rec.s1 * DAG_ATOMS + al], rows[rec.s2 * DAG_ATOMS + al], acc);
+            if (rec.flags & DAG_END) {
+                if (rec.flags & DAG_GLOBAL) {
+                    if (atom < natoms)
+                        adjoint[(size_t)rec.out * npad + atom] = acc;
+                } else if (rec.out >= 0) {
+                    rows[rec.out * DAG_ATOMS + al] = acc;
+                }
+            }
+        }
+        __syncthreads();
+    }
+}
+
+cudaError_t launch_dag(const DagPlan &plan, const DagRec *recs, const int *phase_row0, int nslot,
+                       int natoms, int npad, const int *types, const double *species_coeffs,
+                       const double *basic, double *adjoint, double *site_energy,
+                       cudaStream_t s)
+{
+    const int blocks = (natoms + DAG_ATOMS - 1) / DAG_ATOMS;
+    if (blocks == 0)
+        return cudaSuccess;
+    const size_t smem = sizeof(double) * (size_t)plan.nrows * DAG_ATOMS;
+    cudaError_t err = cudaFuncSetAttribute(k_dag, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem);
+    if (err != cudaSuccess)
+        return err;
+    k_dag<<<blocks, DAG_WARPS * 32, smem, s>>>(recs, phase_row0, plan.n_fwd, plan.n_rev,
+                                               plan.nrows, plan.one_row, plan.zero_row, nslot,
+                                               natoms, npad, types, species_coeffs, basic,
+                                               adjoint, site_energy);
+    return cudaGetLastError();
+}
+
+// ----------------------------------------------------------------------------
+// Forces and per-atom virial by gather (deterministic, no atomics):
+//   F_k = sum_{e in out(k)} d_e - sum_{e in in(k)} d_e      (getEFS scatter)
+//   W_k = - sum_{e in out(k)} d_e (x) r_e                   (stress_ -= d r)
+// ----------------------------------------------------------------------------
+__global__ void k_force_gather(int natoms, int ntotal, const int *__restrict__ offsets,
+                               const int *__restrict__ in_offsets,
+                               const int *__restrict__ in_edges, const double *__restrict__ dx,
+                               const double *__restrict__ dy, const double *__restrict__ dz,
+                               const double *__restrict__ rx, const double *__restrict__ ry,
+                               const double *__restrict__ rz, double *__restrict__ forces,
+                               double *__restrict__ atom_virial, int accumulate)
+{
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= ntotal)
+        return;
+    double fx = 0.0, fy = 0.0, fz = 0.0;
+    double w[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+    if (k < natoms) {
+        for (int e = offsets[k]; e < offsets[k + 1]; ++e) {
+            const double a = dx[e], b = dy[e], c = dz[e];
+            fx += a;
+            fy += b;
+            fz += c;
+            const double x = rx[e], y = ry[e], z = rz[e];
+            w[0] -= a * x; w[1] -= a * y; w[2] -= a * z;
+            w[3] -= b * x; w[4] -= b * y; w[5] -= b * z;
+            w[6] -= c * x; w[7] -= c * y; w[8] -= c * z;
+        }
+    }
+    for (int q = in_offsets[k]; q < in_offsets[k + 1]; ++q) {
+        const int e = in_edges[q];
+        fx -= dx[e];
+        fy -= dy[e];
+        fz -= dz[e];
+    }
+    if (accumulate) {
+        forces[3 * k] += fx;
+        forces[3 * k + 1] += fy;
+        forces[3 * k + 2] += fz;
+    } else {
+        forces[3 * k] = fx;
+        forces[3 * k + 1] = fy;
+        forces[3 * k + 2] = fz;
+    }
+    if (atom_virial && k < natoms) {
+#pragma unroll
+        for (int i = 0; i < 9; ++i)
+            atom_virial[(size_t)i * natoms + k] = w[i];
+    }
+}
+
+cudaError_t launch_force_gather(int natoms, int ntotal, const int *offsets, const int *in_offsets,
+                                const int *in_edges, const double *dx, const double *dy,
+                                const double *dz, const double *rx, const double *ry,
+                                const double *rz, double *forces, double *atom_virial,
+                                int accumulate, cudaStream_t s)
+{
+    if (ntotal == 0)
+        return cudaSuccess;
+    const int threads = 128;
+    k_force_gather<<<(ntotal + threads - 1) / threads, threads, 0, s>>>(
+        natoms, ntotal, offsets, in_offsets, in_edges, dx, dy, dz, rx, ry, rz, forces,
+        atom_virial, accumulate);
+    return cudaGetLastError();
+}
+
+// ----------------------------------------------------------------------------
+// Deterministic reductions: segments (contiguous atoms of one structure, at
+// most 1024 atoms) -> partials[seg][10] = {E, W00..W22}; then per structure.
+// ----------------------------------------------------------------------------
+__global__ void k_segment_reduce(const int *__restrict__ seg_begin,
+                                 const int *__restrict__ seg_end,
+                                 const double *__restrict__ site_energy,
+                                 const double *__restrict__ atom_virial, int natoms,
+                                 double *__restrict__ partials)
+{
+    __shared__ double sh[10][256];
+    const int seg = blockIdx.x;
+    const int b = seg_begin[seg], e = seg_end[seg];
+    double v[10] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+    for (int i = b + threadIdx.x; i < e; i += blockDim.x) {
+        v[0] += site_energy[i];
+        if (atom_virial)
+#pragma unroll
+            for (int q = 0; q < 9; ++q)
+                v[1 + q] += atom_virial[(size_t)q * natoms + i];
+    }
+#pragma unroll
+    for (int q = 0; q < 10; ++q)
+        sh[q][threadIdx.x] = v[q];
+    __syncthreads();
+    for (int st = blockDim.x / 2; st > 0; st >>= 1) {
+        if (threadIdx.x < st)
+#pragma unroll
+            for (int q = 0; q < 10; ++q)
+                sh[q][threadIdx.x] += sh[q][threadIdx.x + st];
+        __syncthreads();
+    }
+    if (threadIdx.x < 10)
+        partials[(size_t)seg * 10 + threadIdx.x] = sh[threadIdx.x][0];
+}
+
+cudaError_t launch_segment_reduce(int nseg, const int *seg_begin, const int *seg_end,
+                                  const double *site_energy, const double *atom_virial,
+                                  int natoms, double *partials, cudaStream_t s)
+{
+    if (nseg == 0)
+        return cudaSuccess;
+    k_segment_reduce<<<nseg, 256, 0, s>>>(seg_begin, seg_end, site_energy, atom_virial, natoms,
+                                          partials);
+    return cudaGetLastError();
+}
+
+__global__ void k_struct_reduce(int nstruct, const int *__restrict__ struct_seg0,
+                                const double *__restrict__ partials, double *__restrict__ energy,
+                                double *__restrict__ virial)
+{
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= nstruct)
+        return;
+    double v[10] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+    for (int g = struct_seg0[s]; g < struct_seg0[s + 1]; ++g)
+#pragma unroll
+        for (int q = 0; q < 10; ++q)
+            v[q] += partials[(size_t)g * 10 + q];
+    if (energy)
+        energy[s] = v[0];
+    if (virial)
+#pragma unroll
+        for (int q = 0; q < 9; ++q)
+            virial[(size_t)s * 9 + q] = v[1 + q];
+}
+
+cudaError_t launch_struct_reduce(int nstruct, const int *struct_seg0, const double *partials,
+                                 double *energy, double *virial, cudaStream_t s)
+{
+    if (nstruct == 0)
+        return cudaSuccess;
+    const int threads = 128;
+    k_struct_reduce<<<(nstruct + threads - 1) / threads, threads, 0, s>>>(
+        nstruct, struct_seg0, partials, energy, virial);
+    return cudaGetLastError();
+}
+
+} // namespace mtpb

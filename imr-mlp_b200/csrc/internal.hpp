@@ -1,0 +1,102 @@
+// internal.hpp -- structures shared by the host planner and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+namespace mtpb {
+
+// Identifies one instantiated basis shape (see shapes.cuh).
+enum ShapeId : int {
+    SHAPE_S1 = 0,
+    SHAPE_S2,
+    SHAPE_L16,
+    SHAPE_L20,
+    SHAPE_L24,
+    SHAPE_PS,
+    SHAPE_COUNT
+};
+
+struct ShapeDesc {
+    int nmu;
+    int numax[8];
+    int nslot;
+};
+
+// Host query of the instantiated shapes and their slot map.
+const ShapeDesc &shape_desc(int id);
+int shape_slot(int id, int mu, int a, int b, int c);
+
+// Radial parameters of one ordered species pair (RBasis_Chebyshev::setup,
+// basis/basis.cpp:119-126): pu = rmax + rmin, su = rmax - rmin,
+// mult = 2 / (rmax - rmin), rmax is also the pair cutoff.
+struct PairParams {
+    double pu, su, mult, rmax;
+};
+
+// Record of the moment-graph program (see dag.cu for the semantics).
+struct DagRec {
+    int s1, s2, out, flags;
+    double c, e;
+};
+enum DagFlags : int {
+    DAG_START = 1,   // first record of an item
+    DAG_END = 2,     // last record of an item: store / accumulate
+    DAG_GLOBAL = 4,  // reverse: out is a kernel slot of the global adjoint array
+};
+
+constexpr int DAG_ATOMS = 16;        // atoms per DAG block (half-warp)
+constexpr int DAG_WARPS = 8;         // warps per DAG block
+constexpr int DAG_STREAMS = 2 * DAG_WARPS;
+
+struct DagPlan {
+    int nrows = 0;           // shared-memory rows (one double per atom each)
+    int one_row = 0;         // row holding 1.0
+    int zero_row = 0;        // row holding 0.0
+    std::vector<int> phase_rows;   // record rows per phase (fwd phases, then reverse)
+    int n_fwd = 0, n_rev = 0;
+    std::vector<DagRec> recs;      // [sum rows][DAG_STREAMS]
+};
+
+// Edge-kernel parameters (device pointers).
+struct EdgeArgs {
+    int natoms;          // centres
+    int npad;            // row stride of the moment/adjoint arrays
+    const int *types;    // [ntotal] species of every atom referenced
+    const int *offsets;  // [natoms+1]
+    const int *nbr;      // [E]
+    const double *rx, *ry, *rz;  // [E]
+    const int *group_maxdeg;     // [ceil(natoms/32)]
+    int K, R, mu_total;
+    double scaling;
+    const double *radial;          // [K*K][mu_total][R]
+    const PairParams *pairs;       // [K*K]
+};
+
+// launchers (efs.cu)
+cudaError_t launch_moments_fwd(int shape, const EdgeArgs &a, double *basic, cudaStream_t s);
+cudaError_t launch_moments_rev(int shape, const EdgeArgs &a, const double *adjoint, double *dx,
+                               double *dy, double *dz, cudaStream_t s);
+cudaError_t launch_dag(const DagPlan &plan, const DagRec *recs, const int *phase_row0,
+                       int nslot, int natoms, int npad, const int *types,
+                       const double *species_coeffs, const double *basic, double *adjoint,
+                       double *site_energy, cudaStream_t s);
+cudaError_t launch_group_maxdeg(int natoms, const int *offsets, int *group_maxdeg,
+                                cudaStream_t s);
+cudaError_t launch_force_gather(int natoms, int ntotal, const int *offsets, const int *in_offsets,
+                                const int *in_edges, const double *dx, const double *dy,
+                                const double *dz, const double *rx, const double *ry,
+                                const double *rz, double *forces, double *atom_virial,
+                                int accumulate, cudaStream_t s);
+cudaError_t launch_segment_reduce(int nseg, const int *seg_begin, const int *seg_end,
+                                  const double *site_energy, const double *atom_virial,
+                                  int natoms, double *partials, cudaStream_t s);
+cudaError_t launch_struct_reduce(int nstruct, const int *struct_seg0, const double *partials,
+                                 double *energy, double *virial, cudaStream_t s);
+
+
+} // namespace mtpb

@@ -1,0 +1,389 @@
+// neighbors.cu -- GPU cell-list neighbour builder whose per-atom neighbour
+// sets equal the reference's default builder bit for bit.
+//
+// Reference behaviour (paths relative to the reference project):
+//   base/neighborhoods_base.h:113-126  wrap: frac = p * inv(cell),
+//                                      frac -= floor(frac), p = frac * cell
+//   base/neighborhoods_base.h:31-99    periodic images: translation =
+//                                      basis * image, basis = periodic cell
+//                                      rows sorted by squared length
+//   base/neighborhood.cpp:103-134      for a centre i and an image point of
+//                                      atom o with i <= o: r = p_o - p_i,
+//                                      accept r.r < rc^2, emit (o, r) to i
+//                                      and (i, -r) to o when i != o
+// A centre i therefore sees neighbour o at displacement
+//   (w_o + T) - w_i            when i <= o, and
+//   -((w_i + (-T)) - w_o)      when i >  o,
+// where w are wrapped positions and T the image translation, every operation
+// rounded as written (no fused multiply-add).  Each centre computes its own
+// list independently with that rule, so no pairing step is needed.
+//
+// The search itself is a cell list in fractional coordinates: cells at least
+// rc (perpendicular) thick, a stencil of +-ceil(rc*n/width) cells, periodic
+// cell indices mapped to (cell, shift).  Atom lists inside a cell are sorted
+// so that the output order is deterministic.
+#include "internal.hpp"
+#include "neighbors.hpp"
+
+#include <cub/cub.cuh>
+
+namespace mtpb {
+
+__device__ __forceinline__ double dadd(double a, double b) { return __dadd_rn(a, b); }
+__device__ __forceinline__ double dmul(double a, double b) { return __dmul_rn(a, b); }
+
+// (p0*M(0,d) + p1*M(1,d)) + p2*M(2,d)  (Eigen RowVector3d * Matrix3d)
+__device__ __forceinline__ void rowvec_mat(const double p[3], const double *M, double out[3])
+{
+    double r[3];
+#pragma unroll
+    for (int d = 0; d < 3; ++d)
+        r[d] = dadd(dadd(dmul(p[0], M[d]), dmul(p[1], M[3 + d])), dmul(p[2], M[6 + d]));
+    out[0] = r[0];
+    out[1] = r[1];
+    out[2] = r[2];
+}
+
+// Eigen Matrix3d * Vector3d: rows 0,1 (t0 + t1) + t2; row 2 t0 + (t1 + t2).
+__device__ __forceinline__ void image_translation(const NbStruct &st, int s0, int s1, int s2,
+                                                  double t[3])
+{
+    const int sh[3] = {s0, s1, s2};
+    double img[3] = {0.0, 0.0, 0.0};
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+        if (k < st.dims)
+            img[k] = (double)sh[st.axes[k]];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+        t[r] = dadd(dadd(dmul(st.B[r][0], img[0]), dmul(st.B[r][1], img[1])),
+                    dmul(st.B[r][2], img[2]));
+    t[2] = dadd(dmul(st.B[2][0], img[0]), dadd(dmul(st.B[2][1], img[1]), dmul(st.B[2][2], img[2])));
+}
+
+__global__ void k_struct_ids(int nstruct, const int *__restrict__ atom_offsets, int natoms,
+                             int *__restrict__ struct_of)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= natoms)
+        return;
+    int lo = 0, hi = nstruct - 1;
+    while (lo < hi) {   // last s with atom_offsets[s] <= i
+        const int mid = (lo + hi + 1) >> 1;
+        if (atom_offsets[mid] <= i)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    struct_of[i] = lo;
+}
+
+__global__ void k_wrap_bin(int natoms, const NbStruct *__restrict__ structs,
+                           const int *__restrict__ struct_of, const double *__restrict__ pos,
+                           double *__restrict__ wx, double *__restrict__ wy,
+                           double *__restrict__ wz, int *__restrict__ cell_of,
+                           int *__restrict__ cell_count)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= natoms)
+        return;
+    const NbStruct &st = structs[struct_of[i]];
+    const double p[3] = {pos[3 * i], pos[3 * i + 1], pos[3 * i + 2]};
+    double f[3];
+    rowvec_mat(p, st.inv, f);
+#pragma unroll
+    for (int d = 0; d < 3; ++d)
+        f[d] = __dsub_rn(f[d], floor(f[d]));
+    double w[3];
+    rowvec_mat(f, st.cell, w);
+    wx[i] = w[0];
+    wy[i] = w[1];
+    wz[i] = w[2];
+    int c[3];
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+        int q = (int)floor(f[d] * st.ncell[d]);
+        c[d] = q < 0 ? 0 : (q >= st.ncell[d] ? st.ncell[d] - 1 : q);
+    }
+    const int cell = st.cell0 + (c[0] * st.ncell[1] + c[1]) * st.ncell[2] + c[2];
+    cell_of[i] = cell;
+    atomicAdd(cell_count + cell, 1);
+}
+
+__global__ void k_fill_cells(int natoms, const int *__restrict__ cell_of,
+                             const int *__restrict__ cell_start, int *__restrict__ cell_cursor,
+                             int *__restrict__ cell_atoms)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= natoms)
+        return;
+    const int c = cell_of[i];
+    cell_atoms[cell_start[c] + atomicAdd(cell_cursor + c, 1)] = i;
+}
+
+// insertion sort of small segments (atoms of a cell, in-edges of an atom)
+__global__ void k_sort_segments(int nseg, const int *__restrict__ start, int *__restrict__ data)
+{
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= nseg)
+        return;
+    const int b = start[s], e = start[s + 1];
+    for (int i = b + 1; i < e; ++i) {
+        const int v = data[i];
+        int j = i - 1;
+        while (j >= b && data[j] > v) {
+            data[j + 1] = data[j];
+            --j;
+        }
+        data[j + 1] = v;
+    }
+}
+
+// Traverses the candidate set of centre i; FILL selects counting or writing.
+template <bool FILL>
+__global__ void k_neighbors(int natoms, const NbStruct *__restrict__ structs,
+                            const int *__restrict__ struct_of, const double *__restrict__ wx,
+                            const double *__restrict__ wy, const double *__restrict__ wz,
+                            const int *__restrict__ cell_of, const int *__restrict__ cell_start,
+                            const int *__restrict__ cell_atoms, int *__restrict__ counts,
+                            const int *__restrict__ offsets, int *__restrict__ nbr,
+                            int *__restrict__ shift_code, double *__restrict__ rx,
+                            double *__restrict__ ry, double *__restrict__ rz)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= natoms)
+        return;
+    const NbStruct &st = structs[struct_of[i]];
+    const double xi = wx[i], yi = wy[i], zi = wz[i];
+    int rel = cell_of[i] - st.cell0;
+    const int c2 = rel % st.ncell[2];
+    rel /= st.ncell[2];
+    const int c1 = rel % st.ncell[1];
+    const int c0 = rel / st.ncell[1];
+    int count = 0;
+    int out = FILL ? offsets[i] : 0;
+    for (int d0 = -st.stencil[0]; d0 <= st.stencil[0]; ++d0) {
+        const int a0 = c0 + d0;
+        const int s0 = (a0 >= 0) ? a0 / st.ncell[0] : -((-a0 + st.ncell[0] - 1) / st.ncell[0]);
+        const int w0 = a0 - s0 * st.ncell[0];
+        for (int d1 = -st.stencil[1]; d1 <= st.stencil[1]; ++d1) {
+            const int a1 = c1 + d1;
+            const int s1 = (a1 >= 0) ? a1 / st.ncell[1] : -((-a1 + st.ncell[1] - 1) / st.ncell[1]);
+            const int w1 = a1 - s1 * st.ncell[1];
+            for (int d2 = -st.stencil[2]; d2 <= st.stencil[2]; ++d2) {
+                const int a2 = c2 + d2;
+                const int s2 =
+                    (a2 >= 0) ? a2 / st.ncell[2] : -((-a2 + st.ncell[2] - 1) / st.ncell[2]);
+                const int w2 = a2 - s2 * st.ncell[2];
+                const bool zero = (s0 == 0 && s1 == 0 && s2 == 0);
+                double t[3];
+                image_translation(st, s0, s1, s2, t);
+                const int cell = st.cell0 + (w0 * st.ncell[1] + w1) * st.ncell[2] + w2;
+                for (int q = cell_start[cell]; q < cell_start[cell + 1]; ++q) {
+                    const int o = cell_atoms[q];
+                    if (zero && o == i)
+                        continue;
+                    const double xo = wx[o], yo = wy[o], zo = wz[o];
+                    double r0, r1, r2;
+                    if (i <= o) {
+                        const double px = zero ? xo : dadd(xo, t[0]);
+                        const double py = zero ? yo : dadd(yo, t[1]);
+                        const double pz = zero ? zo : dadd(zo, t[2]);
+                        r0 = __dsub_rn(px, xi);
+                        r1 = __dsub_rn(py, yi);
+                        r2 = __dsub_rn(pz, zi);
+                    } else {
+                        const double px = zero ? xi : dadd(xi, -t[0]);
+                        const double py = zero ? yi : dadd(yi, -t[1]);
+                        const double pz = zero ? zi : dadd(zi, -t[2]);
+                        r0 = -__dsub_rn(px, xo);
+                        r1 = -__dsub_rn(py, yo);
+                        r2 = -__dsub_rn(pz, zo);
+                    }
+                    const double dsq = dadd(dadd(dmul(r0, r0), dmul(r1, r1)), dmul(r2, r2));
+                    if (dsq < st.cutsq) {
+                        if (FILL) {
+                            nbr[out] = o;
+                            shift_code[out] = (s0 + 128) | ((s1 + 128) << 8) | ((s2 + 128) << 16);
+                            rx[out] = r0;
+                            ry[out] = r1;
+                            rz[out] = r2;
+                            ++out;
+                        } else {
+                            ++count;
+                        }
+                    }
+                }
+            }
+        }
+    }
+    if (!FILL)
+        counts[i] = count;
+}
+
+__global__ void k_in_count(long nedges, const int *__restrict__ nbr, int *__restrict__ in_count)
+{
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e < nedges)
+        atomicAdd(in_count + nbr[e], 1);
+}
+
+__global__ void k_in_fill(long nedges, const int *__restrict__ nbr,
+                          const int *__restrict__ in_offsets, int *__restrict__ cursor,
+                          int *__restrict__ in_edges)
+{
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e < nedges) {
+        const int j = nbr[e];
+        in_edges[in_offsets[j] + atomicAdd(cursor + j, 1)] = (int)e;
+    }
+}
+
+// r_ij = x[j] - x[i] for caller-supplied lists (LAMMPS / CSR requests)
+__global__ void k_edge_vectors(int ncenter, const int *__restrict__ offsets,
+                               const int *__restrict__ nbr, const double *__restrict__ x,
+                               double *__restrict__ rx, double *__restrict__ ry,
+                               double *__restrict__ rz)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= ncenter)
+        return;
+    const double xi = x[3 * i], yi = x[3 * i + 1], zi = x[3 * i + 2];
+    for (int e = offsets[i]; e < offsets[i + 1]; ++e) {
+        const int j = nbr[e];
+        rx[e] = __dsub_rn(x[3 * j], xi);
+        ry[e] = __dsub_rn(x[3 * j + 1], yi);
+        rz[e] = __dsub_rn(x[3 * j + 2], zi);
+    }
+}
+
+static inline int nblk(long n, int t) { return (int)((n + t - 1) / t); }
+
+cudaError_t exclusive_scan(const int *in, int *out, int n, DeviceArena &arena, cudaStream_t s)
+{
+    // out has n+1 entries: out[0] = 0, out[k+1] = sum in[0..k]
+    size_t tmp = 0;
+    cudaError_t err = cub::DeviceScan::InclusiveSum(nullptr, tmp, in, out + 1, n, s);
+    if (err != cudaSuccess)
+        return err;
+    void *t = arena.get("scan_tmp", tmp + 16);
+    if (!t)
+        return cudaErrorMemoryAllocation;
+    err = cudaMemsetAsync(out, 0, sizeof(int), s);
+    if (err != cudaSuccess)
+        return err;
+    if (n == 0)
+        return cudaSuccess;
+    return cub::DeviceScan::InclusiveSum(t, tmp, in, out + 1, n, s);
+}
+
+cudaError_t build_neighbors(const NbBuildInput &in, DeviceArena &arena, NbResult &res,
+                            cudaStream_t s)
+{
+    const int N = in.natoms;
+    const int T = 256;
+    cudaError_t err;
+#define CK(x)                                                                                      \
+    do {                                                                                           \
+        err = (x);                                                                                 \
+        if (err != cudaSuccess)                                                                    \
+            return err;                                                                            \
+    } while (0)
+    int *struct_of = arena.get<int>("nb_struct_of", N);
+    double *wx = arena.get<double>("nb_wx", N), *wy = arena.get<double>("nb_wy", N),
+           *wz = arena.get<double>("nb_wz", N);
+    int *cell_of = arena.get<int>("nb_cell_of", N);
+    int *cell_count = arena.get<int>("nb_cell_count", in.total_cells + 1);
+    int *cell_start = arena.get<int>("nb_cell_start", in.total_cells + 1);
+    int *cell_cursor = arena.get<int>("nb_cell_cursor", in.total_cells + 1);
+    int *cell_atoms = arena.get<int>("nb_cell_atoms", N);
+    int *counts = arena.get<int>("nb_counts", N + 1);
+    int *offsets = arena.get<int>("offsets", N + 1);
+    if (!struct_of || !wx || !wy || !wz || !cell_of || !cell_count || !cell_start ||
+        !cell_cursor || !cell_atoms || !counts || !offsets)
+        return cudaErrorMemoryAllocation;
+    res.wx = wx;
+    res.wy = wy;
+    res.wz = wz;
+    res.offsets = offsets;
+    if (N == 0) {
+        CK(cudaMemsetAsync(offsets, 0, sizeof(int), s));
+        res.nedges = 0;
+        return cudaSuccess;
+    }
+    CK(cudaMemsetAsync(cell_count, 0, sizeof(int) * (in.total_cells + 1), s));
+    CK(cudaMemsetAsync(cell_cursor, 0, sizeof(int) * (in.total_cells + 1), s));
+    k_struct_ids<<<nblk(N, T), T, 0, s>>>(in.nstruct, in.atom_offsets, N, struct_of);
+    k_wrap_bin<<<nblk(N, T), T, 0, s>>>(N, in.structs, struct_of, in.positions, wx, wy, wz,
+                                       cell_of, cell_count);
+    CK(cudaGetLastError());
+    CK(exclusive_scan(cell_count, cell_start, in.total_cells, arena, s));
+    k_fill_cells<<<nblk(N, T), T, 0, s>>>(N, cell_of, cell_start, cell_cursor, cell_atoms);
+    k_sort_segments<<<nblk(in.total_cells, T), T, 0, s>>>(in.total_cells, cell_start,
+                                                          cell_atoms);
+    k_neighbors<false><<<nblk(N, 128), 128, 0, s>>>(N, in.structs, struct_of, wx, wy, wz, cell_of,
+                                                    cell_start, cell_atoms, counts, nullptr,
+                                                    nullptr, nullptr, nullptr, nullptr, nullptr);
+    CK(cudaGetLastError());
+    CK(exclusive_scan(counts, offsets, N, arena, s));
+    int E = 0;
+    CK(cudaMemcpyAsync(&E, offsets + N, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    res.nedges = E;
+    int *nbr = arena.get<int>("nbr", (size_t)E + 1);
+    int *shift = arena.get<int>("shift", (size_t)E + 1);
+    double *rx = arena.get<double>("rx", (size_t)E + 1);
+    double *ry = arena.get<double>("ry", (size_t)E + 1);
+    double *rz = arena.get<double>("rz", (size_t)E + 1);
+    if (!nbr || !shift || !rx || !ry || !rz)
+        return cudaErrorMemoryAllocation;
+    k_neighbors<true><<<nblk(N, 128), 128, 0, s>>>(N, in.structs, struct_of, wx, wy, wz, cell_of,
+                                                   cell_start, cell_atoms, nullptr, offsets, nbr,
+                                                   shift, rx, ry, rz);
+    CK(cudaGetLastError());
+    res.nbr = nbr;
+    res.shift = shift;
+    res.rx = rx;
+    res.ry = ry;
+    res.rz = rz;
+    CK(build_in_edges(N, E, nbr, arena, res, s));
+    return cudaSuccess;
+#undef CK
+}
+
+cudaError_t build_in_edges(int ntotal, long E, const int *nbr, DeviceArena &arena, NbResult &res,
+                           cudaStream_t s)
+{
+    cudaError_t err;
+    int *in_count = arena.get<int>("in_count", ntotal + 1);
+    int *in_offsets = arena.get<int>("in_offsets", ntotal + 1);
+    int *cursor = arena.get<int>("in_cursor", ntotal + 1);
+    int *in_edges = arena.get<int>("in_edges", (size_t)E + 1);
+    if (!in_count || !in_offsets || !cursor || !in_edges)
+        return cudaErrorMemoryAllocation;
+    if ((err = cudaMemsetAsync(in_count, 0, sizeof(int) * (ntotal + 1), s)) != cudaSuccess)
+        return err;
+    if ((err = cudaMemsetAsync(cursor, 0, sizeof(int) * (ntotal + 1), s)) != cudaSuccess)
+        return err;
+    if (E > 0)
+        k_in_count<<<nblk(E, 256), 256, 0, s>>>(E, nbr, in_count);
+    if ((err = exclusive_scan(in_count, in_offsets, ntotal, arena, s)) != cudaSuccess)
+        return err;
+    if (E > 0)
+        k_in_fill<<<nblk(E, 256), 256, 0, s>>>(E, nbr, in_offsets, cursor, in_edges);
+    k_sort_segments<<<nblk(ntotal, 128), 128, 0, s>>>(ntotal, in_offsets, in_edges);
+    res.in_offsets = in_offsets;
+    res.in_edges = in_edges;
+    return cudaGetLastError();
+}
+
+cudaError_t edge_vectors(int ncenter, const int *offsets, const int *nbr, const double *x,
+                         double *rx, double *ry, double *rz, cudaStream_t s)
+{
+    if (ncenter == 0)
+        return cudaSuccess;
+    k_edge_vectors<<<nblk(ncenter, 128), 128, 0, s>>>(ncenter, offsets, nbr, x, rx, ry, rz);
+    return cudaGetLastError();
+}
+
+} // namespace mtpb

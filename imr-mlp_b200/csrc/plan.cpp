@@ -1,0 +1,408 @@
+// plan.cpp -- host-side model planning: graph validation, basis-shape
+// selection, kernel slot map, moment-graph program and cell preparation.
+#include "plan.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <numeric>
+#include <unordered_set>
+
+namespace mtpb {
+
+// Moment-graph checks of MLIPCore::setup_from_text
+// (runtime/mtp/mlip.cpp:700-760): every rule input defined before use, no
+// cycles, no accumulation into a target after it was consumed, scalars map to
+// defined moments.
+bool validate_model(const ModelHost &m, std::string *err)
+{
+    auto fail = [&](const std::string &s) {
+        if (err)
+            *err = "invalid MTP model: " + s;
+        return false;
+    };
+    if (m.K <= 0 || m.K > 64)
+        return fail("species_count must be in 1..64");
+    if (m.mu <= 0 || m.R <= 0 || m.R > 64)
+        return fail("radial_funcs_count and radial_basis_size must be positive (R <= 64)");
+    const int pairs = m.split ? m.K * m.K : 1;
+    if ((int)m.min_dist.size() != pairs || (int)m.max_dist.size() != pairs)
+        return fail("radial interval count does not match the split flag");
+    for (int p = 0; p < pairs; ++p)
+        if (!(m.max_dist[p] > m.min_dist[p]) || !std::isfinite(m.max_dist[p]) ||
+            !std::isfinite(m.min_dist[p]) || m.min_dist[p] < 0)
+            return fail("invalid radial interval");
+    if (!std::isfinite(m.scaling))
+        return fail("scaling must be finite");
+    const int nb = m.nb(), M = m.M;
+    if (nb <= 0 || nb > M)
+        return fail("basic moment count exceeds total moment slots");
+    for (int i = 0; i < nb; ++i) {
+        const int *b = &m.basic[4 * i];
+        if (b[0] < 0 || b[0] >= m.mu || b[1] < 0 || b[2] < 0 || b[3] < 0)
+            return fail("invalid basic moment index");
+    }
+    std::vector<char> defined(M, 0), consumed(M, 0);
+    for (int i = 0; i < nb; ++i)
+        defined[i] = 1;
+    for (int t = 0; t < m.T(); ++t) {
+        const int *r = &m.times[4 * t];
+        const int l1 = r[0], l2 = r[1], id = r[3];
+        if (l1 < 0 || l1 >= M || l2 < 0 || l2 >= M || id < nb || id >= M || !defined[l1] ||
+            !defined[l2] || id == l1 || id == l2 || consumed[id])
+            return fail("moment graph has an undefined input, cycle or late accumulation");
+        defined[id] = 1;
+        consumed[l1] = 1;
+        consumed[l2] = 1;
+    }
+    for (int s = 0; s < m.S(); ++s) {
+        const int x = m.mapping[s];
+        if (x < 0 || x >= M || !defined[x])
+            return fail("scalar maps to an undefined moment");
+    }
+    if ((int)m.radial.size() != m.K * m.K * m.mu * m.R || (int)m.species.size() != m.K ||
+        (int)m.moment.size() != m.S())
+        return fail("coefficient array sizes do not match the model");
+    for (double v : m.radial)
+        if (!std::isfinite(v))
+            return fail("radial coefficients must be finite");
+    for (double v : m.species)
+        if (!std::isfinite(v))
+            return fail("species coefficients must be finite");
+    for (double v : m.moment)
+        if (!std::isfinite(v))
+            return fail("moment coefficients must be finite");
+    return true;
+}
+
+// Smallest instantiated shape whose complete tensors contain every basic
+// moment of the model.
+int select_shape(const ModelHost &m, std::string *err)
+{
+    std::vector<int> need(m.mu, -1);
+    for (int i = 0; i < m.nb(); ++i) {
+        const int *b = &m.basic[4 * i];
+        need[b[0]] = std::max(need[b[0]], b[1] + b[2] + b[3]);
+    }
+    int best = -1, best_slots = 1 << 30;
+    for (int id = 0; id < SHAPE_COUNT; ++id) {
+        const ShapeDesc &d = shape_desc(id);
+        bool ok = true;
+        for (int mu = 0; mu < m.mu && ok; ++mu)
+            if (need[mu] >= 0 && (mu >= d.nmu || d.numax[mu] < need[mu]))
+                ok = false;
+        if (ok && d.nslot < best_slots) {
+            best = id;
+            best_slots = d.nslot;
+        }
+    }
+    if (best < 0 && err) {
+        std::string s = "basis shape not supported by the compiled kernels; max degree per "
+                        "radial channel:";
+        for (int v : need)
+            s += " " + std::to_string(v);
+        *err = s;
+    }
+    return best;
+}
+
+bool build_slot_map(const ModelHost &m, int shape, std::vector<int> &slot_of_basic,
+                    std::string *err)
+{
+    slot_of_basic.assign(m.nb(), -1);
+    std::vector<char> used(shape_desc(shape).nslot, 0);
+    for (int i = 0; i < m.nb(); ++i) {
+        const int *b = &m.basic[4 * i];
+        const int s = shape_slot(shape, b[0], b[1], b[2], b[3]);
+        if (s < 0) {
+            if (err)
+                *err = "basic moment outside the selected kernel shape";
+            return false;
+        }
+        if (used[s]) {
+            if (err)
+                *err = "duplicate basic moment in alpha_index_basic";
+            return false;
+        }
+        used[s] = 1;
+        slot_of_basic[i] = s;
+    }
+    return true;
+}
+
+namespace {
+
+struct Item {
+    std::vector<DagRec> recs;
+};
+
+// Longest-processing-time assignment of items to DAG_STREAMS streams, then
+// padding to equal length.  Appends the phase to plan.recs.
+void emit_phase(std::vector<Item> &items, DagPlan &plan)
+{
+    std::vector<int> order(items.size());
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
+        return items[a].recs.size() > items[b].recs.size();
+    });
+    std::vector<std::vector<DagRec>> streams(DAG_STREAMS);
+    std::vector<size_t> load(DAG_STREAMS, 0);
+    for (int idx : order) {
+        int s = (int)(std::min_element(load.begin(), load.end()) - load.begin());
+        for (const DagRec &r : items[idx].recs)
+            streams[s].push_back(r);
+        load[s] += items[idx].recs.size();
+    }
+    size_t len = *std::max_element(load.begin(), load.end());
+    DagRec pad{plan.zero_row, plan.zero_row, -1, 0, 0.0, 0.0};
+    for (size_t r = 0; r < len; ++r)
+        for (int s = 0; s < DAG_STREAMS; ++s)
+            plan.recs.push_back(r < streams[s].size() ? streams[s][r] : pad);
+    plan.phase_rows.push_back((int)len);
+}
+
+} // namespace
+
+// Builds the record program executed by k_dag (efs.cu).  Forward phases follow
+// the forward product rules level by level (potential_mtp.cpp:2914-2921 order
+// within a target), accumulating the linear energy of scalar moments
+// (:2966-2970).  Reverse phases compute the adjoint of every moment that is a
+// rule operand, by decreasing level, as a sum over its uses (the gather form
+// of backpropagate_moments, :3292-3305), and finally the adjoints of the basic
+// moments, written to the kernel slots.
+bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_of_basic,
+                    DagPlan &plan, std::string *err)
+{
+    const int nb = m.nb(), M = m.M, T = m.T();
+    const int nslot = shape_desc(shape).nslot;
+    std::vector<int> level(M, 0);
+    std::vector<char> is_operand(M, 0), is_target(M, 0);
+    for (int t = 0; t < T; ++t) {
+        const int *r = &m.times[4 * t];
+        level[r[3]] = std::max(level[r[3]], std::max(level[r[0]], level[r[1]]) + 1);
+        is_operand[r[0]] = is_operand[r[1]] = 1;
+        is_target[r[3]] = 1;
+    }
+    int maxlevel = 0;
+    for (int x = 0; x < M; ++x)
+        maxlevel = std::max(maxlevel, level[x]);
+    std::vector<double> scal(M, 0.0);
+    std::vector<char> is_scalar(M, 0);
+    for (int s = 0; s < m.S(); ++s) {
+        scal[m.mapping[s]] += m.moment[s];
+        is_scalar[m.mapping[s]] = 1;
+    }
+    // rows: kernel slots, operand targets, their adjoints, constants
+    std::vector<int> row(M, -1), adjrow(M, -1);
+    for (int i = 0; i < nb; ++i)
+        row[i] = slot_of_basic[i];
+    int next = nslot;
+    for (int x = nb; x < M; ++x)
+        if (is_target[x] && is_operand[x])
+            row[x] = next++;
+    for (int x = nb; x < M; ++x)
+        if (row[x] >= 0)
+            adjrow[x] = next++;
+    plan = DagPlan{};
+    plan.one_row = next++;
+    plan.zero_row = next++;
+    plan.nrows = next;
+    if ((size_t)plan.nrows * DAG_ATOMS * sizeof(double) > 220 * 1024) {
+        if (err)
+            *err = "moment graph too large for the shared-memory plan (" +
+                   std::to_string(plan.nrows) + " rows)";
+        return false;
+    }
+    // rules grouped by target, in file order
+    std::vector<std::vector<int>> rules_of(M);
+    for (int t = 0; t < T; ++t)
+        rules_of[m.times[4 * t + 3]].push_back(t);
+
+    // ---- forward phases ----------------------------------------------------
+    const int nfwd = std::max(1, maxlevel);
+    for (int L = 1; L <= nfwd; ++L) {
+        std::vector<Item> items;
+        if (L == 1) {   // scalar basic moments contribute directly
+            for (int x = 0; x < nb; ++x)
+                if (is_scalar[x]) {
+                    Item it;
+                    it.recs.push_back({row[x], plan.one_row, -1, DAG_START | DAG_END, 1.0, scal[x]});
+                    items.push_back(std::move(it));
+                }
+        }
+        for (int x = nb; x < M; ++x) {
+            if (!is_target[x] || level[x] != L)
+                continue;
+            if (!is_operand[x] && !is_scalar[x])
+                continue;   // contributes nothing
+            Item it;
+            const auto &rl = rules_of[x];
+            for (size_t k = 0; k < rl.size(); ++k) {
+                const int *r = &m.times[4 * rl[k]];
+                DagRec rec{row[r[0]], row[r[1]], -1, 0, (double)r[2], 0.0};
+                if (k == 0)
+                    rec.flags |= DAG_START;
+                if (k + 1 == rl.size()) {
+                    rec.flags |= DAG_END;
+                    rec.out = is_operand[x] ? row[x] : -1;
+                    rec.e = scal[x];
+                }
+                it.recs.push_back(rec);
+            }
+            items.push_back(std::move(it));
+        }
+        emit_phase(items, plan);
+    }
+    plan.n_fwd = nfwd;
+
+    // ---- reverse phases ----------------------------------------------------
+    // uses of each operand: (target, other operand, coefficient)
+    struct Use {
+        int target, other;
+        double c;
+    };
+    std::vector<std::vector<Use>> uses(M);
+    for (int t = 0; t < T; ++t) {
+        const int *r = &m.times[4 * t];
+        uses[r[0]].push_back({r[3], r[1], (double)r[2]});
+        uses[r[1]].push_back({r[3], r[0], (double)r[2]});
+    }
+    auto make_item = [&](int x, int out, int flags) {
+        Item it;
+        for (const Use &u : uses[x]) {
+            if (adjrow[u.target] >= 0)
+                it.recs.push_back({adjrow[u.target], row[u.other], -1, 0, u.c, 0.0});
+            else if (is_scalar[u.target])
+                it.recs.push_back({plan.one_row, row[u.other], -1, 0, u.c * scal[u.target], 0.0});
+        }
+        if (it.recs.empty())
+            it.recs.push_back({plan.zero_row, plan.zero_row, -1, 0, 0.0, 0.0});
+        it.recs.front().flags |= DAG_START;
+        it.recs.front().e = scal[x];
+        it.recs.back().flags |= DAG_END | flags;
+        it.recs.back().out = out;
+        return it;
+    };
+    int nrev = 0;
+    for (int L = maxlevel - 1; L >= 1; --L) {
+        std::vector<Item> items;
+        for (int x = nb; x < M; ++x)
+            if (adjrow[x] >= 0 && level[x] == L)
+                items.push_back(make_item(x, adjrow[x], 0));
+        emit_phase(items, plan);
+        ++nrev;
+    }
+    {
+        std::vector<Item> items;
+        std::vector<char> slot_used(nslot, 0);
+        for (int x = 0; x < nb; ++x) {
+            items.push_back(make_item(x, slot_of_basic[x], DAG_GLOBAL));
+            slot_used[slot_of_basic[x]] = 1;
+        }
+        for (int s = 0; s < nslot; ++s)
+            if (!slot_used[s]) {
+                Item it;
+                it.recs.push_back({plan.zero_row, plan.zero_row, s,
+                                   DAG_START | DAG_END | DAG_GLOBAL, 0.0, 0.0});
+                items.push_back(std::move(it));
+            }
+        emit_phase(items, plan);
+        ++nrev;
+    }
+    plan.n_rev = nrev;
+    return true;
+}
+
+// Eigen fixed-size 3x3 inverse order (see oracle/mtp_oracle.c inverse3 for
+// the bit-level check against Eigen): det = (c0*m00 + c1*m10) + c2*m20,
+// inv(i,j) = cofactor(j,i) * (1/det).
+static double cof3(const double *m, int i, int j)
+{
+    int i1 = (i + 1) % 3, i2 = (i + 2) % 3, j1 = (j + 1) % 3, j2 = (j + 2) % 3;
+    return m[i1 * 3 + j1] * m[i2 * 3 + j2] - m[i1 * 3 + j2] * m[i2 * 3 + j1];
+}
+
+bool prepare_struct(const double *cell, const int *pbc, double cutoff, NbStruct &out,
+                    std::string *error)
+{
+    for (int a = 0; a < 3; ++a)
+        if (pbc && !pbc[a]) {
+            if (error)
+                *error = "the GPU neighbour builder handles fully periodic cells; pass "
+                         "explicit neighbour lists (mtpb_efs_csr) for other boundaries";
+            return false;
+        }
+    for (int i = 0; i < 9; ++i) {
+        if (!std::isfinite(cell[i])) {
+            if (error)
+                *error = "cell must be finite";
+            return false;
+        }
+        out.cell[i] = cell[i];
+    }
+    volatile double c0 = cof3(cell, 0, 0), c1 = cof3(cell, 1, 0), c2 = cof3(cell, 2, 0);
+    volatile double det = (c0 * cell[0] + c1 * cell[3]) + c2 * cell[6];
+    if (!(std::fabs(det) > 0)) {
+        if (error)
+            *error = "singular cell";
+        return false;
+    }
+    const double invdet = 1.0 / det;
+    for (int i = 0; i < 3; ++i)
+        for (int j = 0; j < 3; ++j)
+            out.inv[i * 3 + j] = cof3(cell, j, i) * invdet;
+    // image basis (neighborhoods_base.h:36-48): rows sorted by squared norm,
+    // stable for ties
+    auto sqn = [&](int a) {
+        const double *r = cell + 3 * a;
+        return r[0] * r[0] + (r[1] * r[1] + r[2] * r[2]);
+    };
+    int axes[3] = {0, 1, 2};
+    for (int i = 1; i < 3; ++i) {
+        int v = axes[i], j = i;
+        while (j > 0 && sqn(v) < sqn(axes[j - 1])) {
+            axes[j] = axes[j - 1];
+            --j;
+        }
+        axes[j] = v;
+    }
+    out.dims = 3;
+    for (int k = 0; k < 3; ++k) {
+        out.axes[k] = axes[k];
+        for (int r = 0; r < 3; ++r)
+            out.B[r][k] = cell[3 * axes[k] + r];
+    }
+    // cell grid: perpendicular widths V / |a_b x a_c|
+    const double *rows[3] = {cell, cell + 3, cell + 6};
+    double cr[3][3];
+    for (int a = 0; a < 3; ++a) {
+        const double *u = rows[(a + 1) % 3], *v = rows[(a + 2) % 3];
+        cr[a][0] = u[1] * v[2] - u[2] * v[1];
+        cr[a][1] = u[2] * v[0] - u[0] * v[2];
+        cr[a][2] = u[0] * v[1] - u[1] * v[0];
+    }
+    const double vol =
+        std::fabs(rows[0][0] * cr[0][0] + rows[0][1] * cr[0][1] + rows[0][2] * cr[0][2]);
+    for (int a = 0; a < 3; ++a) {
+        const double nrm = std::sqrt(cr[a][0] * cr[a][0] + cr[a][1] * cr[a][1] + cr[a][2] * cr[a][2]);
+        const double width = vol / nrm;
+        // cells at least rc thick (with a small safety margin)
+        int n = (int)std::floor(width / (cutoff * (1.0 + 1e-9)));
+        if (n < 1)
+            n = 1;
+        if (n > 1024)
+            n = 1024;
+        out.ncell[a] = n;
+        const double thick = width / n;
+        out.stencil[a] = (int)std::ceil(cutoff * (1.0 + 1e-9) / thick);
+        if (out.stencil[a] > 64) {
+            if (error)
+                *error = "cell too thin for the cutoff (more than 64 periodic images)";
+            return false;
+        }
+    }
+    out.cutsq = cutoff * cutoff;
+    out.cell0 = 0;
+    return true;
+}
+
+} // namespace mtpb

@@ -1,0 +1,126 @@
+"""Seeded synthetic structures and model coefficients for the benchmark
+configurations (no dataset is involved; every input is generated).
+
+Species indices: Ni = 0, Al = 1, Cr = 2 for the metallic configurations;
+Ru = 0, O = 1, H = 2 for the interface configuration.
+
+Structures are plain dictionaries of numpy arrays:
+``cell`` (3x3, rows are lattice vectors, Angstrom), ``pbc`` (3 ints),
+``positions`` (N x 3), ``types`` (N int32).
+"""
+from __future__ import annotations
+
+import dataclasses
+from typing import Dict, List
+
+import numpy as np
+
+from .mtpfile import MTPModel
+
+FCC_BASIS = np.array([[0.0, 0.0, 0.0], [0.5, 0.5, 0.0], [0.5, 0.0, 0.5], [0.0, 0.5, 0.5]])
+BCC_BASIS = np.array([[0.0, 0.0, 0.0], [0.5, 0.5, 0.5]])
+
+
+def _supercell(basis: np.ndarray, reps: int, a: float):
+    g = np.arange(reps)
+    cells = np.stack(np.meshgrid(g, g, g, indexing="ij"), -1).reshape(-1, 3)
+    frac = (cells[:, None, :] + basis[None, :, :]).reshape(-1, 3)
+    return frac * a, np.eye(3) * (a * reps)
+
+
+def ni3al_l12(reps: int, a: float, sigma: float, seed: int) -> Dict[str, np.ndarray]:
+    """Ni3Al L1_2: Al on the cube corner, Ni on the three face centres."""
+    pos, cell = _supercell(FCC_BASIS, reps, a)
+    types = np.tile(np.array([1, 0, 0, 0], dtype=np.int32), reps ** 3)
+    rng = np.random.default_rng(seed)
+    pos = pos + rng.normal(0.0, sigma, size=pos.shape)
+    return {"cell": cell, "pbc": np.array([1, 1, 1], dtype=np.int32),
+            "positions": np.ascontiguousarray(pos), "types": types}
+
+
+def config1(seed: int = 1) -> Dict[str, np.ndarray]:
+    """256-atom Ni3Al (4x4x4 cubic fcc cells), a=3.52, sigma=0.05."""
+    return ni3al_l12(4, 3.52, 0.05, seed)
+
+
+def config3(seed: int = 3, reps: int = 64) -> Dict[str, np.ndarray]:
+    """1,048,576-atom Ni3Al box (64x64x64 cells), a=3.52, sigma=0.08."""
+    return ni3al_l12(reps, 3.52, 0.08, seed)
+
+
+def _strained(cell: np.ndarray, pos: np.ndarray, rng, amp: float):
+    e = rng.uniform(-amp, amp, size=(3, 3))
+    e = 0.5 * (e + e.T)
+    F = np.eye(3) + e
+    return cell @ F, pos @ F
+
+
+def config2(n_struct: int = 4096, seed: int = 2) -> List[Dict[str, np.ndarray]]:
+    """Random Ni/Al/Cr fcc alloys of 32/108/256 atoms, a=3.55, symmetric
+    strain U(-0.03, 0.03), sigma=0.1."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(n_struct):
+        reps = int(rng.choice([2, 3, 4]))
+        pos, cell = _supercell(FCC_BASIS, reps, 3.55)
+        cell, pos = _strained(cell, pos, rng, 0.03)
+        pos = pos + rng.normal(0.0, 0.1, size=pos.shape)
+        types = rng.integers(0, 3, size=pos.shape[0]).astype(np.int32)
+        out.append({"cell": cell, "pbc": np.array([1, 1, 1], dtype=np.int32),
+                    "positions": np.ascontiguousarray(pos), "types": types})
+    return out
+
+
+def config4_structures(n_struct: int = 8192, seed: int = 4) -> List[Dict[str, np.ndarray]]:
+    """Ni/Al fcc or bcc supercells of 64-216 atoms, random composition,
+    symmetric strain U(-0.03, 0.03), sigma=0.1."""
+    rng = np.random.default_rng(seed)
+    choices = [("fcc", 3, 3.55), ("fcc", 4, 3.55),   # 108, 256 -> 256 exceeds; filtered
+               ("bcc", 4, 2.86), ("bcc", 5, 2.86), ("fcc", 3, 3.52), ("bcc", 4, 2.88)]
+    choices = [c for c in choices if 64 <= (4 if c[0] == "fcc" else 2) * c[1] ** 3 <= 216]
+    out = []
+    for _ in range(n_struct):
+        kind, reps, a = choices[int(rng.integers(0, len(choices)))]
+        basis = FCC_BASIS if kind == "fcc" else BCC_BASIS
+        pos, cell = _supercell(basis, reps, a)
+        cell, pos = _strained(cell, pos, rng, 0.03)
+        pos = pos + rng.normal(0.0, 0.1, size=pos.shape)
+        frac_al = rng.uniform(0.0, 1.0)
+        types = (rng.uniform(size=pos.shape[0]) < frac_al).astype(np.int32)
+        out.append({"cell": cell, "pbc": np.array([1, 1, 1], dtype=np.int32),
+                    "positions": np.ascontiguousarray(pos), "types": types})
+    return out
+
+
+def seeded_coefficients(model: MTPModel, seed: int, low: float = -0.1,
+                        high: float = 0.1) -> MTPModel:
+    """All radial, species and moment coefficients drawn U(low, high)."""
+    rng = np.random.default_rng(seed)
+    c = rng.uniform(low, high, size=model.coeff_count)
+    return model.with_coefficients(c)
+
+
+def with_species(model: MTPModel, species_count: int, rmin: float, rmax: float,
+                 rb_size: int = None) -> MTPModel:
+    """Adapts a coefficient-free template header (species count, radial
+    interval and size) as the benchmark configurations require."""
+    R = rb_size or model.rb_size
+    K = species_count
+    return dataclasses.replace(
+        model, species_count=K, rb_size=R, min_dist=np.array([rmin]), max_dist=np.array([rmax]),
+        radial_basis_split=False, radial_coeffs=np.zeros(K * K * model.radial_func_count * R),
+        species_coeffs=np.zeros(K), moment_coeffs=np.zeros(model.alpha_scalar_moments))
+
+
+def batch(structures: List[Dict[str, np.ndarray]]):
+    """Concatenates structures: returns (atom_offsets, cells[S,9], pbc[S,3],
+    positions[N,3], types[N])."""
+    offs = np.zeros(len(structures) + 1, dtype=np.int32)
+    for i, s in enumerate(structures):
+        offs[i + 1] = offs[i] + s["positions"].shape[0]
+    cells = np.stack([s["cell"].reshape(9) for s in structures]).astype(np.float64)
+    pbc = np.stack([s["pbc"] for s in structures]).astype(np.int32)
+    pos = np.concatenate([s["positions"] for s in structures]).astype(np.float64)
+    types = np.concatenate([s["types"] for s in structures]).astype(np.int32)
+    return offs, np.ascontiguousarray(cells), np.ascontiguousarray(pbc), \
+        np.ascontiguousarray(pos), np.ascontiguousarray(types)

@@ -1,0 +1,258 @@
+/*
+ * mtpb200.h -- C ABI of the B200 MTP energy/force/stress and
+ * coefficient-gradient path.
+ *
+ * Every entry point returns MTPB_OK (0) or a nonzero status; the message of
+ * the last failure on the calling thread is available from
+ * mtpb_last_error().  No entry point throws, aborts or exits.  All pointers
+ * are borrowed for the duration of the call only.  One context belongs to one
+ * CUDA device and must not be used by two threads at once.
+ *
+ * Array pointers carry host memory unless a call takes a `memory` argument
+ * equal to MTPB_MEMORY_DEVICE, in which case every array of that call is
+ * device memory on the context's device.
+ *
+ * Each declaration names the reference interface it replaces (paths relative
+ * to the reference project root).
+ */
+#ifndef MTPB200_H
+#define MTPB200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define MTPB_ABI_VERSION 1
+
+enum mtpb_status {
+    MTPB_OK = 0,
+    MTPB_ERR_ARGUMENT = 1,     /* invalid argument or inconsistent sizes */
+    MTPB_ERR_UNSUPPORTED = 2,  /* model or geometry outside what the kernels implement */
+    MTPB_ERR_CUDA = 3,         /* CUDA runtime error (message holds the CUDA text) */
+    MTPB_ERR_MEMORY = 4,       /* device allocation failed */
+    MTPB_ERR_STATE = 5         /* call order violated (e.g. no neighbour list yet) */
+};
+
+enum mtpb_memory { MTPB_MEMORY_HOST = 0, MTPB_MEMORY_DEVICE = 1 };
+
+typedef struct mtpb_context mtpb_context;
+
+/* Linear MTP with Chebyshev radial bases.  Field meaning follows
+ * MTPGpuPotentialView (runtime/mtp/gpu-direct/mtp_gpu_direct.h:270-325) and the
+ * .mtp layout read by PotMTP::Load (potentials/potential_mtp.cpp:119-576):
+ * radial_coeffs[(ti*K + tj)*mu*R + m*R + xi], alpha_index_basic[i] =
+ * {mu, a, b, c}, alpha_index_times[t] = {l1, l2, coefficient, target}. */
+typedef struct mtpb_model_view {
+    int species_count;
+    int radial_func_count;
+    int rb_size;
+    int radial_basis_split;     /* 0: one basis; 1: one basis per ordered pair */
+    const double *min_dist;     /* [1] or [K*K] */
+    const double *max_dist;     /* [1] or [K*K]; also the pair cutoff */
+    double scaling;
+    int alpha_moments_count;
+    int alpha_index_basic_count;
+    int alpha_index_times_count;
+    int alpha_scalar_moments;
+    const int *alpha_index_basic;     /* [nb][4] */
+    const int *alpha_index_times;     /* [T][4] */
+    const int *alpha_moment_mapping;  /* [S] */
+    const double *radial_coeffs;      /* [K*K*mu*R] */
+    const double *species_coeffs;     /* [K] */
+    const double *moment_coeffs;      /* [S] */
+} mtpb_model_view;
+
+/* A batch of periodic structures (the Atoms + Neighborhoods inputs of
+ * PotMTP::getEFS, potentials/potential_mtp.cpp:1892-1933, and of the CSR batch
+ * built by MTPGpuBatch::build_impl, potentials/mtp_gpu_adapter.cpp:1011-1180). */
+typedef struct mtpb_structures {
+    int n_structures;
+    const int *atom_offsets;   /* [S+1]: atoms of structure s are [off[s], off[s+1]) */
+    const double *cells;       /* [S][9]: row-major, rows are lattice vectors (Atoms::cell_) */
+    const int *pbc;            /* [S][3] periodic flags; NULL means fully periodic */
+    const double *positions;   /* [N][3] Cartesian, Angstrom */
+    const int *types;          /* [N] species index 0..K-1 (Atoms::chemmap_) */
+} mtpb_structures;
+
+/* Outputs of a structure batch; any pointer may be NULL. */
+typedef struct mtpb_efs_output {
+    double *energy;       /* [S] eV */
+    double *forces;       /* [N][3] eV/Angstrom (Atoms::forces_) */
+    double *stress;       /* [S][9] virial in eV, row-major (Atoms::stress_) */
+    double *site_energy;  /* [N] eV (Atoms::site_energies_) */
+} mtpb_efs_output;
+
+/* ---- library and context ------------------------------------------------ */
+
+/* Message of the last failed call on this thread ("" if none). */
+const char *mtpb_last_error(void);
+int mtpb_abi_version(void);
+/* Replaces MTPGpuDirect::available_device_count (mtp_gpu_direct.h:803). */
+int mtpb_device_count(int *count);
+
+/* Replaces MTPGpuDirect::set_device + initialize (mtp_gpu_direct.h:801-813):
+ * selects the device, validates the moment graph, uploads coefficients and
+ * prepares the kernels for the model's basis shape. */
+int mtpb_create(int device, const mtpb_model_view *model, mtpb_context **ctx);
+int mtpb_destroy(mtpb_context *ctx);
+
+/* Replaces MTPGpuDirect::update_coefficients (mtp_gpu_direct.h:814-816).
+ * Host arrays in the native order: radial [K*K*mu*R], species [K], moment [S]. */
+int mtpb_update_coefficients(mtpb_context *ctx, const double *radial, const double *species,
+                             const double *moment);
+
+/* Model cutoff (largest pair max_dist), in Angstrom. */
+int mtpb_cutoff(const mtpb_context *ctx, double *cutoff);
+
+/* Extra neighbour-list radius beyond the cutoff (default 0).  With a skin the
+ * list can be reused while atoms move less than skin/2; pairs beyond the
+ * model cutoff are skipped by the kernels (potential_mtp.cpp:2842). */
+int mtpb_set_skin(mtpb_context *ctx, double skin);
+
+/* ---- structures: neighbour build + EFS ---------------------------------- */
+
+/* Builds the neighbour lists of all structures on the GPU (replaces
+ * Neighborhoods(atoms, cutoff), base/neighborhood.cpp:149-157) and keeps them
+ * in the context.  Per-atom neighbour sets equal the reference builder's bit
+ * for bit (neighbour index and displacement vector). */
+int mtpb_build_neighbors(mtpb_context *ctx, const mtpb_structures *in, int memory);
+
+/* Number of directed edges of the list built last. */
+int mtpb_neighbor_count(const mtpb_context *ctx, long *n_edges);
+
+/* Copies the list built last into host arrays: offsets[N+1], nbr[E]
+ * (structure-local atom index is nbr - atom_offsets[s]; nbr is global),
+ * rij[E][3] (Neighborhood::pos_), shift[E] (packed periodic image, may be NULL). */
+int mtpb_get_neighbors(const mtpb_context *ctx, int *offsets, int *nbr, double *rij, int *shift);
+
+/* Energy, forces, virial (and site energies) of the structures whose
+ * neighbour list was built last; replaces PotMTP::getEFS(Atoms&,
+ * AnyNeighborhoods&) (potential_mtp.cpp:1899-1933).  Positions are taken from
+ * that build.  Outputs are `memory`-side arrays. */
+int mtpb_efs_compute(mtpb_context *ctx, int memory, const mtpb_efs_output *out);
+
+/* Convenience: build + compute in one call (PotMTP::getEFS(Atoms&),
+ * potential_mtp.cpp:1892-1897, batched like calc_efs, apps/calc_efs.cpp:336-380).
+ * reuse_neighbors != 0 keeps the previous list when the batch layout is
+ * unchanged (MTPGpuComputeRequest::reuse_topology). */
+int mtpb_efs_structures(mtpb_context *ctx, const mtpb_structures *in, int memory,
+                        int reuse_neighbors, const mtpb_efs_output *out);
+
+/* ---- caller-supplied neighbour lists ------------------------------------ */
+
+/* CSR request with explicit lists (MTPGpuBatchRequest,
+ * mtp_gpu_direct.h:455-517).  Centres are atoms 0..center_count-1; atoms
+ * center_count..ntotal-1 are ghosts that only appear as neighbours.
+ * neighbor_vectors[E][3] (optional) gives r_ij directly; otherwise
+ * r_ij = x[j] - x[i].  force[ntotal][3] receives (or, with
+ * accumulate_force, adds) -dE/dx; site_virial[ntotal][6] (xx yy zz xy xz yz)
+ * splits each pair term 0.5/0.25 onto both atoms as MLIPCore::compute does
+ * (runtime/mtp/mlip.cpp:1164-1190); global_virial[6] is the sum. */
+typedef struct mtpb_csr_request {
+    int center_count;
+    int ntotal;
+    const int *offsets;           /* [center_count+1] */
+    const int *neighbors;         /* [E] atom indices (masked with neighbor_mask) */
+    int neighbor_mask;            /* e.g. 0x3fffffff for LAMMPS lists; -1 keeps all bits */
+    const double *neighbor_vectors;  /* [E][3] or NULL */
+    const int *types;             /* [ntotal] species index, -1 skips the atom */
+    const double *x;              /* [ntotal][3] */
+    double *force;                /* [ntotal][3] or NULL */
+    int accumulate_force;
+    double *total_energy;         /* [1] or NULL */
+    double *site_energy;          /* [center_count] or NULL */
+    double *site_virial;          /* [ntotal][6] or NULL */
+    double *global_virial;        /* [6] or NULL */
+} mtpb_csr_request;
+
+/* Replaces MTPGpuDirect::compute_batch (mtp_gpu_direct.h:870) for the FP64
+ * linear model. */
+int mtpb_efs_csr(mtpb_context *ctx, const mtpb_csr_request *req, int memory);
+
+/* LAMMPS pair-style request (MTPGpuComputeRequest, mtp_gpu_direct.h:326-450;
+ * PairMLIPGpuDirect::compute, LAMMPS/USER-MLIP/pair_MLIP_gpu_direct.cpp:540-640):
+ * full neighbour list, newton on, forces added to f for local and ghost
+ * atoms.  type[i] is the LAMMPS type; type_map[type] gives the model species
+ * or -1 to skip the atom. */
+typedef struct mtpb_lammps_request {
+    int inum;
+    const int *ilist;               /* [inum] */
+    const int *numneigh;            /* indexed by atom */
+    const int *const *firstneigh;   /* indexed by atom */
+    int neighbor_mask;
+    int ntotal;                     /* local + ghost atoms */
+    const int *type;                /* [ntotal] */
+    const int *type_map;            /* [type_map_count] */
+    int type_map_count;
+    const double *x;                /* [ntotal][3] contiguous */
+    double *f;                      /* [ntotal][3] accumulated */
+    double *energy;                 /* [1] accumulated, or NULL */
+    double *site_energy;            /* [ntotal] or NULL (written for centres) */
+    double *site_virial;            /* [ntotal][6] accumulated, or NULL */
+    double *virial;                 /* [6] accumulated, or NULL */
+} mtpb_lammps_request;
+
+/* Host arrays only. */
+int mtpb_efs_lammps(mtpb_context *ctx, const mtpb_lammps_request *req);
+
+/* ---- training: loss and coefficient gradient ---------------------------- */
+
+/* Trainer_MTP loss settings (train/train_mtp.h:205-216). */
+typedef struct mtpb_loss_weights {
+    double weight_eng, weight_force, weight_stress;
+    double weight_eng_power, weight_force_power, weight_stress_power;
+} mtpb_loss_weights;
+
+/* Labels of a structure batch (Atoms::energy_, forces_, stress_); a NULL
+ * array disables that term for all structures. */
+typedef struct mtpb_labels {
+    const double *energy;   /* [S] */
+    const double *forces;   /* [N][3] */
+    const double *stress;   /* [S][9] virial, eV */
+} mtpb_labels;
+
+/* Loss and gradient of the structures whose neighbour list was built last
+ * (Trainer_MTP::AccumulateGard without the penalty term,
+ * train/train_mtp.cpp:3039-3094 with AddLossGard :3839-3996 and
+ * PotMTP::AccumulateEFSCombinationGard, potential_mtp.cpp:6896-6922).
+ * loss and grad are divided by the number of structures in `norm_count`
+ * (pass the global count when shards are reduced across ranks, or 0 for the
+ * local count).  metrics[7] = {total, energy, force, stress loss, squared
+ * per-atom energy error, squared force error, squared stress error}
+ * (un-normalised).  grad[K*K*mu*R + K + S] in the native order.  Labels and
+ * outputs are `memory`-side arrays. */
+int mtpb_loss_grad(mtpb_context *ctx, const mtpb_labels *labels, const mtpb_loss_weights *w,
+                   int norm_count, int memory, double *loss, double *metrics, double *grad);
+
+/* ---- diagnostics ---------------------------------------------------------- */
+
+/* Device-side timing of the last mtpb_efs_compute/mtpb_efs_structures call,
+ * milliseconds: [0] neighbour build (0 when reused), [1] forward moments,
+ * [2] moment graph, [3] reverse moments, [4] force gather and reductions. */
+int mtpb_last_timings(const mtpb_context *ctx, double *ms5);
+
+/* Kernel launches issued by the last compute call. */
+int mtpb_last_launch_count(const mtpb_context *ctx, int *launches);
+
+/* Basic moments and their energy adjoints of the last EFS call, [N][nb] in
+ * the model's basic ordering (host arrays, either may be NULL). */
+int mtpb_get_site_moments(const mtpb_context *ctx, double *basic, double *adjoint);
+
+/* Per-edge site energy derivatives dE_i/dr_ij of the last EFS call, [E][3]
+ * in neighbour-list order (PotMTP::CalcSiteEFS buff_site_energy_ders). */
+int mtpb_get_edge_derivatives(const mtpb_context *ctx, double *dedr);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MTPB200_H */
