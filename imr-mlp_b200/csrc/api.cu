@@ -94,6 +94,12 @@ static int upload_model(mtpb_context *c)
     for (size_t i = 0; i < c->plan.phase_rows.size(); ++i)
         row0[i + 1] = row0[i] + c->plan.phase_rows[i];
     c->d_phase_row0 = c->arena.get<int>("model_dag_row0", row0.size());
+    if (!c->d_err) {
+        c->d_err = c->arena.get<int>("err_flag", 4);
+        if (!c->d_err)
+            return fail(MTPB_ERR_MEMORY, "device allocation failed");
+        CUDA_TRY(cudaMemsetAsync(c->d_err, 0, sizeof(int), c->stream), "memset");
+    }
     if (!c->d_radial || !c->d_species || !c->d_pairs || !c->d_recs || !c->d_phase_row0)
         return fail(MTPB_ERR_MEMORY, "device allocation for the model failed");
     CUDA_TRY(cudaMemcpyAsync(c->d_radial, m.radial.data(), sizeof(double) * m.radial.size(),
@@ -156,13 +162,25 @@ int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offse
     c->launches++;
     CUDA_TRY(cudaEventRecord(c->ev[2], c->stream), "event");
     CUDA_TRY(launch_dag(c->plan, c->d_recs, c->d_phase_row0, c->nslot, ncenter, c->npad, types,
-                        c->d_species, basic, adjoint, site_energy, c->stream),
+                        c->d_species, basic, adjoint, site_energy, c->d_err, c->stream),
              "moment graph");
     c->launches++;
     CUDA_TRY(cudaEventRecord(c->ev[3], c->stream), "event");
     CUDA_TRY(launch_moments_rev(c->shape, a, adjoint, dx, dy, dz, c->stream), "moments reverse");
     c->launches++;
     CUDA_TRY(cudaEventRecord(c->ev[4], c->stream), "event");
+    return MTPB_OK;
+}
+
+int check_device_error(mtpb_context *c)
+{
+    int flag = 0;
+    CUDA_TRY(cudaMemcpy(&flag, c->d_err, sizeof(int), cudaMemcpyDeviceToHost), "read error flag");
+    if (flag) {
+        CUDA_TRY(cudaMemset(c->d_err, 0, sizeof(int)), "clear error flag");
+        return fail(MTPB_ERR_CUDA, "a device-side wait gave up (record stream did not arrive); "
+                                   "results of this call are invalid");
+    }
     return MTPB_OK;
 }
 
@@ -598,10 +616,13 @@ int mtpb_efs_compute(mtpb_context *c, int memory, const mtpb_efs_output *out)
                                      c->stream),
                      "copy");
     }
-    if (!dev)
+    if (!dev) {
         CUDA_TRY(cudaStreamSynchronize(c->stream), "EFS");
-    else
+        if ((rc = check_device_error(c)))
+            return rc;
+    } else {
         CUDA_TRY(cudaGetLastError(), "EFS");
+    }
     c->have_efs = true;
     return MTPB_OK;
 }
@@ -706,6 +727,44 @@ int mtpb_get_edge_derivatives(const mtpb_context *c, double *dedr)
         dedr[3 * e + 1] = y[e];
         dedr[3 * e + 2] = z[e];
     }
+    return MTPB_OK;
+}
+
+int mtpb_graph_program(const mtpb_model_view *view, int *nslot, int *slot_of_basic, int *nrows,
+                       int *one_row, int *zero_row, int *n_fwd, int *n_rev, int *phase_rows,
+                       long *n_records, unsigned int *records)
+{
+    ModelHost m;
+    std::string err;
+    if (!copy_model(view, m, &err) || !validate_model(m, &err))
+        return fail(MTPB_ERR_ARGUMENT, err);
+    const int shape = select_shape(m, &err);
+    if (shape < 0)
+        return fail(MTPB_ERR_UNSUPPORTED, err);
+    std::vector<int> sob;
+    DagPlan plan;
+    if (!build_slot_map(m, shape, sob, &err) || !build_dag_plan(m, shape, sob, plan, &err))
+        return fail(MTPB_ERR_UNSUPPORTED, err);
+    if (nslot)
+        *nslot = shape_desc(shape).nslot;
+    if (slot_of_basic)
+        std::copy(sob.begin(), sob.end(), slot_of_basic);
+    if (nrows)
+        *nrows = plan.nrows;
+    if (one_row)
+        *one_row = plan.one_row;
+    if (zero_row)
+        *zero_row = plan.zero_row;
+    if (n_fwd)
+        *n_fwd = plan.n_fwd;
+    if (n_rev)
+        *n_rev = plan.n_rev;
+    if (phase_rows)
+        std::copy(plan.phase_rows.begin(), plan.phase_rows.end(), phase_rows);
+    if (n_records)
+        *n_records = (long)plan.recs.size();
+    if (records)
+        std::memcpy(records, plan.recs.data(), sizeof(DagRec) * plan.recs.size());
     return MTPB_OK;
 }
 

@@ -47,6 +47,7 @@ struct mtpb_context {
     mtpb::PairParams *d_pairs = nullptr;
     mtpb::DagRec *d_recs = nullptr;
     int *d_phase_row0 = nullptr;
+    int *d_err = nullptr;   // device error flag (bounded waits that gave up)
     // current batch (structures path)
     int nstruct = 0, natoms = 0, ntotal = 0;
     long nedges = 0;
@@ -72,6 +73,8 @@ struct mtpb_context {
 
 namespace mtpb {
 int set_device(mtpb_context *c);
+// Reads and clears the device error flag (call after a stream sync).
+int check_device_error(mtpb_context *c);
 EdgeArgs edge_args(const mtpb_context *c, int ncenter, const int *types, const int *offsets,
                    const int *nbr, const double *rx, const double *ry, const double *rz);
 int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offsets,

@@ -264,6 +264,8 @@ int csr_compute_impl(mtpb_context *c, const mtpb_csr_request *r, int memory,
         }
     }
     CUDA_TRY(cudaStreamSynchronize(s), "CSR EFS");
+    if ((rc = check_device_error(c)))
+        return rc;
     if (r->force && NT && r->accumulate_force) {
         if (dev)
             return fail(MTPB_ERR_ARGUMENT, "accumulate_force needs host memory");

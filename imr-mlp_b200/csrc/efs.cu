@@ -540,104 +540,187 @@ cudaError_t launch_group_maxdeg(int natoms, const int *offsets, int *group_maxde
 // Moment graph: forward product rules, site energy, reverse adjoints.
 // One block = 16 atoms; each half-warp runs one record stream of the plan.
 // Shared memory holds one row of 16 doubles per graph value (basic moments,
-// product moments that feed later rules, their adjoints, and constants).
+// product moments that feed later rules, their adjoints, 1 and 0).  Record
+// rows (16 B per stream) are streamed into a double-buffered shared ring by
+// TMA bulk copies completing on an mbarrier.
 //
-// Forward record:  acc = START ? 0 : acc;  acc += (c * row[s1]) * row[s2];
-//                  END: row[out] = acc (out >= 0), E += e * acc.
-// Reverse record:  acc = START ? e : acc;  acc += (c * row[s1]) * row[s2];
-//                  END: GLOBAL ? adjoint[out] = acc : row[out] = acc.
+// Record semantics (one record = one product rule, use, or marker):
+//   acc = (c * row[s1]) * row[s2] + (START ? 0 : acc)
+//   END:    GLOBAL ? adjoint[out][atom] = acc : row[out] = acc
+//   ENERGY: E += c * acc          (its own product is 0 * 0)
 // ----------------------------------------------------------------------------
-__global__ void __launch_bounds__(DAG_WARPS * 32)
+__device__ __forceinline__ unsigned smem_u32(const void *p)
+{
+    return (unsigned)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(unsigned long long *bar, unsigned count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, unsigned bytes,
+                                          unsigned long long *bar)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], "
+                 "%2, [%3];" ::"r"(smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long *bar, unsigned parity)
+{
+    unsigned ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+                 " selp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(ok)
+                 : "r"(smem_u32(bar)), "r"(parity)
+                 : "memory");
+    return ok != 0;
+}
+
+constexpr int DAG_MAX_PHASES = 64;
+constexpr long DAG_WAIT_LIMIT = 1L << 22;   // bounded wait: sets the error flag
+
+__global__ void __launch_bounds__(DAG_WARPS * 32, 1)
     k_dag(const DagRec *__restrict__ recs, const int *__restrict__ phase_row0, int n_fwd,
-          int n_rev, int nrows, int one_row, int zero_row, int nslot, int natoms, int npad,
+          int n_rev, int one_row, int zero_row, int nslot, int natoms, int npad,
           const int *__restrict__ types, const double *__restrict__ species_coeffs,
           const double *__restrict__ basic, double *__restrict__ adjoint,
-          double *__restrict__ site_energy)
+          double *__restrict__ site_energy, int *__restrict__ err_flag)
 {
-    extern __shared__ double rows[];   // [nrows][16]
+    extern __shared__ __align__(128) unsigned char dsm[];
+    DagRec *ring = reinterpret_cast<DagRec *>(dsm);   // [2][CH][STREAMS]
+    double *rows = reinterpret_cast<double *>(dsm + 2 * DAG_CHUNK_ROWS * DAG_STREAMS *
+                                                        sizeof(DagRec));   // [nrows][16]
+    __shared__ unsigned long long bar[2];
     __shared__ double epart[DAG_STREAMS][DAG_ATOMS];
-    const int atom0 = blockIdx.x * DAG_ATOMS;
-    // load basic moments (kernel slot s -> row s)
-    for (int i = threadIdx.x; i < nslot * DAG_ATOMS; i += blockDim.x) {
-        const int s = i / DAG_ATOMS, a = i - s * DAG_ATOMS;
-        const int atom = atom0 + a;
-        rows[i] = atom < natoms ? basic[(size_t)s * npad + atom] : 0.0;
-    }
-    if (threadIdx.x < DAG_ATOMS) {
-        rows[one_row * DAG_ATOMS + threadIdx.x] = 1.0;
-        rows[zero_row * DAG_ATOMS + threadIdx.x] = 0.0;
+    __shared__ int ph0[DAG_MAX_PHASES + 1];
+    const int tid = threadIdx.x;
+    const int nph = n_fwd + n_rev;
+    for (int i = tid; i <= nph; i += blockDim.x)
+        ph0[i] = phase_row0[i];
+    const int total_rows = phase_row0[nph];
+    const int nchunks = (total_rows + DAG_CHUNK_ROWS - 1) / DAG_CHUNK_ROWS;
+    constexpr unsigned CHUNK_BYTES = DAG_CHUNK_ROWS * DAG_STREAMS * sizeof(DagRec);
+    auto chunk_bytes = [&](int k) -> unsigned {
+        const int r = min(DAG_CHUNK_ROWS, total_rows - k * DAG_CHUNK_ROWS);
+        return (unsigned)(r * DAG_STREAMS * sizeof(DagRec));
+    };
+    if (tid == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (tid == 0)
+        for (int k = 0; k < 2 && k < nchunks; ++k)
+            bulk_load(ring + k * DAG_CHUNK_ROWS * DAG_STREAMS,
+                      recs + (size_t)k * DAG_CHUNK_ROWS * DAG_STREAMS, chunk_bytes(k), &bar[k]);
+    const int atom0 = blockIdx.x * DAG_ATOMS;
+    for (int i = tid; i < nslot * DAG_ATOMS; i += blockDim.x) {
+        const int sl = i / DAG_ATOMS, a = i - sl * DAG_ATOMS;
+        const int atom = atom0 + a;
+        rows[i] = atom < natoms ? basic[(size_t)sl * npad + atom] : 0.0;
+    }
+    if (tid < DAG_ATOMS) {
+        rows[one_row * DAG_ATOMS + tid] = 1.0;
+        rows[zero_row * DAG_ATOMS + tid] = 0.0;
+    }
+    __syncthreads();
+    const int warp = tid >> 5, lane = tid & 31;
     const int stream = warp * 2 + (lane >> 4);
     const int al = lane & 15;
+    const int atom = atom0 + al;
     double E = 0.0, acc = 0.0;
-    for (int ph = 0; ph < n_fwd; ++ph) {
-        const int r0 = phase_row0[ph], r1 = phase_row0[ph + 1];
-        for (int r = r0; r < r1; ++r) {
-            const DagRec rec = recs[(size_t)r * DAG_STREAMS + stream];
-            if (rec.flags & DAG_START)
-                acc = 0.0;
-            acc = fma(rec.c * rows[rec.s1 * DAG_ATOMS + al], rows[rec.s2 * DAG_ATOMS + al], acc);
-            if (rec.flags & DAG_END) {
-                if (rec.out >= 0)
-                    rows[rec.out * DAG_ATOMS + al] = acc;
-                E = fma(rec.e, acc, E);
+    int ph = 0;
+    auto advance_phase = [&]() {
+        __syncthreads();
+        ++ph;
+        if (ph == n_fwd) {
+            epart[stream][al] = E;
+            __syncthreads();
+            if (tid < DAG_ATOMS && atom0 + tid < natoms) {
+                const int t = types[atom0 + tid];
+                double se = 0.0;
+                if (t >= 0) {
+                    se = species_coeffs[t];
+                    for (int q = 0; q < DAG_STREAMS; ++q)
+                        se += epart[q][tid];
+                }
+                site_energy[atom0 + tid] = se;
             }
         }
-        __syncthreads();
-    }
-    epart[stream][al] = E;
-    __syncthreads();
-    if (threadIdx.x < DAG_ATOMS) {
-        const int atom = atom0 + threadIdx.x;
-        if (atom < natoms) {
-            const int t = types[atom];
-            double se = t >= 0 ? species_coeffs[t] : 0.0;
-            if (t >= 0)
-                for (int s = 0; s < DAG_STREAMS; ++s)
-                    se += epart[s][threadIdx.x];
-            site_energy[atom] = se;
+    };
+    for (int k = 0; k < nchunks; ++k) {
+        const int b = k & 1;
+        long it = 0;
+        while (!mbar_try_wait(&bar[b], (unsigned)((k >> 1) & 1))) {
+            if (++it > DAG_WAIT_LIMIT) {
+                *err_flag = 1;
+                break;
+            }
         }
-    }
-    const int atom = atom0 + al;
-    for (int ph = n_fwd; ph < n_fwd + n_rev; ++ph) {
-        const int r0 = phase_row0[ph], r1 = phase_row0[ph + 1];
+        const DagRec *cb = ring + b * DAG_CHUNK_ROWS * DAG_STREAMS;
+        const int r0 = k * DAG_CHUNK_ROWS;
+        const int r1 = min(total_rows, r0 + DAG_CHUNK_ROWS);
         for (int r = r0; r < r1; ++r) {
-            const DagRec rec = recs[(size_t)r * DAG_STREAMS + stream];
-            if (rec.flags & DAG_START)
-                acc = rec.e;
-            acc = fma(rec.c * rows[rec.s1 * DAG_ATOMS + al], rows[rec.s2 * DAG_ATOMS + al], acc);
-            if (rec.flags & DAG_END) {
-                if (rec.flags & DAG_GLOBAL) {
+            while (ph < nph && r == ph0[ph + 1])
+                advance_phase();
+            const uint4 w = *reinterpret_cast<const uint4 *>(cb + (r - r0) * DAG_STREAMS + stream);
+            const double c = __hiloint2double((int)w.w, (int)w.z);
+            const unsigned s1 = w.x & 0xffffu, s2 = w.x >> 16;
+            const unsigned out = w.y & 0xffffu, f = w.y >> 16;
+            const double p = c * rows[s1 * DAG_ATOMS + al];
+            acc = fma(p, rows[s2 * DAG_ATOMS + al], (f & DAG_START) ? 0.0 : acc);
+            if (f & DAG_END) {
+                if (f & DAG_GLOBAL) {
                     if (atom < natoms)
-                        adjoint[(size_t)rec.out * npad + atom] = acc;
-                } else if (rec.out >= 0) {
-                    rows[rec.out * DAG_ATOMS + al] = acc;
+                        adjoint[(size_t)out * npad + atom] = acc;
+                } else {
+                    rows[out * DAG_ATOMS + al] = acc;
                 }
             }
+            if (f & DAG_ENERGY)
+                E = fma(c, acc, E);
         }
         __syncthreads();
+        if (tid == 0 && k + 2 < nchunks) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            bulk_load(ring + b * DAG_CHUNK_ROWS * DAG_STREAMS,
+                      recs + (size_t)(k + 2) * DAG_CHUNK_ROWS * DAG_STREAMS, chunk_bytes(k + 2),
+                      &bar[b]);
+        }
     }
+    while (ph < nph)
+        advance_phase();
+    (void)CHUNK_BYTES;
 }
 
 cudaError_t launch_dag(const DagPlan &plan, const DagRec *recs, const int *phase_row0, int nslot,
                        int natoms, int npad, const int *types, const double *species_coeffs,
-                       const double *basic, double *adjoint, double *site_energy,
+                       const double *basic, double *adjoint, double *site_energy, int *err_flag,
                        cudaStream_t s)
 {
     const int blocks = (natoms + DAG_ATOMS - 1) / DAG_ATOMS;
     if (blocks == 0)
         return cudaSuccess;
-    const size_t smem = sizeof(double) * (size_t)plan.nrows * DAG_ATOMS;
+    if (plan.n_fwd + plan.n_rev > DAG_MAX_PHASES)
+        return cudaErrorInvalidValue;
+    const size_t smem = 2 * DAG_CHUNK_ROWS * DAG_STREAMS * sizeof(DagRec) +
+                        sizeof(double) * (size_t)plan.nrows * DAG_ATOMS;
     cudaError_t err = cudaFuncSetAttribute(k_dag, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)smem);
     if (err != cudaSuccess)
         return err;
     k_dag<<<blocks, DAG_WARPS * 32, smem, s>>>(recs, phase_row0, plan.n_fwd, plan.n_rev,
-                                               plan.nrows, plan.one_row, plan.zero_row, nslot,
-                                               natoms, npad, types, species_coeffs, basic,
-                                               adjoint, site_energy);
+                                               plan.one_row, plan.zero_row, nslot, natoms, npad,
+                                               types, species_coeffs, basic, adjoint, site_energy,
+                                               err_flag);
     return cudaGetLastError();
 }
 

@@ -38,20 +38,32 @@ struct PairParams {
     double pu, su, mult, rmax;
 };
 
-// Record of the moment-graph program (see dag.cu for the semantics).
-struct DagRec {
-    int s1, s2, out, flags;
-    double c, e;
+// Record of the moment-graph program (see k_dag in efs.cu): 16 bytes,
+// {s1 | s2 << 16, out | flags << 16, c (double)}.
+struct alignas(16) DagRec {
+    unsigned int s12;
+    unsigned int outf;
+    double c;
 };
-enum DagFlags : int {
-    DAG_START = 1,   // first record of an item
-    DAG_END = 2,     // last record of an item: store / accumulate
-    DAG_GLOBAL = 4,  // reverse: out is a kernel slot of the global adjoint array
+enum DagFlags : unsigned {
+    DAG_START = 1,   // acc restarts from this record's product
+    DAG_END = 2,     // store acc to row `out` (or the global adjoint slot)
+    DAG_GLOBAL = 4,  // reverse: `out` is a kernel slot of the global adjoint array
+    DAG_ENERGY = 8,  // forward: E += c * acc (the product of this record is zero)
 };
+inline DagRec make_rec(int s1, int s2, int out, unsigned flags, double c)
+{
+    DagRec r;
+    r.s12 = (unsigned)s1 | ((unsigned)s2 << 16);
+    r.outf = (unsigned)(out < 0 ? 0 : out) | (flags << 16);
+    r.c = c;
+    return r;
+}
 
 constexpr int DAG_ATOMS = 16;        // atoms per DAG block (half-warp)
-constexpr int DAG_WARPS = 8;         // warps per DAG block
+constexpr int DAG_WARPS = 16;        // warps per DAG block
 constexpr int DAG_STREAMS = 2 * DAG_WARPS;
+constexpr int DAG_CHUNK_ROWS = 32;   // record rows per shared-memory chunk
 
 struct DagPlan {
     int nrows = 0;           // shared-memory rows (one double per atom each)
@@ -84,7 +96,7 @@ cudaError_t launch_moments_rev(int shape, const EdgeArgs &a, const double *adjoi
 cudaError_t launch_dag(const DagPlan &plan, const DagRec *recs, const int *phase_row0,
                        int nslot, int natoms, int npad, const int *types,
                        const double *species_coeffs, const double *basic, double *adjoint,
-                       double *site_energy, cudaStream_t s);
+                       double *site_energy, int *err_flag, cudaStream_t s);
 cudaError_t launch_group_maxdeg(int natoms, const int *offsets, int *group_maxdeg,
                                 cudaStream_t s);
 cudaError_t launch_force_gather(int natoms, int ntotal, const int *offsets, const int *in_offsets,

@@ -153,7 +153,7 @@ void emit_phase(std::vector<Item> &items, DagPlan &plan)
         load[s] += items[idx].recs.size();
     }
     size_t len = *std::max_element(load.begin(), load.end());
-    DagRec pad{plan.zero_row, plan.zero_row, -1, 0, 0.0, 0.0};
+    const DagRec pad = make_rec(plan.zero_row, plan.zero_row, 0, 0, 0.0);
     for (size_t r = 0; r < len; ++r)
         for (int s = 0; s < DAG_STREAMS; ++s)
             plan.recs.push_back(r < streams[s].size() ? streams[s][r] : pad);
@@ -206,7 +206,7 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
     plan.one_row = next++;
     plan.zero_row = next++;
     plan.nrows = next;
-    if ((size_t)plan.nrows * DAG_ATOMS * sizeof(double) > 220 * 1024) {
+    if ((size_t)plan.nrows * DAG_ATOMS * sizeof(double) > 190 * 1024 || plan.nrows > 65535) {
         if (err)
             *err = "moment graph too large for the shared-memory plan (" +
                    std::to_string(plan.nrows) + " rows)";
@@ -225,7 +225,8 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
             for (int x = 0; x < nb; ++x)
                 if (is_scalar[x]) {
                     Item it;
-                    it.recs.push_back({row[x], plan.one_row, -1, DAG_START | DAG_END, 1.0, scal[x]});
+                    it.recs.push_back(make_rec(row[x], plan.one_row, 0, DAG_START, 1.0));
+                    it.recs.push_back(make_rec(plan.zero_row, plan.zero_row, 0, DAG_ENERGY, scal[x]));
                     items.push_back(std::move(it));
                 }
         }
@@ -238,16 +239,18 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
             const auto &rl = rules_of[x];
             for (size_t k = 0; k < rl.size(); ++k) {
                 const int *r = &m.times[4 * rl[k]];
-                DagRec rec{row[r[0]], row[r[1]], -1, 0, (double)r[2], 0.0};
+                unsigned flags = 0;
+                int out = 0;
                 if (k == 0)
-                    rec.flags |= DAG_START;
-                if (k + 1 == rl.size()) {
-                    rec.flags |= DAG_END;
-                    rec.out = is_operand[x] ? row[x] : -1;
-                    rec.e = scal[x];
+                    flags |= DAG_START;
+                if (k + 1 == rl.size() && is_operand[x]) {
+                    flags |= DAG_END;
+                    out = row[x];
                 }
-                it.recs.push_back(rec);
+                it.recs.push_back(make_rec(row[r[0]], row[r[1]], out, flags, (double)r[2]));
             }
+            if (is_scalar[x])
+                it.recs.push_back(make_rec(plan.zero_row, plan.zero_row, 0, DAG_ENERGY, scal[x]));
             items.push_back(std::move(it));
         }
         emit_phase(items, plan);
@@ -266,20 +269,21 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
         uses[r[0]].push_back({r[3], r[1], (double)r[2]});
         uses[r[1]].push_back({r[3], r[0], (double)r[2]});
     }
-    auto make_item = [&](int x, int out, int flags) {
+    auto make_item = [&](int x, int out, unsigned flags) {
         Item it;
+        if (scal[x] != 0.0)   // acc starts at the scalar coefficient of x
+            it.recs.push_back(make_rec(plan.one_row, plan.one_row, 0, 0, scal[x]));
         for (const Use &u : uses[x]) {
             if (adjrow[u.target] >= 0)
-                it.recs.push_back({adjrow[u.target], row[u.other], -1, 0, u.c, 0.0});
+                it.recs.push_back(make_rec(adjrow[u.target], row[u.other], 0, 0, u.c));
             else if (is_scalar[u.target])
-                it.recs.push_back({plan.one_row, row[u.other], -1, 0, u.c * scal[u.target], 0.0});
+                it.recs.push_back(make_rec(plan.one_row, row[u.other], 0, 0, u.c * scal[u.target]));
         }
         if (it.recs.empty())
-            it.recs.push_back({plan.zero_row, plan.zero_row, -1, 0, 0.0, 0.0});
-        it.recs.front().flags |= DAG_START;
-        it.recs.front().e = scal[x];
-        it.recs.back().flags |= DAG_END | flags;
-        it.recs.back().out = out;
+            it.recs.push_back(make_rec(plan.zero_row, plan.zero_row, 0, 0, 0.0));
+        it.recs.front().outf |= (unsigned)DAG_START << 16;
+        const unsigned old = it.recs.back().outf >> 16;
+        it.recs.back().outf = (unsigned)out | ((old | DAG_END | flags) << 16);
         return it;
     };
     int nrev = 0;
@@ -301,8 +305,8 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
         for (int s = 0; s < nslot; ++s)
             if (!slot_used[s]) {
                 Item it;
-                it.recs.push_back({plan.zero_row, plan.zero_row, s,
-                                   DAG_START | DAG_END | DAG_GLOBAL, 0.0, 0.0});
+                it.recs.push_back(make_rec(plan.zero_row, plan.zero_row, s,
+                                           DAG_START | DAG_END | DAG_GLOBAL, 0.0));
                 items.push_back(std::move(it));
             }
         emit_phase(items, plan);

@@ -96,6 +96,8 @@ SIGNATURES = [
     ("mtpb_last_launch_count", C.c_int, [C.c_void_p, _ip]),
     ("mtpb_get_site_moments", C.c_int, [C.c_void_p, _dp, _dp]),
     ("mtpb_get_edge_derivatives", C.c_int, [C.c_void_p, _dp]),
+    ("mtpb_graph_program", C.c_int, [C.POINTER(ModelView), _ip, _ip, _ip, _ip, _ip, _ip, _ip, _ip,
+                                     C.POINTER(C.c_long), C.POINTER(C.c_uint)]),
 ]
 
 

@@ -244,6 +244,17 @@ int mtpb_last_launch_count(const mtpb_context *ctx, int *launches);
  * the model's basic ordering (host arrays, either may be NULL). */
 int mtpb_get_site_moments(const mtpb_context *ctx, double *basic, double *adjoint);
 
+/* Host-only inspection of the moment-graph program that the device executes
+ * for a model (no device needed).  Outputs (each may be NULL): nslot = basic
+ * moment slots of the selected kernel shape; slot_of_basic[nb]; nrows = graph
+ * rows; one_row / zero_row; n_fwd / n_rev phase counts; phase_rows[n_fwd+n_rev];
+ * n_records; records[n_records][4] as 32-bit words {s1 | s2 << 16,
+ * out | flags << 16, low and high words of the coefficient}.  Call with
+ * records == NULL first to size the buffer. */
+int mtpb_graph_program(const mtpb_model_view *model, int *nslot, int *slot_of_basic, int *nrows,
+                       int *one_row, int *zero_row, int *n_fwd, int *n_rev, int *phase_rows,
+                       long *n_records, unsigned int *records);
+
 /* Per-edge site energy derivatives dE_i/dr_ij of the last EFS call, [E][3]
  * in neighbour-list order (PotMTP::CalcSiteEFS buff_site_energy_ders). */
 int mtpb_get_edge_derivatives(const mtpb_context *ctx, double *dedr);
