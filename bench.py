@@ -1,0 +1,431 @@
+"""Benchmark of the MTP energy/force/stress path (BASELINE.json metric
+"MTP EFS atoms/sec (1M-atom, level 20)").
+
+Workload (configs[2] of BASELINE.json): 1,048,576-atom Ni3Al L1_2 box (64^3
+fcc cells, a = 3.52 A, Gaussian sigma 0.08 A, seed 3), level-20 MTP
+(Shapeev level-20 graph, 2 species, R = 8, r_cut = 5 A, seeded U(-0.1, 0.1)
+coefficients), repeated EFS steps with a GPU neighbour-list rebuild every 10
+steps (steps between rebuilds upload positions and refresh the edge vectors
+from the stored periodic images).  Synthetic seeded data; the working set
+(~6 GB) is far larger than the 126 MB L2, so no L2 flush is needed.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+Multi-GPU: launched by torch.distributed.run, one rank per GPU; every rank
+evaluates its own copy of the box (independent replicas, weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "imr-mlp_b200"))
+MODEL = os.path.join(ROOT, "tests", "golden", "models", "l20_k2.mtp")
+METRIC = "MTP EFS atoms/sec (1M-atom, level 20)"
+UNIT = "atoms/s"
+REBUILD_EVERY = 10
+
+# DRAM traffic per atom of the dominant kernel, from the ncu capture
+# summarised in profiles/ (scaled from the 131k-atom capture by atom count).
+NCU_TRAFFIC_BYTES_PER_ATOM = {"k_moments_rev": None}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--reps", type=int, default=64, help="fcc cells per box edge")
+    ap.add_argument("--ref-reps", type=int, default=10,
+                    help="box edge (cells) of the bounded CPU sample")
+    return ap.parse_args()
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def fp64_peak_tflops(torch, device) -> float:
+    """Measured FP64 throughput of cuBLAS DGEMM (torch.matmul, float64,
+    8192^3), best of 5: the FP64 peak denominator."""
+    n = 8192
+    a = torch.randn(n, n, dtype=torch.float64, device=device)
+    b = torch.randn(n, n, dtype=torch.float64, device=device)
+    for _ in range(2):
+        torch.matmul(a, b)
+    torch.cuda.synchronize()
+    best = 1e30
+    for _ in range(5):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        torch.matmul(a, b)
+        e.record()
+        torch.cuda.synchronize()
+        best = min(best, s.elapsed_time(e) / 1e3)
+    del a, b
+    torch.cuda.empty_cache()
+    return 2.0 * n ** 3 / best / 1e12
+
+
+# ---------------------------------------------------------------------------
+# Algorithmic FLOPs (FMA = 2, add/mul/div/sqrt = 1) of the factorised
+# formulation the kernels execute, counted per valid edge and per atom from
+# the model's basis shape.  Numbers per kernel:
+#   fwd  staging (distance, Chebyshev recurrence, f_mu) + chains (monomial
+#        products and one FMA per basic moment)
+#   rev  staging (+ f'_mu) + chains (P, P', Horner value/derivative, chain
+#        epilogue) + per-edge force assembly
+#   dag  three FLOPs per real record (product and accumulate)
+# and the reference-formulation count of the survey (per atom
+#   n_e (64 + 4 mu R + 4 nu_max + 1 + 38 nb + 24) + 11 T + 2 S + 1).
+# ---------------------------------------------------------------------------
+def shape_chains(numax):
+    NU = max(numax)
+
+    def cnt(nu):
+        return sum(1 for v in numax if v >= nu)
+
+    chains = []
+    for s in range(NU + 1):
+        for b in range(s, -1, -1):
+            c = s - b
+            L = NU - s + 1
+            chains.append((b, c, L, [cnt(a + s) for a in range(L)]))
+    return chains
+
+
+def flop_model(model, nmu_used, edges_per_atom, dag_records):
+    numax = model.basis_shape()
+    numax = [v for v in numax if v >= 0]
+    R = model.rb_size
+    chains = shape_chains(numax)
+    stage_f = 25 + 8 * max(R - 2, 0) + 2 * R * nmu_used
+    stage_r = stage_f + 2 * R * nmu_used
+    fwd = 0
+    rev = 0
+    for b, c, L, cnts in chains:
+        base = 1 if (b and c) else 0
+        fwd += base + (L - 1) + 2 * sum(cnts)
+        rev += base + sum(2 * (2 * k - 1) for k in cnts) + 6 * (L - 1) + 4
+        rev += (3 if b else 0) + (3 if c else 0) + 5
+    fwd += 16                  # y, z power tables
+    rev += 16 + 11             # power tables, force assembly
+    per_edge_fwd = stage_f + fwd
+    per_edge_rev = stage_r + rev
+    nb = model.alpha_index_basic_count
+    T = model.alpha_index_times_count
+    S = model.alpha_scalar_moments
+    mu = model.radial_func_count
+    ref = edges_per_atom * (16 + 8 * (R - 2) + 4 * mu * R + 4 * max(numax) + 1 + 38 * nb + 24) \
+        + 11 * T + 2 * S + 1
+    return {"fwd_per_atom": per_edge_fwd * edges_per_atom,
+            "rev_per_atom": per_edge_rev * edges_per_atom,
+            "dag_per_atom": 3.0 * dag_records,
+            "ref_formulation_per_atom": ref}
+
+
+def dag_record_count(model):
+    """Real (non-padding) records of the graph program (host-only query)."""
+    import ctypes as C
+    import mtpb200
+    from mtpb200 import _ModelKeep
+    lib = mtpb200.library()
+    keep = _ModelKeep(model)
+    n = C.c_long()
+    if lib.mtpb_graph_program(C.byref(keep.view), None, None, None, None, None, None, None,
+                              None, C.byref(n), None):
+        return 0
+    recs = np.zeros((n.value, 4), np.uint32)
+    lib.mtpb_graph_program(C.byref(keep.view), None, None, None, None, None, None, None, None,
+                           None, recs.ctypes.data_as(C.POINTER(C.c_uint)))
+    pad = (recs[:, 2] == 0) & (recs[:, 3] == 0) & ((recs[:, 1] >> 16) == 0)
+    return int((~pad).sum())
+
+
+def cpu_reference_sample(model, reps, steps, warmup, threads):
+    """Reference CPU path (compiled reference Neighborhoods + MLIPCore::compute
+    over OpenMP) on a bounded periodic sample of the same box; atoms/s with a
+    neighbour rebuild every REBUILD_EVERY steps (the build time amortised)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import ReferenceEFS  # test infrastructure: baseline leg only
+    from mtpb200 import configs, format_mtp
+    st = configs.config3(reps=reps)
+    ref = ReferenceEFS(format_mtp(model), model.species_count, threads=threads)
+    t0 = time.perf_counter()
+    prob = ref.build(st["cell"], st["pbc"], st["positions"], st["types"])
+    t_build = time.perf_counter() - t0
+    for _ in range(warmup):
+        ref.compute(prob)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        ref.compute(prob)
+        times.append(time.perf_counter() - t0)
+    ref.close()
+    t_step = statistics.median(times) + t_build / REBUILD_EVERY
+    n = len(st["types"])
+    return {"value": n / t_step, "unit": UNIT, "cores": threads, "kind": "reference",
+            "sample": f"{n}-atom Ni3Al box ({reps}^3 fcc cells, sigma 0.08), level 20; "
+                      f"median of {steps} EFS evaluations after {warmup} warm-up, plus 1/"
+                      f"{REBUILD_EVERY} of one neighbour build ({t_build * 1e3:.1f} ms); "
+                      "MPI unavailable, OpenMP only",
+            "ms_per_step": t_step * 1e3}
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from mtpb200 import MTPGpuDirect, StructureBatch, configs, read_mtp
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    model = read_mtp(MODEL)
+    st = configs.config3(reps=args.reps)
+    batch = StructureBatch.from_structures([st])
+    N = batch.n_atoms
+    gpu = MTPGpuDirect(model, local)
+    # a dedicated stream shared by the library and the timing events
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    gpu.set_stream(stream.cuda_stream)
+
+    # device-resident inputs and outputs
+    offs_d = torch.from_numpy(batch.atom_offsets).to(dev)
+    cells_d = torch.from_numpy(batch.cells).to(dev)
+    pbc_d = torch.ones((1, 3), dtype=torch.int32, device=dev)
+    pos_d = torch.from_numpy(batch.positions).to(dev)
+    types_d = torch.from_numpy(batch.types).to(dev)
+    energy_d = torch.zeros(1, dtype=torch.float64, device=dev)
+    forces_d = torch.zeros((N, 3), dtype=torch.float64, device=dev)
+    stress_d = torch.zeros((1, 9), dtype=torch.float64, device=dev)
+
+    def step(k):
+        gpu.efs_device(offs_d, cells_d, pbc_d, pos_d, types_d, energy_d, forces_d, stress_d,
+                       reuse_neighbors=(k % REBUILD_EVERY) != 0)
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if ws == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for k in range(args.warmup):
+        step(k)
+    torch.cuda.synchronize()
+    edges = gpu.neighbor_count()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    kernel_ms = np.zeros(5)
+    t0.record(stream)
+    for k in range(args.steps):
+        step(k)
+        launches += gpu.last_launch_count()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    ms = max_over_ranks(t0.elapsed_time(t1))
+    # per-kernel device time of a reuse step and of a rebuild step (events
+    # recorded by the library on the same stream)
+    step(1)
+    torch.cuda.synchronize()
+    kernel_ms = gpu.last_timings()
+    step(0)
+    torch.cuda.synchronize()
+    build_ms = gpu.last_timings()[0]
+    energy = float(energy_d.item())
+
+    # end-to-end through the public host API: pinned host buffers, H2D of the
+    # positions every step (types and cell too on rebuild steps), D2H of the
+    # energy, forces and virial every step
+    pos_h = torch.from_numpy(batch.positions).pin_memory()
+    types_h = torch.from_numpy(batch.types).pin_memory()
+    hb = StructureBatch(batch.atom_offsets, batch.cells, None, pos_h.numpy(), types_h.numpy())
+    out = {"energy": torch.zeros(1, dtype=torch.float64).pin_memory().numpy(),
+           "forces": torch.zeros((N, 3), dtype=torch.float64).pin_memory().numpy(),
+           "stress": torch.zeros((1, 9), dtype=torch.float64).pin_memory().numpy()}
+    for k in range(args.warmup):
+        gpu.efs_structures(hb, reuse_neighbors=(k % REBUILD_EVERY) != 0, out=out)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(args.steps):
+        gpu.efs_structures(hb, reuse_neighbors=(k % REBUILD_EVERY) != 0, out=out)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    n_rebuild = sum(1 for k in range(args.steps) if k % REBUILD_EVERY == 0)
+    h2d = (N * 24 * args.steps + n_rebuild * (N * 4 + 9 * 8 + 8)) / args.steps
+    d2h = N * 24 + 8 + 72
+    e2e_ok = abs(float(out["energy"][0]) - energy) <= 1e-9 * max(1.0, abs(energy))
+
+    peak = fp64_peak_tflops(torch, dev) if rank == 0 else None
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    # roofline of the dominant kernel (FP64 CUDA-core bound)
+    recs = dag_record_count(model)
+    fm = flop_model(model, len([v for v in model.basis_shape() if v >= 0]), edges / N, recs)
+    names = {1: ("k_moments<fwd>", fm["fwd_per_atom"]), 2: ("k_dag", fm["dag_per_atom"]),
+             3: ("k_moments<rev>", fm["rev_per_atom"])}
+    dom = max(names, key=lambda i: kernel_ms[i])
+    kname, kflops = names[dom]
+    achieved = kflops * N / (kernel_ms[dom] / 1e3) / 1e12
+    total_atoms = N * ws * args.steps
+    value = total_atoms / (ms / 1e3)
+    step_ms = float(kernel_ms[1:].sum())
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (seeded Ni3Al L1_2 box, seeded level-20 coefficients)",
+        "config": {"workload": f"config 3: {N}-atom Ni3Al box, level-20 MTP, EFS steps with a "
+                               f"neighbour rebuild every {REBUILD_EVERY} steps",
+                   "atoms_per_gpu": N, "edges_per_gpu": edges, "level": 20, "species": 2,
+                   "rb_size": 8, "r_cut": 5.0, "skin": 0.0,
+                   "parallelism": f"replicas{ws}" if ws > 1 else "single",
+                   "l2": "working set ~6 GB per GPU, larger than L2 (no flush)"},
+        "e2e": {"value": N * ws * args.steps / (e2e_ms / 1e3), "unit": UNIT,
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                "matches_device_energy": e2e_ok},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "fp64", "kernel": kname, "achieved": achieved, "peak": peak,
+                     "unit": "TFLOP/s", "frac": achieved / peak if peak else None,
+                     "traffic": None,
+                     "peak_source": "measured by bench.py: cuBLAS DGEMM 8192^3 (torch.matmul "
+                                    "float64); MEASURED_PEAKS.json has no FP64 figure",
+                     "flops_per_atom": kflops},
+        "kernel_ms": {"refresh": float(kernel_ms[0]), "neighbor_build": float(build_ms),
+                      "moments_fwd": float(kernel_ms[1]), "graph": float(kernel_ms[2]),
+                      "moments_rev": float(kernel_ms[3]), "gather_reduce": float(kernel_ms[4])},
+        "step_tflops_executed": (fm["fwd_per_atom"] + fm["rev_per_atom"] + fm["dag_per_atom"])
+        * N / (step_ms / 1e3) / 1e12,
+        "step_tflops_ref_formulation": fm["ref_formulation_per_atom"] * N / (step_ms / 1e3) / 1e12,
+        "clocks": clocks,
+        "energy_eV": energy,
+    }
+    try:
+        threads = os.cpu_count() or 1
+        line["cpu_baseline"] = cpu_reference_sample(model, args.ref_reps, 3, 1, threads)
+    except Exception as exc:   # reference build absent on this machine
+        line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": 0, "kind": "reference",
+                                "sample": f"unavailable: {exc}"}
+    return line
+
+
+def run_reference(args):
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return None
+    from mtpb200 import read_mtp
+    model = read_mtp(MODEL)
+    threads = os.cpu_count() or 1
+    r = cpu_reference_sample(model, args.ref_reps, max(args.steps, 1), max(args.warmup, 0),
+                             threads)
+    return {"metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (seeded Ni3Al L1_2 box, seeded level-20 coefficients)",
+            "config": {"workload": "config 3 sample: reference CPU path (Neighborhoods + "
+                                   "MLIPCore::compute, OpenMP over centres) on a bounded box",
+                       "parallelism": f"openmp{threads}"},
+            "impl": "reference", "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores",
+                                                                   "kind", "sample")},
+            "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse()
+    line = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

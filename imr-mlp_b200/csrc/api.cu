@@ -6,6 +6,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <exception>
 #include <new>
@@ -237,6 +238,8 @@ int mtpb_create(int device, const mtpb_model_view *view, mtpb_context **out)
             rc = fail(MTPB_ERR_ARGUMENT, err);
             break;
         }
+        if (const char *v = std::getenv("MTPB_DAG_APT"))
+            g_dag_apt = std::atoi(v) == 4 ? 4 : 2;
         c->shape = select_shape(c->model, &err);
         if (c->shape < 0) {
             rc = fail(MTPB_ERR_UNSUPPORTED, err);
@@ -272,10 +275,12 @@ int mtpb_create(int device, const mtpb_model_view *view, mtpb_context **out)
             rc = fail(MTPB_ERR_UNSUPPORTED, "this library is built for sm_100a (B200) devices");
             break;
         }
-        if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess) {
+        if ((e = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking)) !=
+            cudaSuccess) {
             rc = cuda_fail(e, "cudaStreamCreate");
             break;
         }
+        c->stream = c->own_stream;
         for (auto &ev : c->ev)
             if ((e = cudaEventCreate(&ev)) != cudaSuccess) {
                 rc = cuda_fail(e, "cudaEventCreate");
@@ -305,8 +310,8 @@ int mtpb_destroy(mtpb_context *c)
     for (auto &ev : c->ev)
         if (ev)
             cudaEventDestroy(ev);
-    if (c->stream)
-        cudaStreamDestroy(c->stream);
+    if (c->own_stream)
+        cudaStreamDestroy(c->own_stream);
     delete c;
     return MTPB_OK;
 }
@@ -334,6 +339,18 @@ int mtpb_update_coefficients(mtpb_context *c, const double *radial, const double
     c->plan = std::move(plan);
     c->have_efs = false;
     return upload_model(c);
+}
+
+int mtpb_set_stream(mtpb_context *c, void *stream)
+{
+    if (!c)
+        return fail(MTPB_ERR_ARGUMENT, "ctx is NULL");
+    int rc = set_device(c);
+    if (rc)
+        return rc;
+    CUDA_TRY(cudaStreamSynchronize(c->stream), "sync");
+    c->stream = stream ? static_cast<cudaStream_t>(stream) : c->own_stream;
+    return MTPB_OK;
 }
 
 int mtpb_cutoff(const mtpb_context *c, double *cutoff)
@@ -473,6 +490,14 @@ int mtpb_build_neighbors(mtpb_context *c, const mtpb_structures *in, int memory)
         return cuda_fail(e, "neighbour build");
     c->nb = res;
     c->nedges = res.nedges;
+    c->d_ns = d_ns;
+    c->d_x_build = c->arena.get<double>("x_build", 3 * (size_t)N + 3);
+    if (!c->d_x_build)
+        return fail(MTPB_ERR_MEMORY, "device allocation failed");
+    if (N)
+        CUDA_TRY(cudaMemcpyAsync(c->d_x_build, d_pos, sizeof(double) * 3 * N,
+                                 cudaMemcpyDeviceToDevice, c->stream),
+                 "keep positions");
     c->natoms = N;
     c->ntotal = N;
     c->nstruct = S;
@@ -513,6 +538,9 @@ int mtpb_build_neighbors(mtpb_context *c, const mtpb_structures *in, int memory)
     CUDA_TRY(cudaStreamSynchronize(c->stream), "neighbour build");
     c->have_list = true;
     c->nb_built_this_call = true;
+    // struct ids, wrap/bin, 3 scans (2 kernels each), cell fill and sort,
+    // count, fill, in-edge count, fill and sort
+    c->pending_launches = 17;
     return MTPB_OK;
 }
 
@@ -569,7 +597,8 @@ int mtpb_efs_compute(mtpb_context *c, int memory, const mtpb_efs_output *out)
     const bool dev = memory == MTPB_MEMORY_DEVICE;
     const int N = c->natoms, S = c->nstruct;
     const long E = c->nedges;
-    c->launches = 0;
+    c->launches = c->nb_built_this_call ? c->pending_launches : 0;
+    c->pending_launches = 0;
     if (!c->nb_built_this_call)
         CUDA_TRY(cudaEventRecord(c->ev[0], c->stream), "event");
     double *site_energy = c->arena.get<double>("site_energy", N + 1);
@@ -637,15 +666,39 @@ int mtpb_efs_structures(mtpb_context *c, const mtpb_structures *in, int memory,
         return rc;
     bool reuse = reuse_neighbors && c->have_list && in->n_structures == c->nstruct;
     if (reuse) {
-        // the layout must be unchanged; positions are those of the build
-        if (memory != MTPB_MEMORY_DEVICE)
-            for (int s = 0; s <= in->n_structures && reuse; ++s)
-                reuse = in->atom_offsets[s] == c->h_atom_offsets[s];
+        // the batch layout must be unchanged; cells are those of the build
+        // host arrays are checked; for device arrays the caller guarantees an
+        // unchanged batch layout (no device-to-host read on the reuse path)
+        if (memory != MTPB_MEMORY_DEVICE) {
+            std::vector<int> off(in->atom_offsets, in->atom_offsets + in->n_structures + 1);
+            reuse = off == c->h_atom_offsets;
+        }
     }
     if (!reuse) {
         rc = mtpb_build_neighbors(c, in, memory);
         if (rc)
             return rc;
+    } else {
+        if ((rc = set_device(c)))
+            return rc;
+        const int N = c->natoms;
+        const double *x = in->positions;
+        if (memory != MTPB_MEMORY_DEVICE && N) {
+            double *p = c->arena.get<double>("in_positions", 3 * (size_t)N);
+            if (!p)
+                return fail(MTPB_ERR_MEMORY, "device allocation failed");
+            CUDA_TRY(cudaMemcpyAsync(p, in->positions, sizeof(double) * 3 * N,
+                                     cudaMemcpyHostToDevice, c->stream),
+                     "upload positions");
+            x = p;
+        }
+        CUDA_TRY(cudaEventRecord(c->ev[0], c->stream), "event");
+        CUDA_TRY(refresh_edges(N, c->d_ns, c->nb.struct_of, c->nb, c->d_x_build, x,
+                               const_cast<double *>(c->nb.rx), const_cast<double *>(c->nb.ry),
+                               const_cast<double *>(c->nb.rz), c->stream),
+                 "refresh edge vectors");
+        c->nb_built_this_call = true;   // ev[0] marks the refresh
+        c->pending_launches = 1;
     }
     return mtpb_efs_compute(c, memory, out);
 }

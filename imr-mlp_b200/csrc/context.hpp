@@ -34,7 +34,8 @@ int cuda_fail(cudaError_t e, const char *where);
 
 struct mtpb_context {
     int device = 0;
-    cudaStream_t stream = nullptr;
+    cudaStream_t stream = nullptr;      // stream in use
+    cudaStream_t own_stream = nullptr;  // stream created by the context
     mtpb::ModelHost model;
     int shape = -1;
     int nslot = 0;
@@ -56,6 +57,8 @@ struct mtpb_context {
     std::vector<double> h_cells;
     mtpb::NbResult nb;
     const int *d_types = nullptr;
+    double *d_x_build = nullptr;          // positions of the last build
+    const mtpb::NbStruct *d_ns = nullptr;  // structures of the last build
     const int *d_offsets = nullptr;
     int *d_group_maxdeg = nullptr;
     int *d_seg_begin = nullptr, *d_seg_end = nullptr, *d_struct_seg0 = nullptr;
@@ -66,6 +69,7 @@ struct mtpb_context {
     bool ev_valid = false;
     bool nb_built_this_call = false;
     int launches = 0;
+    int pending_launches = 0;   // neighbour build / refresh launches of this call
     bool have_efs = false;
     mtpb::TrainingState train;
 };

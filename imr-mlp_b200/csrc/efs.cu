@@ -586,13 +586,73 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long *bar, unsigned 
 constexpr int DAG_MAX_PHASES = 64;
 constexpr long DAG_WAIT_LIMIT = 1L << 22;   // bounded wait: sets the error flag
 
-__global__ void __launch_bounds__(DAG_WARPS * 32, 1)
+// APT atoms per thread: a record stream is served by LPS = 16/APT lanes, a
+// warp serves 32/LPS streams, the block DAG_STREAMS streams.  Each lane reads
+// its APT consecutive atoms of a row with 128-bit loads; for APT = 4 the two
+// halves of a row are visited in an order that alternates between streams,
+// so the eight streams of a warp cover all 32 banks (conflict-free).
+template <int APT> struct DagGeom {
+    static constexpr int LPS = DAG_ATOMS / APT;
+    static constexpr int SPW = 32 / LPS;
+    static constexpr int WARPS = DAG_STREAMS / SPW;
+    static constexpr int THREADS = WARPS * 32;
+};
+
+struct DecodedRec {
+    double c;
+    unsigned s1, s2, out, f;
+};
+
+__device__ __forceinline__ DecodedRec decode(const DagRec *p)
+{
+    const uint4 w = *reinterpret_cast<const uint4 *>(p);
+    DecodedRec d;
+    d.c = __hiloint2double((int)w.w, (int)w.z);
+    d.s1 = w.x & 0xffffu;
+    d.s2 = w.x >> 16;
+    d.out = w.y & 0xffffu;
+    d.f = w.y >> 16;
+    return d;
+}
+
+template <int APT> struct AtomVec {
+    double v[APT];
+};
+
+// loads the APT values of this lane from row `row`
+template <int APT>
+__device__ __forceinline__ AtomVec<APT> load_row(const double *rows, unsigned row, int a0, int a1)
+{
+    AtomVec<APT> r;
+    const double2 x = *reinterpret_cast<const double2 *>(rows + row * DAG_ATOMS + a0);
+    r.v[0] = x.x;
+    r.v[1] = x.y;
+    if constexpr (APT == 4) {
+        const double2 y = *reinterpret_cast<const double2 *>(rows + row * DAG_ATOMS + a1);
+        r.v[2] = y.x;
+        r.v[3] = y.y;
+    }
+    return r;
+}
+
+template <int APT>
+__device__ __forceinline__ void store_row(double *rows, unsigned row, int a0, int a1,
+                                          const double *acc)
+{
+    *reinterpret_cast<double2 *>(rows + row * DAG_ATOMS + a0) = make_double2(acc[0], acc[1]);
+    if constexpr (APT == 4)
+        *reinterpret_cast<double2 *>(rows + row * DAG_ATOMS + a1) = make_double2(acc[2], acc[3]);
+}
+
+template <int APT>
+__global__ void __launch_bounds__(DagGeom<APT>::THREADS, 1)
     k_dag(const DagRec *__restrict__ recs, const int *__restrict__ phase_row0, int n_fwd,
           int n_rev, int one_row, int zero_row, int nslot, int natoms, int npad,
           const int *__restrict__ types, const double *__restrict__ species_coeffs,
           const double *__restrict__ basic, double *__restrict__ adjoint,
           double *__restrict__ site_energy, int *__restrict__ err_flag)
 {
+    using G = DagGeom<APT>;
     extern __shared__ __align__(128) unsigned char dsm[];
     DagRec *ring = reinterpret_cast<DagRec *>(dsm);   // [2][CH][STREAMS]
     double *rows = reinterpret_cast<double *>(dsm + 2 * DAG_CHUNK_ROWS * DAG_STREAMS *
@@ -606,7 +666,6 @@ __global__ void __launch_bounds__(DAG_WARPS * 32, 1)
         ph0[i] = phase_row0[i];
     const int total_rows = phase_row0[nph];
     const int nchunks = (total_rows + DAG_CHUNK_ROWS - 1) / DAG_CHUNK_ROWS;
-    constexpr unsigned CHUNK_BYTES = DAG_CHUNK_ROWS * DAG_STREAMS * sizeof(DagRec);
     auto chunk_bytes = [&](int k) -> unsigned {
         const int r = min(DAG_CHUNK_ROWS, total_rows - k * DAG_CHUNK_ROWS);
         return (unsigned)(r * DAG_STREAMS * sizeof(DagRec));
@@ -632,96 +691,154 @@ __global__ void __launch_bounds__(DAG_WARPS * 32, 1)
         rows[zero_row * DAG_ATOMS + tid] = 0.0;
     }
     __syncthreads();
-    const int warp = tid >> 5, lane = tid & 31;
-    const int stream = warp * 2 + (lane >> 4);
-    const int al = lane & 15;
-    const int atom = atom0 + al;
-    double E = 0.0, acc = 0.0;
-    int ph = 0;
-    auto advance_phase = [&]() {
+    const int lane = tid & 31, warp = tid >> 5;
+    const int g = lane / G::LPS, q = lane - g * G::LPS;
+    const int stream = warp * G::SPW + g;
+    // atoms of this lane: [a0, a0+2) and, for APT 4, [a1, a1+2)
+    int a0, a1;
+    if constexpr (APT == 2) {
+        a0 = 2 * q;
+        a1 = a0;
+    } else {
+        const int h = g & 1;
+        a0 = h * 8 + 2 * q;
+        a1 = (h ^ 1) * 8 + 2 * q;
+    }
+    double E[APT], acc[APT];
+#pragma unroll
+    for (int j = 0; j < APT; ++j) {
+        E[j] = 0.0;
+        acc[j] = 0.0;
+    }
+    auto atom_of = [&](int j) { return atom0 + (j < 2 ? a0 + j : a1 + j - 2); };
+    auto apply = [&](const DecodedRec &d, const AtomVec<APT> &x, const AtomVec<APT> &y) {
+        const bool st = d.f & DAG_START;
+#pragma unroll
+        for (int j = 0; j < APT; ++j)
+            acc[j] = fma(d.c * x.v[j], y.v[j], st ? 0.0 : acc[j]);
+        if (d.f & DAG_END) {
+            if (d.f & DAG_GLOBAL) {
+#pragma unroll
+                for (int j = 0; j < APT; ++j) {
+                    const int at = atom_of(j);
+                    if (at < natoms)
+                        adjoint[(size_t)d.out * npad + at] = acc[j];
+                }
+            } else {
+                store_row<APT>(rows, d.out, a0, a1, acc);
+            }
+        }
+        if (d.f & DAG_ENERGY) {
+#pragma unroll
+            for (int j = 0; j < APT; ++j)
+                E[j] = fma(d.c, acc[j], E[j]);
+        }
+    };
+    int k = -1, cr0 = 0, cr1 = 0;
+    const DagRec *cb = ring;
+    for (int ph = 0; ph < nph; ++ph) {
+        int r = ph0[ph];
+        const int rend = ph0[ph + 1];
+        while (r < rend) {
+            if (r >= cr1) {   // next chunk (block-uniform)
+                if (k >= 0) {
+                    __syncthreads();
+                    if (tid == 0 && k + 2 < nchunks) {
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        bulk_load(ring + (k & 1) * DAG_CHUNK_ROWS * DAG_STREAMS,
+                                  recs + (size_t)(k + 2) * DAG_CHUNK_ROWS * DAG_STREAMS,
+                                  chunk_bytes(k + 2), &bar[k & 1]);
+                    }
+                }
+                ++k;
+                long it = 0;
+                while (!mbar_try_wait(&bar[k & 1], (unsigned)((k >> 1) & 1))) {
+                    if (++it > DAG_WAIT_LIMIT) {
+                        *err_flag = 1;
+                        break;
+                    }
+                }
+                cb = ring + (k & 1) * DAG_CHUNK_ROWS * DAG_STREAMS + stream;
+                cr0 = k * DAG_CHUNK_ROWS;
+                cr1 = min(total_rows, cr0 + DAG_CHUNK_ROWS);
+            }
+            const int seg_end = min(rend, cr1);
+            // two records per step: rows written in a phase are never read in
+            // the same phase, so the second record's loads may run first
+            for (; r + 1 < seg_end; r += 2) {
+                const DecodedRec d0 = decode(cb + (r - cr0) * DAG_STREAMS);
+                const DecodedRec d1 = decode(cb + (r + 1 - cr0) * DAG_STREAMS);
+                const AtomVec<APT> x0 = load_row<APT>(rows, d0.s1, a0, a1);
+                const AtomVec<APT> y0 = load_row<APT>(rows, d0.s2, a0, a1);
+                const AtomVec<APT> x1 = load_row<APT>(rows, d1.s1, a0, a1);
+                const AtomVec<APT> y1 = load_row<APT>(rows, d1.s2, a0, a1);
+                apply(d0, x0, y0);
+                apply(d1, x1, y1);
+            }
+            if (r < seg_end) {
+                const DecodedRec d0 = decode(cb + (r - cr0) * DAG_STREAMS);
+                const AtomVec<APT> x0 = load_row<APT>(rows, d0.s1, a0, a1);
+                const AtomVec<APT> y0 = load_row<APT>(rows, d0.s2, a0, a1);
+                apply(d0, x0, y0);
+                ++r;
+            }
+        }
         __syncthreads();
-        ++ph;
-        if (ph == n_fwd) {
-            epart[stream][al] = E;
+        if (ph + 1 == n_fwd) {
+#pragma unroll
+            for (int j = 0; j < APT; ++j)
+                epart[stream][j < 2 ? a0 + j : a1 + j - 2] = E[j];
             __syncthreads();
             if (tid < DAG_ATOMS && atom0 + tid < natoms) {
                 const int t = types[atom0 + tid];
                 double se = 0.0;
                 if (t >= 0) {
                     se = species_coeffs[t];
-                    for (int q = 0; q < DAG_STREAMS; ++q)
-                        se += epart[q][tid];
+                    for (int s2 = 0; s2 < DAG_STREAMS; ++s2)
+                        se += epart[s2][tid];
                 }
                 site_energy[atom0 + tid] = se;
             }
         }
-    };
-    for (int k = 0; k < nchunks; ++k) {
-        const int b = k & 1;
-        long it = 0;
-        while (!mbar_try_wait(&bar[b], (unsigned)((k >> 1) & 1))) {
-            if (++it > DAG_WAIT_LIMIT) {
-                *err_flag = 1;
-                break;
-            }
-        }
-        const DagRec *cb = ring + b * DAG_CHUNK_ROWS * DAG_STREAMS;
-        const int r0 = k * DAG_CHUNK_ROWS;
-        const int r1 = min(total_rows, r0 + DAG_CHUNK_ROWS);
-        for (int r = r0; r < r1; ++r) {
-            while (ph < nph && r == ph0[ph + 1])
-                advance_phase();
-            const uint4 w = *reinterpret_cast<const uint4 *>(cb + (r - r0) * DAG_STREAMS + stream);
-            const double c = __hiloint2double((int)w.w, (int)w.z);
-            const unsigned s1 = w.x & 0xffffu, s2 = w.x >> 16;
-            const unsigned out = w.y & 0xffffu, f = w.y >> 16;
-            const double p = c * rows[s1 * DAG_ATOMS + al];
-            acc = fma(p, rows[s2 * DAG_ATOMS + al], (f & DAG_START) ? 0.0 : acc);
-            if (f & DAG_END) {
-                if (f & DAG_GLOBAL) {
-                    if (atom < natoms)
-                        adjoint[(size_t)out * npad + atom] = acc;
-                } else {
-                    rows[out * DAG_ATOMS + al] = acc;
-                }
-            }
-            if (f & DAG_ENERGY)
-                E = fma(c, acc, E);
-        }
-        __syncthreads();
-        if (tid == 0 && k + 2 < nchunks) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            bulk_load(ring + b * DAG_CHUNK_ROWS * DAG_STREAMS,
-                      recs + (size_t)(k + 2) * DAG_CHUNK_ROWS * DAG_STREAMS, chunk_bytes(k + 2),
-                      &bar[b]);
-        }
     }
-    while (ph < nph)
-        advance_phase();
-    (void)CHUNK_BYTES;
 }
+
+template <int APT>
+static cudaError_t launch_dag_apt(const DagPlan &plan, const DagRec *recs, const int *phase_row0,
+                                 int nslot, int natoms, int npad, const int *types,
+                                 const double *species_coeffs, const double *basic,
+                                 double *adjoint, double *site_energy, int *err_flag,
+                                 cudaStream_t s)
+{
+    const int blocks = (natoms + DAG_ATOMS - 1) / DAG_ATOMS;
+    const size_t smem = 2 * DAG_CHUNK_ROWS * DAG_STREAMS * sizeof(DagRec) +
+                        sizeof(double) * (size_t)plan.nrows * DAG_ATOMS;
+    cudaError_t err = cudaFuncSetAttribute(k_dag<APT>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err != cudaSuccess)
+        return err;
+    k_dag<APT><<<blocks, DagGeom<APT>::THREADS, smem, s>>>(
+        recs, phase_row0, plan.n_fwd, plan.n_rev, plan.one_row, plan.zero_row, nslot, natoms, npad,
+        types, species_coeffs, basic, adjoint, site_energy, err_flag);
+    return cudaGetLastError();
+}
+
+int g_dag_apt = 2;   // atoms per thread of the graph kernel (2 or 4)
 
 cudaError_t launch_dag(const DagPlan &plan, const DagRec *recs, const int *phase_row0, int nslot,
                        int natoms, int npad, const int *types, const double *species_coeffs,
                        const double *basic, double *adjoint, double *site_energy, int *err_flag,
                        cudaStream_t s)
 {
-    const int blocks = (natoms + DAG_ATOMS - 1) / DAG_ATOMS;
-    if (blocks == 0)
+    if (natoms == 0)
         return cudaSuccess;
     if (plan.n_fwd + plan.n_rev > DAG_MAX_PHASES)
         return cudaErrorInvalidValue;
-    const size_t smem = 2 * DAG_CHUNK_ROWS * DAG_STREAMS * sizeof(DagRec) +
-                        sizeof(double) * (size_t)plan.nrows * DAG_ATOMS;
-    cudaError_t err = cudaFuncSetAttribute(k_dag, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)smem);
-    if (err != cudaSuccess)
-        return err;
-    k_dag<<<blocks, DAG_WARPS * 32, smem, s>>>(recs, phase_row0, plan.n_fwd, plan.n_rev,
-                                               plan.one_row, plan.zero_row, nslot, natoms, npad,
-                                               types, species_coeffs, basic, adjoint, site_energy,
-                                               err_flag);
-    return cudaGetLastError();
+    if (g_dag_apt == 2)
+        return launch_dag_apt<2>(plan, recs, phase_row0, nslot, natoms, npad, types,
+                                 species_coeffs, basic, adjoint, site_energy, err_flag, s);
+    return launch_dag_apt<4>(plan, recs, phase_row0, nslot, natoms, npad, types, species_coeffs,
+                             basic, adjoint, site_energy, err_flag, s);
 }
 
 // ----------------------------------------------------------------------------

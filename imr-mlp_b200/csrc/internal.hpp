@@ -60,10 +60,15 @@ inline DagRec make_rec(int s1, int s2, int out, unsigned flags, double c)
     return r;
 }
 
-constexpr int DAG_ATOMS = 16;        // atoms per DAG block (half-warp)
-constexpr int DAG_WARPS = 16;        // warps per DAG block
-constexpr int DAG_STREAMS = 2 * DAG_WARPS;
-constexpr int DAG_CHUNK_ROWS = 32;   // record rows per shared-memory chunk
+#ifndef MTPB_DAG_STREAMS
+#define MTPB_DAG_STREAMS 32
+#endif
+#ifndef MTPB_DAG_CHUNK_ROWS
+#define MTPB_DAG_CHUNK_ROWS 32
+#endif
+constexpr int DAG_ATOMS = 16;                         // atoms per graph block
+constexpr int DAG_STREAMS = MTPB_DAG_STREAMS;         // record streams per block
+constexpr int DAG_CHUNK_ROWS = MTPB_DAG_CHUNK_ROWS;   // record rows per shared chunk
 
 struct DagPlan {
     int nrows = 0;           // shared-memory rows (one double per atom each)
@@ -93,6 +98,7 @@ struct EdgeArgs {
 cudaError_t launch_moments_fwd(int shape, const EdgeArgs &a, double *basic, cudaStream_t s);
 cudaError_t launch_moments_rev(int shape, const EdgeArgs &a, const double *adjoint, double *dx,
                                double *dy, double *dz, cudaStream_t s);
+extern int g_dag_apt;   // graph kernel atoms per thread (2 or 4)
 cudaError_t launch_dag(const DagPlan &plan, const DagRec *recs, const int *phase_row0,
                        int nslot, int natoms, int npad, const int *types,
                        const double *species_coeffs, const double *basic, double *adjoint,

@@ -257,6 +257,60 @@ __global__ void k_edge_vectors(int ncenter, const int *__restrict__ offsets,
     }
 }
 
+// Edge vectors for new positions with the image of every pair kept from the
+// last build (MD steps between rebuilds, MTPGpuComputeRequest::reuse_topology):
+// w' = w_build + (x - x_build) keeps atoms unwrapped relative to the build, and
+// r follows the build's i <= o rule so that unchanged positions reproduce the
+// build's displacements bit for bit.
+__global__ void k_refresh_edges(long nedges, const NbStruct *__restrict__ structs,
+                                const int *__restrict__ struct_of, const int *__restrict__ center,
+                                const int *__restrict__ nbr, const int *__restrict__ shift,
+                                const double *__restrict__ wx, const double *__restrict__ wy,
+                                const double *__restrict__ wz, const double *__restrict__ x_build,
+                                const double *__restrict__ x, double *__restrict__ rx,
+                                double *__restrict__ ry, double *__restrict__ rz)
+{
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= nedges)
+        return;
+    const int i = center[e];
+    const int o = nbr[e];
+    const NbStruct &st = structs[struct_of[i]];
+    auto wpos = [&](int a, double p[3]) {
+        p[0] = dadd(wx[a], __dsub_rn(x[3 * a], x_build[3 * a]));
+        p[1] = dadd(wy[a], __dsub_rn(x[3 * a + 1], x_build[3 * a + 1]));
+        p[2] = dadd(wz[a], __dsub_rn(x[3 * a + 2], x_build[3 * a + 2]));
+    };
+    double pi[3], po[3];
+    wpos(i, pi);
+    wpos(o, po);
+    const int code = shift[e];
+    const int s0 = (code & 0xff) - 128, s1 = ((code >> 8) & 0xff) - 128,
+              s2 = ((code >> 16) & 0xff) - 128;
+    const bool zero = (s0 == 0 && s1 == 0 && s2 == 0);
+    double t[3];
+    image_translation(st, s0, s1, s2, t);
+    if (i <= o) {
+        rx[e] = __dsub_rn(zero ? po[0] : dadd(po[0], t[0]), pi[0]);
+        ry[e] = __dsub_rn(zero ? po[1] : dadd(po[1], t[1]), pi[1]);
+        rz[e] = __dsub_rn(zero ? po[2] : dadd(po[2], t[2]), pi[2]);
+    } else {
+        rx[e] = -__dsub_rn(zero ? pi[0] : dadd(pi[0], -t[0]), po[0]);
+        ry[e] = -__dsub_rn(zero ? pi[1] : dadd(pi[1], -t[1]), po[1]);
+        rz[e] = -__dsub_rn(zero ? pi[2] : dadd(pi[2], -t[2]), po[2]);
+    }
+}
+
+// centre index of every edge (used by edge-parallel kernels)
+__global__ void k_edge_centers(int natoms, const int *__restrict__ offsets, int *__restrict__ center)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= natoms)
+        return;
+    for (int e = offsets[i]; e < offsets[i + 1]; ++e)
+        center[e] = i;
+}
+
 static inline int nblk(long n, int t) { return (int)((n + t - 1) / t); }
 
 cudaError_t exclusive_scan(const int *in, int *out, int n, DeviceArena &arena, cudaStream_t s)
@@ -306,6 +360,7 @@ cudaError_t build_neighbors(const NbBuildInput &in, DeviceArena &arena, NbResult
     res.wy = wy;
     res.wz = wz;
     res.offsets = offsets;
+    res.struct_of = struct_of;
     if (N == 0) {
         CK(cudaMemsetAsync(offsets, 0, sizeof(int), s));
         res.nedges = 0;
@@ -341,6 +396,11 @@ cudaError_t build_neighbors(const NbBuildInput &in, DeviceArena &arena, NbResult
                                                    cell_start, cell_atoms, nullptr, offsets, nbr,
                                                    shift, rx, ry, rz);
     CK(cudaGetLastError());
+    int *center = arena.get<int>("edge_center", (size_t)E + 1);
+    if (!center)
+        return cudaErrorMemoryAllocation;
+    k_edge_centers<<<nblk(N, 128), 128, 0, s>>>(N, offsets, center);
+    res.center = center;
     res.nbr = nbr;
     res.shift = shift;
     res.rx = rx;
@@ -374,6 +434,18 @@ cudaError_t build_in_edges(int ntotal, long E, const int *nbr, DeviceArena &aren
     k_sort_segments<<<nblk(ntotal, 128), 128, 0, s>>>(ntotal, in_offsets, in_edges);
     res.in_offsets = in_offsets;
     res.in_edges = in_edges;
+    return cudaGetLastError();
+}
+
+cudaError_t refresh_edges(int natoms, const NbStruct *structs, const int *struct_of,
+                          const NbResult &nb, const double *x_build, const double *x, double *rx,
+                          double *ry, double *rz, cudaStream_t s)
+{
+    if (nb.nedges == 0)
+        return cudaSuccess;
+    k_refresh_edges<<<nblk(nb.nedges, 256), 256, 0, s>>>(nb.nedges, structs, struct_of,
+                                                         nb.center, nb.nbr, nb.shift, nb.wx,
+                                                         nb.wy, nb.wz, x_build, x, rx, ry, rz);
     return cudaGetLastError();
 }
 

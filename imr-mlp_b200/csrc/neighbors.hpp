@@ -90,12 +90,17 @@ struct NbResult {
     const double *rx = nullptr, *ry = nullptr, *rz = nullptr;
     const int *in_offsets = nullptr;
     const int *in_edges = nullptr;
+    const int *struct_of = nullptr;   // [natoms]
+    const int *center = nullptr;      // [nedges] centre of every edge
 };
 
 cudaError_t build_neighbors(const NbBuildInput &in, DeviceArena &arena, NbResult &res,
                             cudaStream_t s);
 cudaError_t build_in_edges(int ntotal, long nedges, const int *nbr, DeviceArena &arena,
                            NbResult &res, cudaStream_t s);
+cudaError_t refresh_edges(int natoms, const NbStruct *structs, const int *struct_of,
+                          const NbResult &nb, const double *x_build, const double *x, double *rx,
+                          double *ry, double *rz, cudaStream_t s);
 cudaError_t edge_vectors(int ncenter, const int *offsets, const int *nbr, const double *x,
                          double *rx, double *ry, double *rz, cudaStream_t s);
 cudaError_t exclusive_scan(const int *in, int *out, int n, DeviceArena &arena, cudaStream_t s);

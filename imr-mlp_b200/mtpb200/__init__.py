@@ -170,6 +170,11 @@ class MTPGpuDirect:
         _check(self.lib.mtpb_cutoff(self.ctx, C.byref(v)))
         return v.value
 
+    def set_stream(self, stream_handle: int):
+        """Runs later work on a CUDA stream (e.g. torch.cuda.current_stream()
+        .cuda_stream); 0 returns to the context's own stream."""
+        _check(self.lib.mtpb_set_stream(self.ctx, C.c_void_p(stream_handle or None)))
+
     def set_skin(self, skin: float):
         _check(self.lib.mtpb_set_skin(self.ctx, float(skin)))
 
@@ -207,6 +212,18 @@ class MTPGpuDirect:
         out = _lib.EfsOutput(_dp(e), _dp(f), _dp(st), _dp(se))
         _check(self.lib.mtpb_efs_compute(self.ctx, _lib.MEMORY_HOST, C.byref(out)))
         return e[:S], f[:N], st[:S].reshape(S, 3, 3), (se[:N] if se is not None else None)
+
+    def efs_structures(self, batch: StructureBatch, reuse_neighbors: bool = False,
+                       out=None):
+        """mtpb_efs_structures with host arrays: builds (or, with reuse and an
+        unchanged layout, refreshes) the lists from batch.positions and writes
+        energy[S], forces[N,3], stress[S,9] into `out` (dict of arrays)."""
+        self._batch = batch
+        st = batch.c_struct()
+        o = _lib.EfsOutput(_dp(out.get("energy")), _dp(out.get("forces")),
+                           _dp(out.get("stress")), _dp(out.get("site_energy")))
+        _check(self.lib.mtpb_efs_structures(self.ctx, C.byref(st), _lib.MEMORY_HOST,
+                                            int(reuse_neighbors), C.byref(o)))
 
     def efs(self, batch: StructureBatch, site_energy: bool = False, reuse_neighbors=False):
         if not (reuse_neighbors and self._batch is not None):

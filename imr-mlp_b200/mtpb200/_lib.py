@@ -80,6 +80,7 @@ SIGNATURES = [
     ("mtpb_create", C.c_int, [C.c_int, C.POINTER(ModelView), C.POINTER(C.c_void_p)]),
     ("mtpb_destroy", C.c_int, [C.c_void_p]),
     ("mtpb_update_coefficients", C.c_int, [C.c_void_p, _dp, _dp, _dp]),
+    ("mtpb_set_stream", C.c_int, [C.c_void_p, C.c_void_p]),
     ("mtpb_cutoff", C.c_int, [C.c_void_p, _dp]),
     ("mtpb_set_skin", C.c_int, [C.c_void_p, C.c_double]),
     ("mtpb_build_neighbors", C.c_int, [C.c_void_p, C.POINTER(Structures), C.c_int]),

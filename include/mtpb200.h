@@ -107,6 +107,11 @@ int mtpb_destroy(mtpb_context *ctx);
 int mtpb_update_coefficients(mtpb_context *ctx, const double *radial, const double *species,
                              const double *moment);
 
+/* Runs all later work of the context on `stream` (a cudaStream_t of the
+ * context's device; NULL returns to the context's own stream).  The caller
+ * keeps the stream alive while the context uses it. */
+int mtpb_set_stream(mtpb_context *ctx, void *stream);
+
 /* Model cutoff (largest pair max_dist), in Angstrom. */
 int mtpb_cutoff(const mtpb_context *ctx, double *cutoff);
 
@@ -140,7 +145,10 @@ int mtpb_efs_compute(mtpb_context *ctx, int memory, const mtpb_efs_output *out);
 /* Convenience: build + compute in one call (PotMTP::getEFS(Atoms&),
  * potential_mtp.cpp:1892-1897, batched like calc_efs, apps/calc_efs.cpp:336-380).
  * reuse_neighbors != 0 keeps the previous list when the batch layout is
- * unchanged (MTPGpuComputeRequest::reuse_topology). */
+ * unchanged (MTPGpuComputeRequest::reuse_topology): the new positions are
+ * uploaded and every edge vector is recomputed from its stored periodic image
+ * (the atoms must stay within the skin of the last build).  For host arrays the
+ * layout is checked; for device arrays the caller guarantees it. */
 int mtpb_efs_structures(mtpb_context *ctx, const mtpb_structures *in, int memory,
                         int reuse_neighbors, const mtpb_efs_output *out);
 

@@ -241,6 +241,8 @@ class Reference:
         L.ref_mlip_destroy.argtypes = [C.c_void_p]
         L.ref_mlip_compute.argtypes = [C.c_void_p, C.c_int, _ip, C.c_int, _ip, _dp, _ip, _ip, _ip,
                                        _dp, _dp, _dp, _dp]
+        L.ref_mlip_compute_omp.argtypes = [C.c_void_p, C.c_int, C.c_int, _ip, C.c_int, _ip, _dp,
+                                           _ip, _ip, _ip, _dp, _dp]
 
     @staticmethod
     def available(path: Optional[str] = None) -> bool:
@@ -302,3 +304,61 @@ class Reference:
             return float(en[0]), se[:n], forces, vir
         finally:
             self.lib.ref_mlip_destroy(h)
+
+
+class ReferenceEFS:
+    """The reference CPU path for one periodic structure, as the benchmark's
+    CPU arm runs it: Neighborhoods (compiled reference) builds the lists, the
+    images become explicit ghost atoms, and MLIPCore::compute evaluates the
+    centres with OpenMP (ref_mlip_compute_omp)."""
+
+    def __init__(self, mtp_text: str, species: int, threads: int = 0):
+        self.ref = Reference()
+        L = self.ref.lib
+        tmap = np.arange(species, dtype=np.int32)
+        self._tmap = tmap
+        cut = np.zeros(1)
+        self.handle = L.ref_mlip_setup(mtp_text.encode(), _i(tmap), len(tmap), _d(cut))
+        if not self.handle:
+            raise RuntimeError(self.ref._err())
+        self.cutoff = float(cut[0])
+        self.threads = threads
+
+    def close(self):
+        if self.handle:
+            self.ref.lib.ref_mlip_destroy(self.handle)
+            self.handle = None
+
+    def build(self, cell, pbc, positions, types):
+        """Reference neighbour build; returns the ghost-atom problem."""
+        nl = self.ref.neighbors(cell, pbc, positions, self.cutoff)
+        n = len(types)
+        E = nl.n_edges
+        from_oracle = Oracle()
+        x0 = from_oracle.wrap(cell, pbc, positions)
+        centers = np.repeat(np.arange(n), np.diff(nl.offsets))
+        x = np.ascontiguousarray(np.concatenate([x0, x0[centers] + nl.rij]))
+        ty = np.ascontiguousarray(np.concatenate([types, np.asarray(types)[nl.nbr]]).astype(np.int32))
+        ntot = n + E
+        numneigh = np.zeros(ntot, dtype=np.int32)
+        numneigh[:n] = np.diff(nl.offsets)
+        foff = np.zeros(ntot, dtype=np.int32)
+        foff[:n] = nl.offsets[:-1]
+        flat = (n + np.arange(E)).astype(np.int32)
+        return dict(n=n, nl=nl, x=x, types=ty, numneigh=numneigh, foff=foff, flat=flat)
+
+    def compute(self, prob):
+        n = prob["n"]
+        ntot = len(prob["types"])
+        f = np.zeros((ntot, 3))
+        en = np.zeros(1)
+        ilist = np.arange(n, dtype=np.int32)
+        rc = self.ref.lib.ref_mlip_compute_omp(self.handle, self.threads, n, _i(ilist), ntot,
+                                               _i(prob["types"]), _d(prob["x"]),
+                                               _i(prob["numneigh"]), _i(prob["foff"]),
+                                               _i(prob["flat"]), _d(en), _d(f))
+        if rc:
+            raise RuntimeError(self.ref._err())
+        forces = f[:n].copy()
+        np.add.at(forces, prob["nl"].nbr, f[n:])
+        return float(en[0]), forces

@@ -14,6 +14,7 @@
 #include "runtime/mtp/mlip.h"
 
 #include <cstring>
+#include <omp.h>
 #include <exception>
 #include <string>
 #include <vector>
@@ -132,6 +133,78 @@ int ref_mlip_compute(void *handle, int inum, const int *ilist, int ntotal, const
         MLIPCore::compute(p, buf, ilist, numneigh, inum, type, xptr.data(), nptr.data(), &en,
                           site_energy, site_virial ? vptr.data() : nullptr, fptr.data());
         MLIPCore::destroy_mlip_buffer(buf);
+        *energy = en;
+        return 0;
+    }
+    catch (const std::exception &ex)
+    {
+        g_error = ex.what();
+        return -1;
+    }
+}
+
+// MLIPCore::compute driven by OpenMP over centres: each thread owns one
+// mlip_buffers workspace and private force / virial arrays (the thread-safety
+// contract of the standalone core, runtime/mtp/cpu/mtp_cpu.h:38-40), merged
+// serially afterwards as PotMTP::getEFSOMP does (potential_mtp.cpp:2476-2485).
+int ref_mlip_compute_omp(void *handle, int threads, int inum, const int *ilist, int ntotal,
+                         const int *type, const double *x, const int *numneigh,
+                         const int *firstneigh_off, const int *firstneigh_flat, double *energy,
+                         double *f)
+{
+    try
+    {
+        auto *p = static_cast<MLIPCore::mlip *>(handle);
+        if (threads <= 0)
+            threads = omp_get_max_threads();
+        std::vector<double> xcopy(x, x + 3 * static_cast<std::size_t>(ntotal));
+        std::vector<double *> xptr(ntotal);
+        std::vector<int *> nptr(ntotal);
+        for (int i = 0; i < ntotal; ++i)
+        {
+            xptr[i] = xcopy.data() + 3 * i;
+            nptr[i] = const_cast<int *>(firstneigh_flat) + firstneigh_off[i];
+        }
+        std::vector<std::vector<double>> fbuf(threads);
+        std::vector<double> ebuf(threads, 0.0);
+        int failed = 0;
+#pragma omp parallel num_threads(threads) reduction(| : failed)
+        {
+            const int t = omp_get_thread_num();
+            const int nt = omp_get_num_threads();
+            const int b = (int)((long)inum * t / nt), e = (int)((long)inum * (t + 1) / nt);
+            try
+            {
+                fbuf[t].assign(3 * static_cast<std::size_t>(ntotal), 0.0);
+                std::vector<double *> fptr(ntotal);
+                for (int i = 0; i < ntotal; ++i)
+                    fptr[i] = fbuf[t].data() + 3 * i;
+                MLIPCore::mlip_buffers *buf = MLIPCore::create_mlip_buffer(p);
+                double en = 0;
+                MLIPCore::compute(p, buf, ilist + b, numneigh, e - b, type, xptr.data(),
+                                  nptr.data(), &en, nullptr, nullptr, fptr.data());
+                MLIPCore::destroy_mlip_buffer(buf);
+                ebuf[t] = en;
+            }
+            catch (...)
+            {
+                failed |= 1;
+            }
+        }
+        if (failed)
+        {
+            g_error = "MLIPCore::compute failed in a worker thread";
+            return -1;
+        }
+        double en = 0;
+        for (int t = 0; t < threads; ++t)
+        {
+            en += ebuf[t];
+            if (fbuf[t].empty())
+                continue;
+            for (std::size_t k = 0; k < fbuf[t].size(); ++k)
+                f[k] += fbuf[t][k];
+        }
         *energy = en;
         return 0;
     }

@@ -149,3 +149,39 @@ def test_deterministic_repeat(model_l20):
         r2 = gpu.efs(b, site_energy=True)
     for a, c in zip(r1, r2):
         assert np.array_equal(a, c)
+
+
+def test_neighbor_reuse_with_skin_matches_fresh_build(oracle, model_l16):
+    """MD-style reuse: build with a skin, move atoms by less than skin/2 and
+    recompute with the stored periodic images (reuse_topology semantics)."""
+    from mtpb200 import MTPGpuDirect, StructureBatch
+    st = configs.config1()
+    rng = np.random.default_rng(12)
+    moved = {**st, "positions": st["positions"] + rng.uniform(-0.2, 0.2, st["positions"].shape)}
+    b0 = StructureBatch.from_structures([st])
+    b1 = StructureBatch.from_structures([moved])
+    out = {"energy": np.zeros(1), "forces": np.zeros((256, 3)), "stress": np.zeros((1, 9))}
+    with MTPGpuDirect(model_l16, 0) as gpu:
+        gpu.set_skin(0.5)
+        gpu.efs_structures(b0, reuse_neighbors=False, out=out)
+        gpu.efs_structures(b1, reuse_neighbors=True, out=out)
+        assert gpu.last_launch_count() < 12      # refresh, not a rebuild
+    nl = oracle.neighbors(moved["cell"], moved["pbc"], moved["positions"], model_l16.cutoff)
+    eo, _, fo, so = oracle.efs(model_l16, moved["types"], nl)
+    assert abs(out["energy"][0] - eo) / 256 < TOL_E_ATOM
+    assert np.max(np.abs(out["forces"] - fo)) < TOL_F
+    assert np.max(np.abs(out["stress"][0] - so.reshape(9))) < TOL_W
+
+
+def test_neighbor_reuse_unchanged_positions_bit_identical(model_l20):
+    from mtpb200 import MTPGpuDirect, StructureBatch
+    st = configs.ni3al_l12(6, 3.52, 0.08, seed=4)
+    b = StructureBatch.from_structures([st])
+    N = b.n_atoms
+    o1 = {"energy": np.zeros(1), "forces": np.zeros((N, 3)), "stress": np.zeros((1, 9))}
+    o2 = {k: np.zeros_like(v) for k, v in o1.items()}
+    with MTPGpuDirect(model_l20, 0) as gpu:
+        gpu.efs_structures(b, reuse_neighbors=False, out=o1)
+        gpu.efs_structures(b, reuse_neighbors=True, out=o2)
+    for k in o1:
+        assert np.array_equal(o1[k], o2[k])
