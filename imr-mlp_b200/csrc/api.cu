@@ -90,7 +90,7 @@ static int upload_model(mtpb_context *c)
     c->d_radial = c->arena.get<double>("model_radial", m.radial.size());
     c->d_species = c->arena.get<double>("model_species", m.K);
     c->d_pairs = c->arena.get<PairParams>("model_pairs", KK);
-    c->d_recs = c->arena.get<DagRec>("model_dag", c->plan.recs.size());
+    c->d_recs = c->arena.get<DagDevRec>("model_dag", c->plan.recs.size());
     std::vector<int> row0(c->plan.phase_rows.size() + 1, 0);
     for (size_t i = 0; i < c->plan.phase_rows.size(); ++i)
         row0[i + 1] = row0[i] + c->plan.phase_rows[i];
@@ -112,7 +112,10 @@ static int upload_model(mtpb_context *c)
     CUDA_TRY(cudaMemcpyAsync(c->d_pairs, pp.data(), sizeof(PairParams) * KK,
                              cudaMemcpyHostToDevice, c->stream),
              "upload pairs");
-    CUDA_TRY(cudaMemcpyAsync(c->d_recs, c->plan.recs.data(), sizeof(DagRec) * c->plan.recs.size(),
+    if ((size_t)c->plan.nrows * 16 * sizeof(double) > 190 * 1024)
+        g_dag_atoms = 8;   // the 16-atom geometry does not fit this graph
+    c->h_recs = dag_device_records(c->plan);
+    CUDA_TRY(cudaMemcpyAsync(c->d_recs, c->h_recs.data(), sizeof(DagDevRec) * c->h_recs.size(),
                              cudaMemcpyHostToDevice, c->stream),
              "upload graph");
     CUDA_TRY(cudaMemcpyAsync(c->d_phase_row0, row0.data(), sizeof(int) * row0.size(),
@@ -238,8 +241,8 @@ int mtpb_create(int device, const mtpb_model_view *view, mtpb_context **out)
             rc = fail(MTPB_ERR_ARGUMENT, err);
             break;
         }
-        if (const char *v = std::getenv("MTPB_DAG_APT"))
-            g_dag_apt = std::atoi(v) == 4 ? 4 : 2;
+        if (const char *v = std::getenv("MTPB_DAG_ATOMS"))
+            g_dag_atoms = std::atoi(v) == 16 ? 16 : 8;
         c->shape = select_shape(c->model, &err);
         if (c->shape < 0) {
             rc = fail(MTPB_ERR_UNSUPPORTED, err);

@@ -41,12 +41,13 @@ struct mtpb_context {
     int nslot = 0;
     std::vector<int> slot_of_basic;
     mtpb::DagPlan plan;
+    std::vector<mtpb::DagDevRec> h_recs;   // plan records in the kernel's layout
     mtpb::DeviceArena arena;
     double skin = 0.0;
     // device model data
     double *d_radial = nullptr, *d_species = nullptr;
     mtpb::PairParams *d_pairs = nullptr;
-    mtpb::DagRec *d_recs = nullptr;
+    mtpb::DagDevRec *d_recs = nullptr;
     int *d_phase_row0 = nullptr;
     int *d_err = nullptr;   // device error flag (bounded waits that gave up)
     // current batch (structures path)

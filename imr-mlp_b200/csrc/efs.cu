@@ -586,210 +586,235 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long *bar, unsigned 
 constexpr int DAG_MAX_PHASES = 64;
 constexpr long DAG_WAIT_LIMIT = 1L << 22;   // bounded wait: sets the error flag
 
-// APT atoms per thread: a record stream is served by LPS = 16/APT lanes, a
-// warp serves 32/LPS streams, the block DAG_STREAMS streams.  Each lane reads
-// its APT consecutive atoms of a row with 128-bit loads; for APT = 4 the two
-// halves of a row are visited in an order that alternates between streams,
-// so the eight streams of a warp cover all 32 banks (conflict-free).
-template <int APT> struct DagGeom {
-    static constexpr int LPS = DAG_ATOMS / APT;
+// Geometry: ATOMS atoms per block, two atoms per lane; a record stream is
+// served by LPS = ATOMS/2 lanes, a warp serves SPW = 32/LPS streams and the
+// block DAG_STREAMS streams.  Records are laid out warp-major per phase
+// ([phase][warp][row][SPW streams], see dag_warp_major) so that every warp
+// streams its own contiguous records through a private double-buffered ring
+// filled by TMA bulk copies: warps only meet at the phase barriers.
+template <int ATOMS> struct DagGeom {
+    static constexpr int APT = 2;
+    static constexpr int LPS = ATOMS / APT;
     static constexpr int SPW = 32 / LPS;
     static constexpr int WARPS = DAG_STREAMS / SPW;
     static constexpr int THREADS = WARPS * 32;
+    static constexpr int CH = DAG_CHUNK_ROWS;                // rows per ring slot
+    static constexpr unsigned SLOT_BYTES = CH * SPW * sizeof(DagDevRec);
+    static constexpr size_t ring_bytes() { return (size_t)WARPS * 2 * SLOT_BYTES; }
 };
 
-struct DecodedRec {
-    double c;
-    unsigned s1, s2, out, f;
-};
-
-__device__ __forceinline__ DecodedRec decode(const DagRec *p)
+// shared-memory access with 32-bit addresses
+__device__ __forceinline__ uint4 lds128(unsigned a)
 {
-    const uint4 w = *reinterpret_cast<const uint4 *>(p);
-    DecodedRec d;
-    d.c = __hiloint2double((int)w.w, (int)w.z);
-    d.s1 = w.x & 0xffffu;
-    d.s2 = w.x >> 16;
-    d.out = w.y & 0xffffu;
-    d.f = w.y >> 16;
-    return d;
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(a));
+    return v;
+}
+__device__ __forceinline__ unsigned lds32(unsigned a)
+{
+    unsigned v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ double2 lds_d2(unsigned a)
+{
+    double2 v;
+    asm volatile("ld.shared.v2.f64 {%0, %1}, [%2];" : "=d"(v.x), "=d"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts_d2(unsigned a, double x, double y)
+{
+    asm volatile("st.shared.v2.f64 [%0], {%1, %2};" ::"r"(a), "d"(x), "d"(y) : "memory");
 }
 
-template <int APT> struct AtomVec {
-    double v[APT];
-};
+constexpr unsigned DEV_END = 1u << 28, DEV_GLOBAL = 2u << 28, DEV_ENERGY = 4u << 28;
+constexpr unsigned DEV_OUT_MASK = (1u << 28) - 1;
 
-// loads the APT values of this lane from row `row`
-template <int APT>
-__device__ __forceinline__ AtomVec<APT> load_row(const double *rows, unsigned row, int a0, int a1)
+// Runs n consecutive records of one stream.  All records belong to one
+// phase, so a row written here is never read here and record loads may move
+// ahead of stores.
+template <int ATOMS, bool FWD>
+__device__ __forceinline__ void dag_segment(unsigned rec_addr, unsigned rowsA, int n,
+                                            double *acc, double *E, double *adjoint, int npad,
+                                            int natoms, int atom_a)
 {
-    AtomVec<APT> r;
-    const double2 x = *reinterpret_cast<const double2 *>(rows + row * DAG_ATOMS + a0);
-    r.v[0] = x.x;
-    r.v[1] = x.y;
-    if constexpr (APT == 4) {
-        const double2 y = *reinterpret_cast<const double2 *>(rows + row * DAG_ATOMS + a1);
-        r.v[2] = y.x;
-        r.v[3] = y.y;
+    using G = DagGeom<ATOMS>;
+    constexpr unsigned REC_STRIDE = G::SPW * sizeof(DagDevRec);
+    auto rare = [&](unsigned outf, double c) {
+        if constexpr (FWD) {
+            if (outf & DEV_ENERGY) {
+                E[0] = fma(c, acc[0], E[0]);
+                E[1] = fma(c, acc[1], E[1]);
+            }
+        }
+        if (outf & DEV_END) {
+            const unsigned out = outf & DEV_OUT_MASK;
+            if (!FWD && (outf & DEV_GLOBAL)) {
+                if (atom_a < natoms)
+                    adjoint[(size_t)out * npad + atom_a] = acc[0];
+                if (atom_a + 1 < natoms)
+                    adjoint[(size_t)out * npad + atom_a + 1] = acc[1];
+            } else {
+                sts_d2(rowsA + out, acc[0], acc[1]);
+            }
+            acc[0] = 0.0;
+            acc[1] = 0.0;
+        }
+    };
+    int k = 0;
+    for (; k + 4 <= n; k += 4) {
+        uint4 w[4];
+        unsigned of[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            w[u] = lds128(rec_addr + (k + u) * REC_STRIDE);
+            of[u] = lds32(rec_addr + (k + u) * REC_STRIDE + 16);
+        }
+        double2 x[4], y[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            x[u] = lds_d2(rowsA + w[u].x);
+            y[u] = lds_d2(rowsA + w[u].y);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const double c = __hiloint2double((int)w[u].w, (int)w[u].z);
+            acc[0] = fma(c * x[u].x, y[u].x, acc[0]);
+            acc[1] = fma(c * x[u].y, y[u].y, acc[1]);
+            if (of[u])
+                rare(of[u], c);
+        }
     }
-    return r;
+    for (; k < n; ++k) {
+        const uint4 w = lds128(rec_addr + k * REC_STRIDE);
+        const unsigned of = lds32(rec_addr + k * REC_STRIDE + 16);
+        const double2 x = lds_d2(rowsA + w.x), y = lds_d2(rowsA + w.y);
+        const double c = __hiloint2double((int)w.w, (int)w.z);
+        acc[0] = fma(c * x.x, y.x, acc[0]);
+        acc[1] = fma(c * x.y, y.y, acc[1]);
+        if (of)
+            rare(of, c);
+    }
 }
 
-template <int APT>
-__device__ __forceinline__ void store_row(double *rows, unsigned row, int a0, int a1,
-                                          const double *acc)
+__device__ __forceinline__ void cp_async16(unsigned dst, const void *src)
 {
-    *reinterpret_cast<double2 *>(rows + row * DAG_ATOMS + a0) = make_double2(acc[0], acc[1]);
-    if constexpr (APT == 4)
-        *reinterpret_cast<double2 *>(rows + row * DAG_ATOMS + a1) = make_double2(acc[2], acc[3]);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 
-template <int APT>
-__global__ void __launch_bounds__(DagGeom<APT>::THREADS, 1)
-    k_dag(const DagRec *__restrict__ recs, const int *__restrict__ phase_row0, int n_fwd,
+template <int ATOMS>
+__global__ void __launch_bounds__(DagGeom<ATOMS>::THREADS)
+    k_dag(const DagDevRec *__restrict__ recs, const int *__restrict__ phase_row0, int n_fwd,
           int n_rev, int one_row, int zero_row, int nslot, int natoms, int npad,
           const int *__restrict__ types, const double *__restrict__ species_coeffs,
           const double *__restrict__ basic, double *__restrict__ adjoint,
           double *__restrict__ site_energy, int *__restrict__ err_flag)
 {
-    using G = DagGeom<APT>;
+    using G = DagGeom<ATOMS>;
     extern __shared__ __align__(128) unsigned char dsm[];
-    DagRec *ring = reinterpret_cast<DagRec *>(dsm);   // [2][CH][STREAMS]
-    double *rows = reinterpret_cast<double *>(dsm + 2 * DAG_CHUNK_ROWS * DAG_STREAMS *
-                                                        sizeof(DagRec));   // [nrows][16]
-    __shared__ unsigned long long bar[2];
-    __shared__ double epart[DAG_STREAMS][DAG_ATOMS];
+    __shared__ unsigned long long bar[G::WARPS][2];
+    __shared__ double epart[DAG_STREAMS][ATOMS];
     __shared__ int ph0[DAG_MAX_PHASES + 1];
     const int tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
     const int nph = n_fwd + n_rev;
+    unsigned char *ring = dsm + (size_t)warp * 2 * G::SLOT_BYTES;   // this warp's two slots
+    double *rows = reinterpret_cast<double *>(dsm + G::ring_bytes());   // [nrows][ATOMS]
     for (int i = tid; i <= nph; i += blockDim.x)
         ph0[i] = phase_row0[i];
-    const int total_rows = phase_row0[nph];
-    const int nchunks = (total_rows + DAG_CHUNK_ROWS - 1) / DAG_CHUNK_ROWS;
-    auto chunk_bytes = [&](int k) -> unsigned {
-        const int r = min(DAG_CHUNK_ROWS, total_rows - k * DAG_CHUNK_ROWS);
-        return (unsigned)(r * DAG_STREAMS * sizeof(DagRec));
-    };
-    if (tid == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_init(&bar[1], 1);
+    if (lane == 0) {
+        mbar_init(&bar[warp][0], 1);
+        mbar_init(&bar[warp][1], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    __syncthreads();
-    if (tid == 0)
-        for (int k = 0; k < 2 && k < nchunks; ++k)
-            bulk_load(ring + k * DAG_CHUNK_ROWS * DAG_STREAMS,
-                      recs + (size_t)k * DAG_CHUNK_ROWS * DAG_STREAMS, chunk_bytes(k), &bar[k]);
-    const int atom0 = blockIdx.x * DAG_ATOMS;
-    for (int i = tid; i < nslot * DAG_ATOMS; i += blockDim.x) {
-        const int sl = i / DAG_ATOMS, a = i - sl * DAG_ATOMS;
-        const int atom = atom0 + a;
-        rows[i] = atom < natoms ? basic[(size_t)sl * npad + atom] : 0.0;
+    const int atom0 = blockIdx.x * ATOMS;
+    // basic moments: asynchronous 16-byte copies (two atoms each); in a partial
+    // last block the lanes past natoms read row padding (inside the npad
+    // stride) and their results are never written out
+    const unsigned rows_u32 = smem_u32(rows);
+    for (int i = tid; i < nslot * (ATOMS / 2); i += blockDim.x) {
+        const int sl = i / (ATOMS / 2), a = 2 * (i - sl * (ATOMS / 2));
+        cp_async16(rows_u32 + (unsigned)(sl * ATOMS + a) * 8, basic + (size_t)sl * npad + atom0 + a);
     }
-    if (tid < DAG_ATOMS) {
-        rows[one_row * DAG_ATOMS + tid] = 1.0;
-        rows[zero_row * DAG_ATOMS + tid] = 0.0;
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    if (tid < ATOMS) {
+        rows[one_row * ATOMS + tid] = 1.0;
+        rows[zero_row * ATOMS + tid] = 0.0;
     }
     __syncthreads();
-    const int lane = tid & 31, warp = tid >> 5;
     const int g = lane / G::LPS, q = lane - g * G::LPS;
-    const int stream = warp * G::SPW + g;
-    // atoms of this lane: [a0, a0+2) and, for APT 4, [a1, a1+2)
-    int a0, a1;
-    if constexpr (APT == 2) {
-        a0 = 2 * q;
-        a1 = a0;
-    } else {
-        const int h = g & 1;
-        a0 = h * 8 + 2 * q;
-        a1 = (h ^ 1) * 8 + 2 * q;
-    }
-    double E[APT], acc[APT];
-#pragma unroll
-    for (int j = 0; j < APT; ++j) {
-        E[j] = 0.0;
-        acc[j] = 0.0;
-    }
-    auto atom_of = [&](int j) { return atom0 + (j < 2 ? a0 + j : a1 + j - 2); };
-    auto apply = [&](const DecodedRec &d, const AtomVec<APT> &x, const AtomVec<APT> &y) {
-        const bool st = d.f & DAG_START;
-#pragma unroll
-        for (int j = 0; j < APT; ++j)
-            acc[j] = fma(d.c * x.v[j], y.v[j], st ? 0.0 : acc[j]);
-        if (d.f & DAG_END) {
-            if (d.f & DAG_GLOBAL) {
-#pragma unroll
-                for (int j = 0; j < APT; ++j) {
-                    const int at = atom_of(j);
-                    if (at < natoms)
-                        adjoint[(size_t)d.out * npad + at] = acc[j];
-                }
-            } else {
-                store_row<APT>(rows, d.out, a0, a1, acc);
-            }
+    const int a0 = 2 * q;   // this lane's atoms: a0, a0 + 1
+    const unsigned rowsA = rows_u32 + a0 * 8;
+    const unsigned ring_u32 = smem_u32(ring) + g * sizeof(DagDevRec);
+    double E[2] = {0.0, 0.0}, acc[2] = {0.0, 0.0};
+    int kw = 0;   // ring slots consumed by this warp
+    auto phase_src = [&](int ph) {
+        const int rows_p = ph0[ph + 1] - ph0[ph];
+        return recs + (size_t)ph0[ph] * DAG_STREAMS + (size_t)warp * rows_p * G::SPW;
+    };
+    auto issue = [&](int ph, int c, int slot) {
+        const int rows_p = ph0[ph + 1] - ph0[ph];
+        const int r = min(G::CH, rows_p - c * G::CH);
+        bulk_load(ring + slot * G::SLOT_BYTES, phase_src(ph) + (size_t)c * G::CH * G::SPW,
+                  (unsigned)(r * G::SPW * sizeof(DagDevRec)), &bar[warp][slot]);
+    };
+    auto nchunks = [&](int ph) { return (ph0[ph + 1] - ph0[ph] + G::CH - 1) / G::CH; };
+    // lane 0 issues the warp's chunks in consumption order (phase by phase,
+    // skipping empty phases); issue j goes to slot j & 1 and is made only
+    // after chunk j - 2 has been consumed.  Records do not depend on the
+    // phase barriers, so the next phase's chunks are fetched early.
+    int iph = 0, ic = 0, nissued = 0;
+    auto issue_next = [&]() {
+        while (iph < nph && ic >= nchunks(iph)) {
+            ++iph;
+            ic = 0;
         }
-        if (d.f & DAG_ENERGY) {
-#pragma unroll
-            for (int j = 0; j < APT; ++j)
-                E[j] = fma(d.c, acc[j], E[j]);
+        if (iph < nph) {
+            issue(iph, ic, nissued & 1);
+            ++ic;
+            ++nissued;
         }
     };
-    int k = -1, cr0 = 0, cr1 = 0;
-    const DagRec *cb = ring;
+    if (lane == 0) {
+        issue_next();
+        issue_next();
+    }
     for (int ph = 0; ph < nph; ++ph) {
-        int r = ph0[ph];
-        const int rend = ph0[ph + 1];
-        while (r < rend) {
-            if (r >= cr1) {   // next chunk (block-uniform)
-                if (k >= 0) {
-                    __syncthreads();
-                    if (tid == 0 && k + 2 < nchunks) {
-                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                        bulk_load(ring + (k & 1) * DAG_CHUNK_ROWS * DAG_STREAMS,
-                                  recs + (size_t)(k + 2) * DAG_CHUNK_ROWS * DAG_STREAMS,
-                                  chunk_bytes(k + 2), &bar[k & 1]);
-                    }
+        const int rows_p = ph0[ph + 1] - ph0[ph];
+        const int nch = nchunks(ph);
+        const bool fwd = ph < n_fwd;
+        for (int c = 0; c < nch; ++c, ++kw) {
+            const int slot = kw & 1;
+            long it = 0;
+            while (!mbar_try_wait(&bar[warp][slot], (unsigned)((kw >> 1) & 1))) {
+                if (++it > DAG_WAIT_LIMIT) {
+                    *err_flag = 1;
+                    break;
                 }
-                ++k;
-                long it = 0;
-                while (!mbar_try_wait(&bar[k & 1], (unsigned)((k >> 1) & 1))) {
-                    if (++it > DAG_WAIT_LIMIT) {
-                        *err_flag = 1;
-                        break;
-                    }
-                }
-                cb = ring + (k & 1) * DAG_CHUNK_ROWS * DAG_STREAMS + stream;
-                cr0 = k * DAG_CHUNK_ROWS;
-                cr1 = min(total_rows, cr0 + DAG_CHUNK_ROWS);
             }
-            const int seg_end = min(rend, cr1);
-            // two records per step: rows written in a phase are never read in
-            // the same phase, so the second record's loads may run first
-            for (; r + 1 < seg_end; r += 2) {
-                const DecodedRec d0 = decode(cb + (r - cr0) * DAG_STREAMS);
-                const DecodedRec d1 = decode(cb + (r + 1 - cr0) * DAG_STREAMS);
-                const AtomVec<APT> x0 = load_row<APT>(rows, d0.s1, a0, a1);
-                const AtomVec<APT> y0 = load_row<APT>(rows, d0.s2, a0, a1);
-                const AtomVec<APT> x1 = load_row<APT>(rows, d1.s1, a0, a1);
-                const AtomVec<APT> y1 = load_row<APT>(rows, d1.s2, a0, a1);
-                apply(d0, x0, y0);
-                apply(d1, x1, y1);
-            }
-            if (r < seg_end) {
-                const DecodedRec d0 = decode(cb + (r - cr0) * DAG_STREAMS);
-                const AtomVec<APT> x0 = load_row<APT>(rows, d0.s1, a0, a1);
-                const AtomVec<APT> y0 = load_row<APT>(rows, d0.s2, a0, a1);
-                apply(d0, x0, y0);
-                ++r;
+            const int n = min(G::CH, rows_p - c * G::CH);
+            const unsigned rec_addr = ring_u32 + slot * G::SLOT_BYTES;
+            if (fwd)
+                dag_segment<ATOMS, true>(rec_addr, rowsA, n, acc, E, adjoint, npad, natoms,
+                                         atom0 + a0);
+            else
+                dag_segment<ATOMS, false>(rec_addr, rowsA, n, acc, E, adjoint, npad, natoms,
+                                          atom0 + a0);
+            __syncwarp();
+            if (lane == 0) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                issue_next();
             }
         }
         __syncthreads();
         if (ph + 1 == n_fwd) {
-#pragma unroll
-            for (int j = 0; j < APT; ++j)
-                epart[stream][j < 2 ? a0 + j : a1 + j - 2] = E[j];
+            const int stream = warp * G::SPW + g;
+            epart[stream][a0] = E[0];
+            epart[stream][a0 + 1] = E[1];
             __syncthreads();
-            if (tid < DAG_ATOMS && atom0 + tid < natoms) {
+            if (tid < ATOMS && atom0 + tid < natoms) {
                 const int t = types[atom0 + tid];
                 double se = 0.0;
                 if (t >= 0) {
@@ -803,29 +828,65 @@ __global__ void __launch_bounds__(DagGeom<APT>::THREADS, 1)
     }
 }
 
-template <int APT>
-static cudaError_t launch_dag_apt(const DagPlan &plan, const DagRec *recs, const int *phase_row0,
-                                 int nslot, int natoms, int npad, const int *types,
-                                 const double *species_coeffs, const double *basic,
-                                 double *adjoint, double *site_energy, int *err_flag,
-                                 cudaStream_t s)
+// Device records of a plan: warp-major per phase ([phase][warp][row][SPW
+// streams]) for the selected block geometry, with the operand rows turned
+// into shared-memory byte offsets.
+std::vector<DagDevRec> dag_device_records(const DagPlan &plan)
 {
-    const int blocks = (natoms + DAG_ATOMS - 1) / DAG_ATOMS;
-    const size_t smem = 2 * DAG_CHUNK_ROWS * DAG_STREAMS * sizeof(DagRec) +
-                        sizeof(double) * (size_t)plan.nrows * DAG_ATOMS;
-    cudaError_t err = cudaFuncSetAttribute(k_dag<APT>,
+    const int spw = g_dag_atoms == 16 ? DagGeom<16>::SPW : DagGeom<8>::SPW;
+    const unsigned row_bytes = (unsigned)g_dag_atoms * 8;
+    std::vector<DagDevRec> out(plan.recs.size());
+    size_t row0 = 0, o = 0;
+    const int warps = DAG_STREAMS / spw;
+    for (int rows_p : plan.phase_rows) {
+        for (int w = 0; w < warps; ++w)
+            for (int r = 0; r < rows_p; ++r)
+                for (int s = 0; s < spw; ++s) {
+                    const DagRec &in = plan.recs[(row0 + r) * DAG_STREAMS + w * spw + s];
+                    DagDevRec d{};
+                    d.off1 = (in.s12 & 0xffffu) * row_bytes;
+                    d.off2 = (in.s12 >> 16) * row_bytes;
+                    d.c = in.c;
+                    const unsigned flags = in.outf >> 16, out_ = in.outf & 0xffffu;
+                    unsigned f = 0;
+                    if (flags & DAG_END)
+                        f |= DEV_END;
+                    if (flags & DAG_GLOBAL)
+                        f |= DEV_GLOBAL;
+                    if (flags & DAG_ENERGY)
+                        f |= DEV_ENERGY;
+                    d.outf = f ? (f | ((flags & DAG_GLOBAL) ? out_ : out_ * row_bytes)) : 0u;
+                    out[o++] = d;
+                }
+        row0 += rows_p;
+    }
+    return out;
+}
+
+int g_dag_atoms = 16;   // atoms per graph block (8 or 16)
+
+template <int ATOMS>
+static cudaError_t launch_dag_geom(const DagPlan &plan, const DagDevRec *recs,
+                                   const int *phase_row0, int nslot, int natoms, int npad,
+                                   const int *types, const double *species_coeffs,
+                                   const double *basic, double *adjoint, double *site_energy,
+                                   int *err_flag, cudaStream_t s)
+{
+    using G = DagGeom<ATOMS>;
+    const int blocks = (natoms + ATOMS - 1) / ATOMS;
+    const size_t smem = G::ring_bytes() + sizeof(double) * (size_t)plan.nrows * ATOMS;
+    cudaError_t err = cudaFuncSetAttribute(k_dag<ATOMS>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess)
         return err;
-    k_dag<APT><<<blocks, DagGeom<APT>::THREADS, smem, s>>>(
-        recs, phase_row0, plan.n_fwd, plan.n_rev, plan.one_row, plan.zero_row, nslot, natoms, npad,
-        types, species_coeffs, basic, adjoint, site_energy, err_flag);
+    k_dag<ATOMS><<<blocks, G::THREADS, smem, s>>>(recs, phase_row0, plan.n_fwd, plan.n_rev,
+                                                  plan.one_row, plan.zero_row, nslot, natoms,
+                                                  npad, types, species_coeffs, basic, adjoint,
+                                                  site_energy, err_flag);
     return cudaGetLastError();
 }
 
-int g_dag_apt = 2;   // atoms per thread of the graph kernel (2 or 4)
-
-cudaError_t launch_dag(const DagPlan &plan, const DagRec *recs, const int *phase_row0, int nslot,
+cudaError_t launch_dag(const DagPlan &plan, const DagDevRec *recs, const int *phase_row0, int nslot,
                        int natoms, int npad, const int *types, const double *species_coeffs,
                        const double *basic, double *adjoint, double *site_energy, int *err_flag,
                        cudaStream_t s)
@@ -834,11 +895,11 @@ cudaError_t launch_dag(const DagPlan &plan, const DagRec *recs, const int *phase
         return cudaSuccess;
     if (plan.n_fwd + plan.n_rev > DAG_MAX_PHASES)
         return cudaErrorInvalidValue;
-    if (g_dag_apt == 2)
-        return launch_dag_apt<2>(plan, recs, phase_row0, nslot, natoms, npad, types,
-                                 species_coeffs, basic, adjoint, site_energy, err_flag, s);
-    return launch_dag_apt<4>(plan, recs, phase_row0, nslot, natoms, npad, types, species_coeffs,
-                             basic, adjoint, site_energy, err_flag, s);
+    if (g_dag_atoms == 16)
+        return launch_dag_geom<16>(plan, recs, phase_row0, nslot, natoms, npad, types,
+                                   species_coeffs, basic, adjoint, site_energy, err_flag, s);
+    return launch_dag_geom<8>(plan, recs, phase_row0, nslot, natoms, npad, types, species_coeffs,
+                              basic, adjoint, site_energy, err_flag, s);
 }
 
 // ----------------------------------------------------------------------------

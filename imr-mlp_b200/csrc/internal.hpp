@@ -46,10 +46,9 @@ struct alignas(16) DagRec {
     double c;
 };
 enum DagFlags : unsigned {
-    DAG_START = 1,   // acc restarts from this record's product
-    DAG_END = 2,     // store acc to row `out` (or the global adjoint slot)
+    DAG_END = 2,     // store acc to row `out` (or the global adjoint slot), then acc = 0
     DAG_GLOBAL = 4,  // reverse: `out` is a kernel slot of the global adjoint array
-    DAG_ENERGY = 8,  // forward: E += c * acc (the product of this record is zero)
+    DAG_ENERGY = 8,  // forward: E += c * acc before any store (its product is zero)
 };
 inline DagRec make_rec(int s1, int s2, int out, unsigned flags, double c)
 {
@@ -64,16 +63,26 @@ inline DagRec make_rec(int s1, int s2, int out, unsigned flags, double c)
 #define MTPB_DAG_STREAMS 32
 #endif
 #ifndef MTPB_DAG_CHUNK_ROWS
-#define MTPB_DAG_CHUNK_ROWS 32
+#define MTPB_DAG_CHUNK_ROWS 16
 #endif
-constexpr int DAG_ATOMS = 16;                         // atoms per graph block
 constexpr int DAG_STREAMS = MTPB_DAG_STREAMS;         // record streams per block
+
+// Device form of a record (32 bytes): shared-memory byte offsets of the two
+// operand rows, the coefficient, and a word that is zero for plain product
+// records and otherwise holds flags << 28 | out.
+struct alignas(16) DagDevRec {
+    unsigned off1, off2;
+    double c;
+    unsigned outf;
+    unsigned pad[3];
+};
 constexpr int DAG_CHUNK_ROWS = MTPB_DAG_CHUNK_ROWS;   // record rows per shared chunk
 
 struct DagPlan {
     int nrows = 0;           // shared-memory rows (one double per atom each)
     int one_row = 0;         // row holding 1.0
     int zero_row = 0;        // row holding 0.0
+    int scratch_row = 0;     // row receiving stores that nothing reads
     std::vector<int> phase_rows;   // record rows per phase (fwd phases, then reverse)
     int n_fwd = 0, n_rev = 0;
     std::vector<DagRec> recs;      // [sum rows][DAG_STREAMS]
@@ -98,8 +107,9 @@ struct EdgeArgs {
 cudaError_t launch_moments_fwd(int shape, const EdgeArgs &a, double *basic, cudaStream_t s);
 cudaError_t launch_moments_rev(int shape, const EdgeArgs &a, const double *adjoint, double *dx,
                                double *dy, double *dz, cudaStream_t s);
-extern int g_dag_apt;   // graph kernel atoms per thread (2 or 4)
-cudaError_t launch_dag(const DagPlan &plan, const DagRec *recs, const int *phase_row0,
+extern int g_dag_atoms;   // graph kernel atoms per block (8 or 16)
+std::vector<DagDevRec> dag_device_records(const DagPlan &plan);
+cudaError_t launch_dag(const DagPlan &plan, const DagDevRec *recs, const int *phase_row0,
                        int nslot, int natoms, int npad, const int *types,
                        const double *species_coeffs, const double *basic, double *adjoint,
                        double *site_energy, int *err_flag, cudaStream_t s);

@@ -205,8 +205,9 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
     plan = DagPlan{};
     plan.one_row = next++;
     plan.zero_row = next++;
+    plan.scratch_row = next++;
     plan.nrows = next;
-    if ((size_t)plan.nrows * DAG_ATOMS * sizeof(double) > 190 * 1024 || plan.nrows > 65535) {
+    if ((size_t)plan.nrows * 8 * sizeof(double) > 200 * 1024 || plan.nrows > 65535) {
         if (err)
             *err = "moment graph too large for the shared-memory plan (" +
                    std::to_string(plan.nrows) + " rows)";
@@ -225,8 +226,9 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
             for (int x = 0; x < nb; ++x)
                 if (is_scalar[x]) {
                     Item it;
-                    it.recs.push_back(make_rec(row[x], plan.one_row, 0, DAG_START, 1.0));
-                    it.recs.push_back(make_rec(plan.zero_row, plan.zero_row, 0, DAG_ENERGY, scal[x]));
+                    it.recs.push_back(make_rec(row[x], plan.one_row, 0, 0, 1.0));
+                    it.recs.push_back(make_rec(plan.zero_row, plan.zero_row, plan.scratch_row,
+                                               DAG_ENERGY | DAG_END, scal[x]));
                     items.push_back(std::move(it));
                 }
         }
@@ -239,18 +241,16 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
             const auto &rl = rules_of[x];
             for (size_t k = 0; k < rl.size(); ++k) {
                 const int *r = &m.times[4 * rl[k]];
-                unsigned flags = 0;
-                int out = 0;
-                if (k == 0)
-                    flags |= DAG_START;
-                if (k + 1 == rl.size() && is_operand[x]) {
-                    flags |= DAG_END;
-                    out = row[x];
-                }
-                it.recs.push_back(make_rec(row[r[0]], row[r[1]], out, flags, (double)r[2]));
+                it.recs.push_back(make_rec(row[r[0]], row[r[1]], 0, 0, (double)r[2]));
             }
+            // the item ends with its energy term (scalars) and the store of
+            // the product moment (operands; otherwise a scratch row)
+            const int out = is_operand[x] ? row[x] : plan.scratch_row;
             if (is_scalar[x])
-                it.recs.push_back(make_rec(plan.zero_row, plan.zero_row, 0, DAG_ENERGY, scal[x]));
+                it.recs.push_back(make_rec(plan.zero_row, plan.zero_row, out,
+                                           DAG_ENERGY | DAG_END, scal[x]));
+            else
+                it.recs.back().outf = (unsigned)out | ((unsigned)DAG_END << 16);
             items.push_back(std::move(it));
         }
         emit_phase(items, plan);
@@ -281,7 +281,6 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
         }
         if (it.recs.empty())
             it.recs.push_back(make_rec(plan.zero_row, plan.zero_row, 0, 0, 0.0));
-        it.recs.front().outf |= (unsigned)DAG_START << 16;
         const unsigned old = it.recs.back().outf >> 16;
         it.recs.back().outf = (unsigned)out | ((old | DAG_END | flags) << 16);
         return it;
@@ -306,7 +305,7 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
             if (!slot_used[s]) {
                 Item it;
                 it.recs.push_back(make_rec(plan.zero_row, plan.zero_row, s,
-                                           DAG_START | DAG_END | DAG_GLOBAL, 0.0));
+                                           DAG_END | DAG_GLOBAL, 0.0));
                 items.push_back(std::move(it));
             }
         emit_phase(items, plan);

@@ -9,7 +9,7 @@ import pytest
 from conftest import load_model
 from mtpb200 import configs
 
-START, END, GLOBAL, ENERGY = 1, 2, 4, 8
+END, GLOBAL, ENERGY = 2, 4, 8
 
 
 def program(model):
@@ -52,19 +52,20 @@ def interpret(prog, basic_slots, species_part):
     r = 0
     energy = None
     for ph, nrow in enumerate(prog["phase_rows"]):
+        acc[:] = 0.0
         for _ in range(nrow):
             writes = []
             for s in range(S):
                 c = coef[r, s]
-                prod = c * rows[s1[r, s]] * rows[s2[r, s]]
-                acc[s] = prod if fl[r, s] & START else acc[s] + prod
+                acc[s] = acc[s] + c * rows[s1[r, s]] * rows[s2[r, s]]
+                if fl[r, s] & ENERGY:
+                    E[s] += c * acc[s]
                 if fl[r, s] & END:
                     if fl[r, s] & GLOBAL:
                         adj[out[r, s]] = acc[s]
                     else:
                         writes.append((out[r, s], acc[s].copy()))
-                if fl[r, s] & ENERGY:
-                    E[s] += c * acc[s]
+                    acc[s] = 0.0
             for o, v in writes:
                 rows[o] = v
             r += 1
