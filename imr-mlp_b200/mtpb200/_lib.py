@@ -91,6 +91,7 @@ SIGNATURES = [
                                       C.POINTER(EfsOutput)]),
     ("mtpb_efs_csr", C.c_int, [C.c_void_p, C.POINTER(CsrRequest), C.c_int]),
     ("mtpb_efs_lammps", C.c_int, [C.c_void_p, C.POINTER(LammpsRequest)]),
+    ("mtpb_efs_csr_noalloc", C.c_int, [C.c_void_p, C.POINTER(CsrRequest)]),
     ("mtpb_loss_grad", C.c_int, [C.c_void_p, C.POINTER(Labels), C.POINTER(LossWeights), C.c_int,
                                  C.c_int, _dp, _dp, _dp]),
     ("mtpb_last_timings", C.c_int, [C.c_void_p, _dp]),

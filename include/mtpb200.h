@@ -183,6 +183,25 @@ typedef struct mtpb_csr_request {
  * linear model. */
 int mtpb_efs_csr(mtpb_context *ctx, const mtpb_csr_request *req, int memory);
 
+/* The CSR request of mtpb_efs_csr for small systems, without any device
+ * allocation: for callers that cannot call cudaMalloc while they run, such as
+ * an MD engine or plug-in host that has already reserved the GPU's memory for
+ * its own pool, or a real-time loop that must never enter the allocator.  It
+ * has no counterpart in the reference.
+ *
+ * All arrays of `req` are device memory on the context's device; the context
+ * must exist already (mtpb_create allocates the model's device data once).
+ * Per-call scratch lives in one fixed device array inside the library (about
+ * 9.6 MB, resident on every GPU that loads the library until exit), which
+ * limits a call to 1024 centres, 4096 atoms including ghosts, 65536 edges and
+ * models with at most 320 basic-moment slots (level 20 and below); larger
+ * requests fail with MTPB_ERR_ARGUMENT / MTPB_ERR_UNSUPPORTED.  The first call
+ * on a device looks up the array's device address; make that first call before
+ * any stream capture.  Every call uses the same array, so calls that overlap on
+ * the GPU (from two threads or two contexts on one device) race; the call
+ * returns after its work has completed. */
+int mtpb_efs_csr_noalloc(mtpb_context *ctx, const mtpb_csr_request *req);
+
 /* LAMMPS pair-style request (MTPGpuComputeRequest, mtp_gpu_direct.h:326-450;
  * PairMLIPGpuDirect::compute, LAMMPS/USER-MLIP/pair_MLIP_gpu_direct.cpp:540-640):
  * full neighbour list, newton on, forces added to f for local and ghost
