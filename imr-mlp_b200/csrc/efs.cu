@@ -26,7 +26,8 @@
 namespace mtpb {
 
 constexpr int KS = 8;     // edge slots staged per chunk
-constexpr int STR = 33;   // padded row stride of the staging arrays (doubles)
+constexpr int STR = 36;   // row stride of the staging arrays (doubles): conflict-free
+                          // writes from (lane, slot) pairs and reads by lane
 
 template <class S> struct ShapeCfg;
 template <> struct ShapeCfg<ShapeS1> { static constexpr int NW = 2; };
@@ -363,10 +364,11 @@ __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, 
             part[(2 * KS + k) * 32 + lane] = fma(zh, t, Gz * rinv);
         }
         __syncthreads();
-        // sum the warps' shares in warp order and store per edge
+        // sum the warps' shares in warp order and store per edge (thread ->
+        // (slot, lane) so that the shared reads are lane-contiguous)
         for (int item = threadIdx.x; item < 32 * KS; item += NW * 32) {
-            const int ln = item / KS;
-            const int k = item - ln * KS;
+            const int k = item >> 5;
+            const int ln = item & 31;
             const int at = atom0 + ln;
             if (k >= kend || at >= p.natoms)
                 continue;
@@ -1020,20 +1022,33 @@ __global__ void k_struct_reduce(int nstruct, const int *__restrict__ struct_seg0
                                 const double *__restrict__ partials, double *__restrict__ energy,
                                 double *__restrict__ virial)
 {
-    const int s = blockIdx.x * blockDim.x + threadIdx.x;
-    if (s >= nstruct)
-        return;
+    // one block per structure; fixed-order tree over its segments
+    __shared__ double sh[10][128];
+    const int s = blockIdx.x;
     double v[10] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
-    for (int g = struct_seg0[s]; g < struct_seg0[s + 1]; ++g)
+    for (int g = struct_seg0[s] + threadIdx.x; g < struct_seg0[s + 1]; g += blockDim.x)
 #pragma unroll
         for (int q = 0; q < 10; ++q)
             v[q] += partials[(size_t)g * 10 + q];
-    if (energy)
-        energy[s] = v[0];
-    if (virial)
 #pragma unroll
-        for (int q = 0; q < 9; ++q)
-            virial[(size_t)s * 9 + q] = v[1 + q];
+    for (int q = 0; q < 10; ++q)
+        sh[q][threadIdx.x] = v[q];
+    __syncthreads();
+    for (int st = blockDim.x / 2; st > 0; st >>= 1) {
+        if (threadIdx.x < st)
+#pragma unroll
+            for (int q = 0; q < 10; ++q)
+                sh[q][threadIdx.x] += sh[q][threadIdx.x + st];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        if (energy)
+            energy[s] = sh[0][0];
+        if (virial)
+#pragma unroll
+            for (int q = 0; q < 9; ++q)
+                virial[(size_t)s * 9 + q] = sh[1 + q][0];
+    }
 }
 
 cudaError_t launch_struct_reduce(int nstruct, const int *struct_seg0, const double *partials,
@@ -1041,9 +1056,7 @@ cudaError_t launch_struct_reduce(int nstruct, const int *struct_seg0, const doub
 {
     if (nstruct == 0)
         return cudaSuccess;
-    const int threads = 128;
-    k_struct_reduce<<<(nstruct + threads - 1) / threads, threads, 0, s>>>(
-        nstruct, struct_seg0, partials, energy, virial);
+    k_struct_reduce<<<nstruct, 128, 0, s>>>(nstruct, struct_seg0, partials, energy, virial);
     return cudaGetLastError();
 }
 
