@@ -122,6 +122,7 @@ static int upload_model(mtpb_context *c)
                              cudaMemcpyHostToDevice, c->stream),
              "upload graph phases");
     CUDA_TRY(cudaStreamSynchronize(c->stream), "model upload");
+    c->train.ready = false;   // the gradient program follows the new records
     return MTPB_OK;
 }
 
@@ -540,6 +541,7 @@ int mtpb_build_neighbors(mtpb_context *c, const mtpb_structures *in, int memory)
              "upload segments");
     CUDA_TRY(cudaStreamSynchronize(c->stream), "neighbour build");
     c->have_list = true;
+    c->edge_epoch++;
     c->nb_built_this_call = true;
     // struct ids, wrap/bin, 3 scans (2 kernels each), cell fill and sort,
     // count, fill, in-edge count, fill and sort
@@ -700,6 +702,7 @@ int mtpb_efs_structures(mtpb_context *c, const mtpb_structures *in, int memory,
                                const_cast<double *>(c->nb.rx), const_cast<double *>(c->nb.ry),
                                const_cast<double *>(c->nb.rz), c->stream),
                  "refresh edge vectors");
+        c->edge_epoch++;
         c->nb_built_this_call = true;   // ev[0] marks the refresh
         c->pending_launches = 1;
     }

@@ -13,12 +13,21 @@
 #include <string>
 #include <vector>
 
+struct mtpb_context;
+
 namespace mtpb {
 
 // Device-resident state of the training evaluator (training.cu).
 struct TrainingState {
-    bool ready = false;
+    bool ready = false;               // gradient program uploaded for the model
+    DagDevRec *recs = nullptr;        // dual-graph records (grad.cu layout)
+    std::vector<DagDevRec> h_recs;
+    int *moment_energy = nullptr;     // moment coefficient -> energy-moment index
+    long bucket_epoch = -1;           // edge_epoch the pair buckets belong to
+    int *perm = nullptr;              // edges sorted by species pair
+    long *bounds = nullptr;           // bucket start positions [K*K+2]
 };
+int upload_training_program(mtpb_context *c);
 
 int fail(int status, const std::string &msg);
 int cuda_fail(cudaError_t e, const char *where);
@@ -72,6 +81,7 @@ struct mtpb_context {
     int launches = 0;
     int pending_launches = 0;   // neighbour build / refresh launches of this call
     bool have_efs = false;
+    long edge_epoch = 0;   // advanced whenever the edge list or its vectors change
     mtpb::TrainingState train;
 };
 

@@ -19,23 +19,12 @@
 // the reference's per-edge Jacobian (nb x n_e x 3 doubles per site) by
 // registers.
 #include "internal.hpp"
-#include "shapes.cuh"
+#include "moments.cuh"
+#include "dag.cuh"
 
 #include <cstdio>
 
 namespace mtpb {
-
-constexpr int KS = 8;     // edge slots staged per chunk
-constexpr int STR = 36;   // row stride of the staging arrays (doubles): conflict-free
-                          // writes from (lane, slot) pairs and reads by lane
-
-template <class S> struct ShapeCfg;
-template <> struct ShapeCfg<ShapeS1> { static constexpr int NW = 2; };
-template <> struct ShapeCfg<ShapeS2> { static constexpr int NW = 2; };
-template <> struct ShapeCfg<ShapeL16> { static constexpr int NW = 4; };
-template <> struct ShapeCfg<ShapeL20> { static constexpr int NW = 8; };
-template <> struct ShapeCfg<ShapeL24> { static constexpr int NW = 16; };
-template <> struct ShapeCfg<ShapePS> { static constexpr int NW = 4; };
 
 // staging arrays: 0 xhat, 1 yhat, 2 zhat, 3 1/r, 4.. f_mu, 4+NMU.. f'_mu
 template <class S, bool REV> constexpr int stage_rows()
@@ -60,11 +49,6 @@ struct StageView {
     const PairParams *pairs;
     const double *radial;  // [K*K][NMU][R]
 };
-
-__device__ __forceinline__ double &SV(double *st, int row, int k, int lane)
-{
-    return st[(row * KS + k) * STR + lane];
-}
 
 // Computes the per-edge quantities of one chunk of edge slots for the 32
 // atoms of this block.  Every thread of the block takes part.
@@ -154,16 +138,6 @@ __device__ __forceinline__ void stage_chunk(const EdgeArgs &p, const StageView &
                 SV(v.st, 4 + NMU + m, k, lane) = fp[m];
         }
     }
-}
-
-// accumulator offset of monomial a within a chain (sum of channel counts of
-// the lower powers)
-template <class S> constexpr int chain_acc_off(int s, int a)
-{
-    int o = 0;
-    for (int aa = 0; aa < a; ++aa)
-        o += S::cnt(aa + s);
-    return o;
 }
 
 // ----------------------------------------------------------------------------
@@ -551,89 +525,6 @@ cudaError_t launch_group_maxdeg(int natoms, const int *offsets, int *group_maxde
 //   END:    GLOBAL ? adjoint[out][atom] = acc : row[out] = acc
 //   ENERGY: E += c * acc          (its own product is 0 * 0)
 // ----------------------------------------------------------------------------
-__device__ __forceinline__ unsigned smem_u32(const void *p)
-{
-    return (unsigned)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ void mbar_init(unsigned long long *bar, unsigned count)
-{
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
-                 : "memory");
-}
-
-__device__ __forceinline__ void bulk_load(void *dst, const void *src, unsigned bytes,
-                                          unsigned long long *bar)
-{
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-                 "r"(bytes)
-                 : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], "
-                 "%2, [%3];" ::"r"(smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(unsigned long long *bar, unsigned parity)
-{
-    unsigned ok;
-    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-                 " selp.u32 %0, 1, 0, p;\n}\n"
-                 : "=r"(ok)
-                 : "r"(smem_u32(bar)), "r"(parity)
-                 : "memory");
-    return ok != 0;
-}
-
-constexpr int DAG_MAX_PHASES = 64;
-constexpr long DAG_WAIT_LIMIT = 1L << 22;   // bounded wait: sets the error flag
-
-// Geometry: ATOMS atoms per block, two atoms per lane; a record stream is
-// served by LPS = ATOMS/2 lanes, a warp serves SPW = 32/LPS streams and the
-// block DAG_STREAMS streams.  Records are laid out warp-major per phase
-// ([phase][warp][row][SPW streams], see dag_warp_major) so that every warp
-// streams its own contiguous records through a private double-buffered ring
-// filled by TMA bulk copies: warps only meet at the phase barriers.
-template <int ATOMS> struct DagGeom {
-    static constexpr int APT = 2;
-    static constexpr int LPS = ATOMS / APT;
-    static constexpr int SPW = 32 / LPS;
-    static constexpr int WARPS = DAG_STREAMS / SPW;
-    static constexpr int THREADS = WARPS * 32;
-    static constexpr int CH = DAG_CHUNK_ROWS;                // rows per ring slot
-    static constexpr unsigned SLOT_BYTES = CH * SPW * sizeof(DagDevRec);
-    static constexpr size_t ring_bytes() { return (size_t)WARPS * 2 * SLOT_BYTES; }
-};
-
-// shared-memory access with 32-bit addresses
-__device__ __forceinline__ uint4 lds128(unsigned a)
-{
-    uint4 v;
-    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "r"(a));
-    return v;
-}
-__device__ __forceinline__ unsigned lds32(unsigned a)
-{
-    unsigned v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
-    return v;
-}
-__device__ __forceinline__ double2 lds_d2(unsigned a)
-{
-    double2 v;
-    asm volatile("ld.shared.v2.f64 {%0, %1}, [%2];" : "=d"(v.x), "=d"(v.y) : "r"(a));
-    return v;
-}
-__device__ __forceinline__ void sts_d2(unsigned a, double x, double y)
-{
-    asm volatile("st.shared.v2.f64 [%0], {%1, %2};" ::"r"(a), "d"(x), "d"(y) : "memory");
-}
-
-constexpr unsigned DEV_END = 1u << 28, DEV_GLOBAL = 2u << 28, DEV_ENERGY = 4u << 28;
-constexpr unsigned DEV_OUT_MASK = (1u << 28) - 1;
-
 // Runs n consecutive records of one stream.  All records belong to one
 // phase, so a row written here is never read here and record loads may move
 // ahead of stores.
@@ -699,11 +590,6 @@ __device__ __forceinline__ void dag_segment(unsigned rec_addr, unsigned rowsA, i
         if (of)
             rare(of, c);
     }
-}
-
-__device__ __forceinline__ void cp_async16(unsigned dst, const void *src)
-{
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 
 template <int ATOMS>

@@ -86,6 +86,10 @@ struct DagPlan {
     std::vector<int> phase_rows;   // record rows per phase (fwd phases, then reverse)
     int n_fwd = 0, n_rev = 0;
     std::vector<DagRec> recs;      // [sum rows][DAG_STREAMS]
+    // training: index into energy_moments of the scalar moment an ENERGY
+    // record closes (-1 for every other record), parallel to recs
+    std::vector<int> rec_energy;
+    std::vector<int> energy_moments;   // moment ids with a scalar coefficient
 };
 
 // Edge-kernel parameters (device pointers).
@@ -126,5 +130,19 @@ cudaError_t launch_segment_reduce(int nseg, const int *seg_begin, const int *seg
 cudaError_t launch_struct_reduce(int nstruct, const int *struct_seg0, const double *partials,
                                  double *energy, double *virial, cudaStream_t s);
 
+// training gradient kernels (grad.cu)
+cudaError_t launch_moments_tangent(int shape, const EdgeArgs &a, const double *wx,
+                                   const double *wy, const double *wz, double *tangent,
+                                   cudaStream_t s);
+cudaError_t launch_edge_grad(int shape, const EdgeArgs &a, const double *wx, const double *wy,
+                             const double *wz, const double *adjoint, const double *adjoint2,
+                             double *uv, cudaStream_t s);
+std::vector<DagDevRec> dag_grad_records(const DagPlan &plan);
+size_t dag_grad_smem_bytes(const DagPlan &plan);
+int dag_grad_grid(const DagPlan &plan, int natoms);
+cudaError_t launch_dag_grad(const DagPlan &plan, const DagDevRec *recs, const int *phase_row0,
+                            int grid, int nslot, int natoms, int npad, const double *basic,
+                            const double *tangent, const double *dlde_atom, double *adjoint2,
+                            double *energy_partials, int *err_flag, cudaStream_t s);
 
 } // namespace mtpb

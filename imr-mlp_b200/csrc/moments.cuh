@@ -1,0 +1,37 @@
+// moments.cuh -- constants and helpers shared by the moment kernels of the
+// energy/force path (efs.cu) and of the training path (grad.cu): staging
+// geometry, warps per basis shape, and the accumulator layout of a chain.
+#pragma once
+
+#include "shapes.cuh"
+
+namespace mtpb {
+
+constexpr int KS = 8;     // edge slots staged per chunk
+constexpr int STR = 36;   // row stride of the staging arrays (doubles): conflict-free
+                          // writes from (lane, slot) pairs and reads by lane
+
+template <class S> struct ShapeCfg;
+template <> struct ShapeCfg<ShapeS1> { static constexpr int NW = 2; };
+template <> struct ShapeCfg<ShapeS2> { static constexpr int NW = 2; };
+template <> struct ShapeCfg<ShapeL16> { static constexpr int NW = 4; };
+template <> struct ShapeCfg<ShapeL20> { static constexpr int NW = 8; };
+template <> struct ShapeCfg<ShapeL24> { static constexpr int NW = 16; };
+template <> struct ShapeCfg<ShapePS> { static constexpr int NW = 4; };
+
+__device__ __forceinline__ double &SV(double *st, int row, int k, int lane)
+{
+    return st[(row * KS + k) * STR + lane];
+}
+
+// accumulator offset of monomial a within a chain (sum of channel counts of
+// the lower powers)
+template <class S> constexpr int chain_acc_off(int s, int a)
+{
+    int o = 0;
+    for (int aa = 0; aa < a; ++aa)
+        o += S::cnt(aa + s);
+    return o;
+}
+
+} // namespace mtpb

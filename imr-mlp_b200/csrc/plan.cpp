@@ -133,6 +133,7 @@ namespace {
 
 struct Item {
     std::vector<DagRec> recs;
+    int energy = -1;   // energy_moments index of the item's ENERGY record
 };
 
 // Longest-processing-time assignment of items to DAG_STREAMS streams, then
@@ -145,18 +146,24 @@ void emit_phase(std::vector<Item> &items, DagPlan &plan)
         return items[a].recs.size() > items[b].recs.size();
     });
     std::vector<std::vector<DagRec>> streams(DAG_STREAMS);
+    std::vector<std::vector<int>> energy(DAG_STREAMS);
     std::vector<size_t> load(DAG_STREAMS, 0);
     for (int idx : order) {
         int s = (int)(std::min_element(load.begin(), load.end()) - load.begin());
-        for (const DagRec &r : items[idx].recs)
+        for (const DagRec &r : items[idx].recs) {
             streams[s].push_back(r);
+            energy[s].push_back(((r.outf >> 16) & DAG_ENERGY) ? items[idx].energy : -1);
+        }
         load[s] += items[idx].recs.size();
     }
     size_t len = *std::max_element(load.begin(), load.end());
     const DagRec pad = make_rec(plan.zero_row, plan.zero_row, 0, 0, 0.0);
     for (size_t r = 0; r < len; ++r)
-        for (int s = 0; s < DAG_STREAMS; ++s)
-            plan.recs.push_back(r < streams[s].size() ? streams[s][r] : pad);
+        for (int s = 0; s < DAG_STREAMS; ++s) {
+            const bool real = r < streams[s].size();
+            plan.recs.push_back(real ? streams[s][r] : pad);
+            plan.rec_energy.push_back(real ? energy[s][r] : -1);
+        }
     plan.phase_rows.push_back((int)len);
 }
 
@@ -191,6 +198,12 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
         scal[m.mapping[s]] += m.moment[s];
         is_scalar[m.mapping[s]] = 1;
     }
+    std::vector<int> energy_index(M, -1), energy_moments;
+    for (int x = 0; x < M; ++x)
+        if (is_scalar[x]) {
+            energy_index[x] = (int)energy_moments.size();
+            energy_moments.push_back(x);
+        }
     // rows: kernel slots, operand targets, their adjoints, constants
     std::vector<int> row(M, -1), adjrow(M, -1);
     for (int i = 0; i < nb; ++i)
@@ -207,6 +220,7 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
     plan.zero_row = next++;
     plan.scratch_row = next++;
     plan.nrows = next;
+    plan.energy_moments = energy_moments;
     if ((size_t)plan.nrows * 8 * sizeof(double) > 200 * 1024 || plan.nrows > 65535) {
         if (err)
             *err = "moment graph too large for the shared-memory plan (" +
@@ -229,6 +243,7 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
                     it.recs.push_back(make_rec(row[x], plan.one_row, 0, 0, 1.0));
                     it.recs.push_back(make_rec(plan.zero_row, plan.zero_row, plan.scratch_row,
                                                DAG_ENERGY | DAG_END, scal[x]));
+                    it.energy = energy_index[x];
                     items.push_back(std::move(it));
                 }
         }
@@ -246,9 +261,11 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
             // the item ends with its energy term (scalars) and the store of
             // the product moment (operands; otherwise a scratch row)
             const int out = is_operand[x] ? row[x] : plan.scratch_row;
-            if (is_scalar[x])
+            if (is_scalar[x]) {
                 it.recs.push_back(make_rec(plan.zero_row, plan.zero_row, out,
                                            DAG_ENERGY | DAG_END, scal[x]));
+                it.energy = energy_index[x];
+            }
             else
                 it.recs.back().outf = (unsigned)out | ((unsigned)DAG_END << 16);
             items.push_back(std::move(it));

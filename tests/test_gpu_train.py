@@ -1,0 +1,171 @@
+"""Loss and coefficient gradient on the GPU (mtpb_loss_grad) against the C
+restatement of Trainer_MTP::AddLossGard + PotMTP::AccumulateEFSCombinationGard
+(oracle_loss_grad), the committed gradient fixture and central differences of
+the GPU loss itself.
+
+Tolerances: loss and metrics 1e-10 relative; gradient 1e-9 of its largest
+entry (the device sums a factorised form of the reference's Jacobian
+contraction, in a different order)."""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, load_model
+from mtpb200 import configs
+
+pytestmark = pytest.mark.gpu
+
+TOL_LOSS = 1e-10
+TOL_GRAD = 1e-9
+WEIGHTS = (1.0, 0.01, 0.001, 1.0, 0.0, 1.0)
+
+
+def _batch(structures):
+    from mtpb200 import StructureBatch
+    return StructureBatch.from_structures(structures)
+
+
+def _oracle_grad(oracle, model, structures, te, tf, ts, weights=WEIGHTS):
+    from oracle import concat_lists
+    offs, _, _, _, types = configs.batch(structures)
+    lists = [oracle.neighbors(s["cell"], s["pbc"], s["positions"], model.cutoff)
+             for s in structures]
+    nl = concat_lists(lists, offs)
+    return oracle.loss_grad(model, offs, types, nl, te, tf, ts, weights)
+
+
+def _labels(structures, seed):
+    rng = np.random.default_rng(seed)
+    n = sum(len(s["types"]) for s in structures)
+    return (rng.normal(0, 1, len(structures)), rng.normal(0, 0.1, (n, 3)),
+            rng.normal(0, 0.5, (len(structures), 9)))
+
+
+def _gpu_grad(model, structures, te, tf, ts, weights=WEIGHTS, norm_count=0):
+    from mtpb200 import MTPGpuDirect
+    with MTPGpuDirect(model, 0) as gpu:
+        gpu.build_neighbors(_batch(structures))
+        return gpu.loss_grad(te, tf, ts, weights, norm_count)
+
+
+def _close(got, ref):
+    loss, metrics, grad = got
+    rloss, rmetrics, rgrad = ref
+    assert abs(loss - rloss) <= TOL_LOSS * max(1.0, abs(rloss))
+    assert np.all(np.abs(metrics - rmetrics) <= TOL_LOSS * np.maximum(1.0, np.abs(rmetrics)))
+    scale = max(1.0, np.max(np.abs(rgrad)))
+    err = np.max(np.abs(grad - rgrad))
+    assert err <= TOL_GRAD * scale, (err, scale, int(np.argmax(np.abs(grad - rgrad))))
+
+
+def _mixed(n, seed, K):
+    sts = configs.config2(n, seed=seed)
+    for s in sts:
+        s["types"] = np.minimum(s["types"], K - 1).astype(np.int32)
+    return sts
+
+
+def test_gradient_matches_golden_fixture(model_l16):
+    g = np.load(os.path.join(GOLDEN, "golden_grad_l16.npz"))
+    offs = g["atom_offsets"]
+    sts = [dict(cell=g["cells"][s].reshape(3, 3), pbc=np.ones(3, np.int32),
+                positions=g["positions"][offs[s]:offs[s + 1]],
+                types=g["types"][offs[s]:offs[s + 1]]) for s in range(len(offs) - 1)]
+    got = _gpu_grad(model_l16, sts, g["target_energy"], g["target_forces"], g["target_stress"])
+    _close(got, (float(g["loss"]), g["metrics"], g["grad"]))
+
+
+@pytest.mark.parametrize("name,K", [("l16_k2.mtp", 2), ("l20_k3.mtp", 3),
+                                    ("many_body_k3.mtp", 3), ("pair_k1.mtp", 1)])
+def test_gradient_matches_oracle(oracle, name, K):
+    m = load_model(name)
+    sts = _mixed(3, 61, m.species_count)
+    te, tf, ts = _labels(sts, 7)
+    _close(_gpu_grad(m, sts, te, tf, ts), _oracle_grad(oracle, m, sts, te, tf, ts))
+
+
+@pytest.mark.parametrize("weights", [(1.0, 0.0, 0.0, 1.0, 0.0, 1.0),
+                                     (0.0, 1.0, 0.0, 1.0, 0.0, 1.0),
+                                     (0.0, 0.0, 1.0, 1.0, 0.0, 1.0),
+                                     (2.0, 0.03, 0.5, 2.0, 1.0, 0.5)])
+def test_gradient_weight_variants(oracle, model_l16, weights):
+    sts = _mixed(2, 62, 2)
+    te, tf, ts = _labels(sts, 8)
+    _close(_gpu_grad(model_l16, sts, te, tf, ts, weights),
+           _oracle_grad(oracle, model_l16, sts, te, tf, ts, weights))
+
+
+def test_gradient_missing_labels(oracle, model_l16):
+    """A NULL label array drops that term for every structure."""
+    sts = _mixed(2, 63, 2)
+    te, tf, ts = _labels(sts, 9)
+    _close(_gpu_grad(model_l16, sts, te, None, ts), _oracle_grad(oracle, model_l16, sts, te,
+                                                                 None, ts))
+    _close(_gpu_grad(model_l16, sts, None, tf, None), _oracle_grad(oracle, model_l16, sts, None,
+                                                                   tf, None))
+
+
+def test_gradient_norm_count_and_determinism(model_l16):
+    sts = _mixed(3, 64, 2)
+    te, tf, ts = _labels(sts, 10)
+    from mtpb200 import MTPGpuDirect
+    with MTPGpuDirect(model_l16, 0) as gpu:
+        gpu.build_neighbors(_batch(sts))
+        a = gpu.loss_grad(te, tf, ts, WEIGHTS)
+        b = gpu.loss_grad(te, tf, ts, WEIGHTS)
+        c = gpu.loss_grad(te, tf, ts, WEIGHTS, norm_count=12)
+    assert a[0] == b[0] and np.array_equal(a[2], b[2]) and np.array_equal(a[1], b[1])
+    assert np.allclose(c[2] * 12, a[2] * 3, rtol=1e-14, atol=0)
+    assert np.array_equal(c[1], a[1])   # metrics are not normalised
+
+
+def test_gradient_follows_coefficients_and_positions(oracle, model_l16):
+    """The gradient program follows mtpb_update_coefficients, and the pair
+    buckets follow a position update through the reuse path."""
+    from mtpb200 import MTPGpuDirect
+    sts = _mixed(2, 65, 2)
+    te, tf, ts = _labels(sts, 11)
+    m2 = configs.seeded_coefficients(model_l16, 99)
+    with MTPGpuDirect(model_l16, 0) as gpu:
+        batch = _batch(sts)
+        gpu.build_neighbors(batch)
+        gpu.loss_grad(te, tf, ts, WEIGHTS)
+        gpu.set_coefficients(m2.coefficients())
+        _close(gpu.loss_grad(te, tf, ts, WEIGHTS), _oracle_grad(oracle, m2, sts, te, tf, ts))
+        rng = np.random.default_rng(3)
+        moved = [dict(s, positions=s["positions"] + rng.normal(0, 0.01, s["positions"].shape))
+                 for s in sts]
+        out = dict(energy=np.zeros(len(sts)), forces=np.zeros((batch.n_atoms, 3)),
+                   stress=np.zeros((len(sts), 9)))
+        gpu.efs_structures(_batch(moved), reuse_neighbors=True, out=out)
+        _close(gpu.loss_grad(te, tf, ts, WEIGHTS), _oracle_grad(oracle, m2, moved, te, tf, ts))
+
+
+def test_gradient_central_differences(model_l16):
+    """Directional derivatives of the GPU loss along radial, species and
+    moment directions against the GPU gradient (central differences,
+    step 1e-6 relative; unitest/ut_mtp_cpu_training.cpp:46-55 recipe)."""
+    from mtpb200 import MTPGpuDirect
+    sts = _mixed(2, 66, 2)
+    te, tf, ts = _labels(sts, 12)
+    m = model_l16
+    c0 = m.coefficients()
+    r = m.radial_coeffs_count
+    K = m.species_count
+    rng = np.random.default_rng(13)
+    with MTPGpuDirect(m, 0) as gpu:
+        gpu.build_neighbors(_batch(sts))
+        _, _, g = gpu.loss_grad(te, tf, ts, WEIGHTS)
+        for lo, hi in ((0, r), (r, r + K), (r + K, len(c0))):
+            v = np.zeros_like(c0)
+            v[lo:hi] = rng.normal(0, 1, hi - lo)
+            h = 1e-6 * max(1.0, np.max(np.abs(c0[lo:hi])))
+            gpu.set_coefficients(c0 + h * v)
+            lp = gpu.loss_grad(te, tf, ts, WEIGHTS)[0]
+            gpu.set_coefficients(c0 - h * v)
+            lm = gpu.loss_grad(te, tf, ts, WEIGHTS)[0]
+            gpu.set_coefficients(c0)
+            fd = (lp - lm) / (2 * h)
+            an = float(g @ v)
+            assert abs(fd - an) <= 3e-5 + 3e-6 * abs(an), (lo, fd, an)
