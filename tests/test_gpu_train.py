@@ -72,7 +72,9 @@ def test_gradient_matches_golden_fixture(model_l16):
     sts = [dict(cell=g["cells"][s].reshape(3, 3), pbc=np.ones(3, np.int32),
                 positions=g["positions"][offs[s]:offs[s + 1]],
                 types=g["types"][offs[s]:offs[s + 1]]) for s in range(len(offs) - 1)]
-    got = _gpu_grad(model_l16, sts, g["target_energy"], g["target_forces"], g["target_stress"])
+    # the fixture was made with the weights (1, 0.01, 0.0001; powers 1, 0, 1)
+    got = _gpu_grad(model_l16, sts, g["target_energy"], g["target_forces"], g["target_stress"],
+                    (1.0, 0.01, 0.0001, 1.0, 0.0, 1.0))
     _close(got, (float(g["loss"]), g["metrics"], g["grad"]))
 
 
@@ -122,13 +124,15 @@ def test_gradient_norm_count_and_determinism(model_l16):
 
 def test_gradient_follows_coefficients_and_positions(oracle, model_l16):
     """The gradient program follows mtpb_update_coefficients, and the pair
-    buckets follow a position update through the reuse path."""
+    buckets follow a position update through the reuse path (list built
+    with a skin, so the moved atoms stay inside it)."""
     from mtpb200 import MTPGpuDirect
     sts = _mixed(2, 65, 2)
     te, tf, ts = _labels(sts, 11)
     m2 = configs.seeded_coefficients(model_l16, 99)
     with MTPGpuDirect(model_l16, 0) as gpu:
         batch = _batch(sts)
+        gpu.set_skin(0.5)
         gpu.build_neighbors(batch)
         gpu.loss_grad(te, tf, ts, WEIGHTS)
         gpu.set_coefficients(m2.coefficients())
