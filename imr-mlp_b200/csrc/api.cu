@@ -78,8 +78,47 @@ static bool copy_model(const mtpb_model_view *v, ModelHost &m, std::string *err)
     return true;
 }
 
+// Graph kernel geometry: 16 atoms per block with the rows in shared memory
+// when they fit, else 8 atoms, else rows in an L2-resident global slice per
+// persistent block (one block per SM).  MTPB_DAG_ATOMS=8|16 forces the
+// shared-memory width where it fits.
+static int dag_configure(mtpb_context *c)
+{
+    DagPlan &p = c->plan;
+    int optin = 0, sms = 0;
+    CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device),
+             "device attribute");
+    CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->device),
+             "device attribute");
+    const size_t limit = (size_t)optin - 8 * 1024;   // static shared arrays of the kernels
+    auto fits = [&](int atoms) {
+        return dag_ring_bytes(atoms) + (size_t)p.nrows * atoms * sizeof(double) <= limit;
+    };
+    p.global_rows = false;
+    p.grid = sms;
+    if (c->dag_atoms_env && fits(c->dag_atoms_env))
+        p.atoms = c->dag_atoms_env;
+    else if (fits(16))
+        p.atoms = 16;
+    else if (fits(8))
+        p.atoms = 8;
+    else {
+        p.atoms = 16;
+        p.global_rows = true;
+    }
+    p.grad_global_rows = dag_grad_smem_bytes(p, false) > limit;
+    if (c->force_global_rows) {   // MTPB_DAG_GLOBAL_ROWS=1: test the large-graph mode
+        p.atoms = 16;
+        p.global_rows = true;
+        p.grad_global_rows = true;
+    }
+    p.grad_grid = sms;
+    return MTPB_OK;
+}
+
 static int upload_model(mtpb_context *c)
 {
+    int rc = MTPB_OK;
     const ModelHost &m = c->model;
     const int KK = m.K * m.K;
     std::vector<PairParams> pp(KK);
@@ -112,8 +151,8 @@ static int upload_model(mtpb_context *c)
     CUDA_TRY(cudaMemcpyAsync(c->d_pairs, pp.data(), sizeof(PairParams) * KK,
                              cudaMemcpyHostToDevice, c->stream),
              "upload pairs");
-    if ((size_t)c->plan.nrows * 16 * sizeof(double) > 190 * 1024)
-        g_dag_atoms = 8;   // the 16-atom geometry does not fit this graph
+    if ((rc = dag_configure(c)))
+        return rc;
     c->h_recs = dag_device_records(c->plan);
     CUDA_TRY(cudaMemcpyAsync(c->d_recs, c->h_recs.data(), sizeof(DagDevRec) * c->h_recs.size(),
                              cudaMemcpyHostToDevice, c->stream),
@@ -166,8 +205,15 @@ int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offse
     CUDA_TRY(launch_moments_fwd(c->shape, a, basic, c->stream), "moments forward");
     c->launches++;
     CUDA_TRY(cudaEventRecord(c->ev[2], c->stream), "event");
+    double *gscratch = nullptr;
+    if (c->plan.global_rows) {
+        gscratch = c->arena.get<double>("dag_rows", (size_t)c->plan.grid * c->plan.nrows *
+                                                        c->plan.atoms);
+        if (!gscratch)
+            return fail(MTPB_ERR_MEMORY, "device allocation for graph rows failed");
+    }
     CUDA_TRY(launch_dag(c->plan, c->d_recs, c->d_phase_row0, c->nslot, ncenter, c->npad, types,
-                        c->d_species, basic, adjoint, site_energy, c->d_err, c->stream),
+                        c->d_species, basic, adjoint, site_energy, gscratch, c->d_err, c->stream),
              "moment graph");
     c->launches++;
     CUDA_TRY(cudaEventRecord(c->ev[3], c->stream), "event");
@@ -243,7 +289,9 @@ int mtpb_create(int device, const mtpb_model_view *view, mtpb_context **out)
             break;
         }
         if (const char *v = std::getenv("MTPB_DAG_ATOMS"))
-            g_dag_atoms = std::atoi(v) == 16 ? 16 : 8;
+            c->dag_atoms_env = std::atoi(v) == 16 ? 16 : 8;
+        if (const char *v = std::getenv("MTPB_DAG_GLOBAL_ROWS"))
+            c->force_global_rows = std::atoi(v) == 1;
         c->shape = select_shape(c->model, &err);
         if (c->shape < 0) {
             rc = fail(MTPB_ERR_UNSUPPORTED, err);

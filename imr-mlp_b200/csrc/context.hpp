@@ -81,7 +81,9 @@ struct mtpb_context {
     int launches = 0;
     int pending_launches = 0;   // neighbour build / refresh launches of this call
     bool have_efs = false;
-    long edge_epoch = 0;   // advanced whenever the edge list or its vectors change
+    long edge_epoch = 0;
+    int dag_atoms_env = 0;   // MTPB_DAG_ATOMS override of the graph block width
+    bool force_global_rows = false;   // MTPB_DAG_GLOBAL_ROWS=1   // advanced whenever the edge list or its vectors change
     mtpb::TrainingState train;
 };
 

@@ -87,6 +87,31 @@ __device__ __forceinline__ void sts_d2(unsigned a, double x, double y)
     asm volatile("st.shared.v2.f64 [%0], {%1, %2};" ::"r"(a), "d"(x), "d"(y) : "memory");
 }
 
+// Row storage of the graph kernels: shared memory (32-bit addresses) or, for
+// graphs larger than shared memory, a per-block slice of global scratch that
+// stays resident in L2 (persistent blocks, one slice each).  Offsets are
+// byte offsets from the lane's first atom in row 0.
+template <bool GLOBAL_ROWS> struct Rows;
+template <> struct Rows<false> {
+    unsigned base;
+    __device__ __forceinline__ double2 ld(unsigned off) const { return lds_d2(base + off); }
+    __device__ __forceinline__ void st(unsigned off, double x, double y) const
+    {
+        sts_d2(base + off, x, y);
+    }
+};
+template <> struct Rows<true> {
+    char *base;
+    __device__ __forceinline__ double2 ld(unsigned off) const
+    {
+        return *reinterpret_cast<const double2 *>(base + off);
+    }
+    __device__ __forceinline__ void st(unsigned off, double x, double y) const
+    {
+        *reinterpret_cast<double2 *>(base + off) = make_double2(x, y);
+    }
+};
+
 constexpr unsigned DEV_END = 1u << 28, DEV_GLOBAL = 2u << 28, DEV_ENERGY = 4u << 28;
 constexpr unsigned DEV_OUT_MASK = (1u << 28) - 1;
 

@@ -22,6 +22,7 @@
 #include "moments.cuh"
 #include "dag.cuh"
 
+#include <algorithm>
 #include <cstdio>
 
 namespace mtpb {
@@ -528,8 +529,8 @@ cudaError_t launch_group_maxdeg(int natoms, const int *offsets, int *group_maxde
 // Runs n consecutive records of one stream.  All records belong to one
 // phase, so a row written here is never read here and record loads may move
 // ahead of stores.
-template <int ATOMS, bool FWD>
-__device__ __forceinline__ void dag_segment(unsigned rec_addr, unsigned rowsA, int n,
+template <int ATOMS, bool FWD, bool GR>
+__device__ __forceinline__ void dag_segment(unsigned rec_addr, const Rows<GR> &rowsA, int n,
                                             double *acc, double *E, double *adjoint, int npad,
                                             int natoms, int atom_a)
 {
@@ -550,7 +551,7 @@ __device__ __forceinline__ void dag_segment(unsigned rec_addr, unsigned rowsA, i
                 if (atom_a + 1 < natoms)
                     adjoint[(size_t)out * npad + atom_a + 1] = acc[1];
             } else {
-                sts_d2(rowsA + out, acc[0], acc[1]);
+                rowsA.st(out, acc[0], acc[1]);
             }
             acc[0] = 0.0;
             acc[1] = 0.0;
@@ -568,8 +569,8 @@ __device__ __forceinline__ void dag_segment(unsigned rec_addr, unsigned rowsA, i
         double2 x[4], y[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            x[u] = lds_d2(rowsA + w[u].x);
-            y[u] = lds_d2(rowsA + w[u].y);
+            x[u] = rowsA.ld(w[u].x);
+            y[u] = rowsA.ld(w[u].y);
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -583,7 +584,7 @@ __device__ __forceinline__ void dag_segment(unsigned rec_addr, unsigned rowsA, i
     for (; k < n; ++k) {
         const uint4 w = lds128(rec_addr + k * REC_STRIDE);
         const unsigned of = lds32(rec_addr + k * REC_STRIDE + 16);
-        const double2 x = lds_d2(rowsA + w.x), y = lds_d2(rowsA + w.y);
+        const double2 x = rowsA.ld(w.x), y = rowsA.ld(w.y);
         const double c = __hiloint2double((int)w.w, (int)w.z);
         acc[0] = fma(c * x.x, y.x, acc[0]);
         acc[1] = fma(c * x.y, y.y, acc[1]);
@@ -592,13 +593,16 @@ __device__ __forceinline__ void dag_segment(unsigned rec_addr, unsigned rowsA, i
     }
 }
 
-template <int ATOMS>
+// GR: rows in the global scratch slice of this block (graphs larger than
+// shared memory); the blocks then loop over the atom groups.
+template <int ATOMS, bool GR>
 __global__ void __launch_bounds__(DagGeom<ATOMS>::THREADS)
     k_dag(const DagDevRec *__restrict__ recs, const int *__restrict__ phase_row0, int n_fwd,
-          int n_rev, int one_row, int zero_row, int nslot, int natoms, int npad,
+          int n_rev, int one_row, int zero_row, int nrows, int nslot, int natoms, int npad,
           const int *__restrict__ types, const double *__restrict__ species_coeffs,
           const double *__restrict__ basic, double *__restrict__ adjoint,
-          double *__restrict__ site_energy, int *__restrict__ err_flag)
+          double *__restrict__ site_energy, double *__restrict__ gscratch,
+          int *__restrict__ err_flag)
 {
     using G = DagGeom<ATOMS>;
     extern __shared__ __align__(128) unsigned char dsm[];
@@ -609,7 +613,8 @@ __global__ void __launch_bounds__(DagGeom<ATOMS>::THREADS)
     const int lane = tid & 31, warp = tid >> 5;
     const int nph = n_fwd + n_rev;
     unsigned char *ring = dsm + (size_t)warp * 2 * G::SLOT_BYTES;   // this warp's two slots
-    double *rows = reinterpret_cast<double *>(dsm + G::ring_bytes());   // [nrows][ATOMS]
+    double *rows = GR ? gscratch + (size_t)blockIdx.x * nrows * ATOMS
+                      : reinterpret_cast<double *>(dsm + G::ring_bytes());   // [nrows][ATOMS]
     for (int i = tid; i <= nph; i += blockDim.x)
         ph0[i] = phase_row0[i];
     if (lane == 0) {
@@ -617,100 +622,114 @@ __global__ void __launch_bounds__(DagGeom<ATOMS>::THREADS)
         mbar_init(&bar[warp][1], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    const int atom0 = blockIdx.x * ATOMS;
-    // basic moments: asynchronous 16-byte copies (two atoms each); in a partial
-    // last block the lanes past natoms read row padding (inside the npad
-    // stride) and their results are never written out
-    const unsigned rows_u32 = smem_u32(rows);
-    for (int i = tid; i < nslot * (ATOMS / 2); i += blockDim.x) {
-        const int sl = i / (ATOMS / 2), a = 2 * (i - sl * (ATOMS / 2));
-        cp_async16(rows_u32 + (unsigned)(sl * ATOMS + a) * 8, basic + (size_t)sl * npad + atom0 + a);
-    }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    if (tid < ATOMS) {
-        rows[one_row * ATOMS + tid] = 1.0;
-        rows[zero_row * ATOMS + tid] = 0.0;
-    }
-    __syncthreads();
+    const unsigned rows_u32 = smem_u32(dsm + G::ring_bytes());
     const int g = lane / G::LPS, q = lane - g * G::LPS;
     const int a0 = 2 * q;   // this lane's atoms: a0, a0 + 1
-    const unsigned rowsA = rows_u32 + a0 * 8;
+    Rows<GR> rowsA;
+    if constexpr (GR)
+        rowsA.base = reinterpret_cast<char *>(rows + a0);
+    else
+        rowsA.base = rows_u32 + a0 * 8;
     const unsigned ring_u32 = smem_u32(ring) + g * sizeof(DagDevRec);
-    double E[2] = {0.0, 0.0}, acc[2] = {0.0, 0.0};
-    int kw = 0;   // ring slots consumed by this warp
     auto phase_src = [&](int ph) {
         const int rows_p = ph0[ph + 1] - ph0[ph];
         return recs + (size_t)ph0[ph] * DAG_STREAMS + (size_t)warp * rows_p * G::SPW;
-    };
-    auto issue = [&](int ph, int c, int slot) {
-        const int rows_p = ph0[ph + 1] - ph0[ph];
-        const int r = min(G::CH, rows_p - c * G::CH);
-        bulk_load(ring + slot * G::SLOT_BYTES, phase_src(ph) + (size_t)c * G::CH * G::SPW,
-                  (unsigned)(r * G::SPW * sizeof(DagDevRec)), &bar[warp][slot]);
     };
     auto nchunks = [&](int ph) { return (ph0[ph + 1] - ph0[ph] + G::CH - 1) / G::CH; };
     // lane 0 issues the warp's chunks in consumption order (phase by phase,
     // skipping empty phases); issue j goes to slot j & 1 and is made only
     // after chunk j - 2 has been consumed.  Records do not depend on the
     // phase barriers, so the next phase's chunks are fetched early.
-    int iph = 0, ic = 0, nissued = 0;
+    int iph = 0, ic = 0, nissued = 0, kw = 0;
     auto issue_next = [&]() {
         while (iph < nph && ic >= nchunks(iph)) {
             ++iph;
             ic = 0;
         }
         if (iph < nph) {
-            issue(iph, ic, nissued & 1);
+            const int rows_p = ph0[iph + 1] - ph0[iph];
+            const int r = min(G::CH, rows_p - ic * G::CH);
+            const int slot = nissued & 1;
+            bulk_load(ring + slot * G::SLOT_BYTES, phase_src(iph) + (size_t)ic * G::CH * G::SPW,
+                      (unsigned)(r * G::SPW * sizeof(DagDevRec)), &bar[warp][slot]);
             ++ic;
             ++nissued;
         }
     };
-    if (lane == 0) {
-        issue_next();
-        issue_next();
-    }
-    for (int ph = 0; ph < nph; ++ph) {
-        const int rows_p = ph0[ph + 1] - ph0[ph];
-        const int nch = nchunks(ph);
-        const bool fwd = ph < n_fwd;
-        for (int c = 0; c < nch; ++c, ++kw) {
-            const int slot = kw & 1;
-            long it = 0;
-            while (!mbar_try_wait(&bar[warp][slot], (unsigned)((kw >> 1) & 1))) {
-                if (++it > DAG_WAIT_LIMIT) {
-                    *err_flag = 1;
-                    break;
-                }
-            }
-            const int n = min(G::CH, rows_p - c * G::CH);
-            const unsigned rec_addr = ring_u32 + slot * G::SLOT_BYTES;
-            if (fwd)
-                dag_segment<ATOMS, true>(rec_addr, rowsA, n, acc, E, adjoint, npad, natoms,
-                                         atom0 + a0);
+    const int ngroups = (natoms + ATOMS - 1) / ATOMS;
+    for (int grp = blockIdx.x; grp < ngroups; grp += gridDim.x) {
+        const int atom0 = grp * ATOMS;
+        __syncthreads();   // the previous group's rows are no longer read
+        // basic moments (two atoms per copy); in a partial last group the
+        // lanes past natoms read row padding (inside the npad stride) and
+        // their results are never written out
+        for (int i = tid; i < nslot * (ATOMS / 2); i += blockDim.x) {
+            const int sl = i / (ATOMS / 2), a = 2 * (i - sl * (ATOMS / 2));
+            const double *src = basic + (size_t)sl * npad + atom0 + a;
+            if constexpr (GR)
+                *reinterpret_cast<double2 *>(rows + (size_t)sl * ATOMS + a) =
+                    *reinterpret_cast<const double2 *>(src);
             else
-                dag_segment<ATOMS, false>(rec_addr, rowsA, n, acc, E, adjoint, npad, natoms,
-                                          atom0 + a0);
-            __syncwarp();
-            if (lane == 0) {
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                issue_next();
-            }
+                cp_async16(rows_u32 + (unsigned)(sl * ATOMS + a) * 8, src);
+        }
+        if constexpr (!GR)
+            asm volatile("cp.async.wait_all;" ::: "memory");
+        if (tid < ATOMS) {
+            rows[(size_t)one_row * ATOMS + tid] = 1.0;
+            rows[(size_t)zero_row * ATOMS + tid] = 0.0;
         }
         __syncthreads();
-        if (ph + 1 == n_fwd) {
-            const int stream = warp * G::SPW + g;
-            epart[stream][a0] = E[0];
-            epart[stream][a0 + 1] = E[1];
-            __syncthreads();
-            if (tid < ATOMS && atom0 + tid < natoms) {
-                const int t = types[atom0 + tid];
-                double se = 0.0;
-                if (t >= 0) {
-                    se = species_coeffs[t];
-                    for (int s2 = 0; s2 < DAG_STREAMS; ++s2)
-                        se += epart[s2][tid];
+        if (lane == 0) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            iph = 0;
+            ic = 0;
+            issue_next();
+            issue_next();
+        }
+        double E[2] = {0.0, 0.0}, acc[2] = {0.0, 0.0};
+        for (int ph = 0; ph < nph; ++ph) {
+            const int rows_p = ph0[ph + 1] - ph0[ph];
+            const int nch = nchunks(ph);
+            const bool fwd = ph < n_fwd;
+            for (int c = 0; c < nch; ++c, ++kw) {
+                const int slot = kw & 1;
+                long it = 0;
+                while (!mbar_try_wait(&bar[warp][slot], (unsigned)((kw >> 1) & 1))) {
+                    if (++it > DAG_WAIT_LIMIT) {
+                        *err_flag = 1;
+                        break;
+                    }
                 }
-                site_energy[atom0 + tid] = se;
+                const int n = min(G::CH, rows_p - c * G::CH);
+                const unsigned rec_addr = ring_u32 + slot * G::SLOT_BYTES;
+                if (fwd)
+                    dag_segment<ATOMS, true, GR>(rec_addr, rowsA, n, acc, E, adjoint, npad,
+                                                 natoms, atom0 + a0);
+                else
+                    dag_segment<ATOMS, false, GR>(rec_addr, rowsA, n, acc, E, adjoint, npad,
+                                                  natoms, atom0 + a0);
+                __syncwarp();
+                if (lane == 0) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    issue_next();
+                }
+            }
+            __syncthreads();
+            if (ph + 1 == n_fwd) {
+                const int stream = warp * G::SPW + g;
+                epart[stream][a0] = E[0];
+                epart[stream][a0 + 1] = E[1];
+                __syncthreads();
+                if (tid < ATOMS && atom0 + tid < natoms) {
+                    const int t = types[atom0 + tid];
+                    double se = 0.0;
+                    if (t >= 0) {
+                        se = species_coeffs[t];
+                        for (int s2 = 0; s2 < DAG_STREAMS; ++s2)
+                            se += epart[s2][tid];
+                    }
+                    site_energy[atom0 + tid] = se;
+                }
             }
         }
     }
@@ -721,8 +740,8 @@ __global__ void __launch_bounds__(DagGeom<ATOMS>::THREADS)
 // into shared-memory byte offsets.
 std::vector<DagDevRec> dag_device_records(const DagPlan &plan)
 {
-    const int spw = g_dag_atoms == 16 ? DagGeom<16>::SPW : DagGeom<8>::SPW;
-    const unsigned row_bytes = (unsigned)g_dag_atoms * 8;
+    const int spw = plan.atoms == 16 ? DagGeom<16>::SPW : DagGeom<8>::SPW;
+    const unsigned row_bytes = (unsigned)plan.atoms * 8;
     std::vector<DagDevRec> out(plan.recs.size());
     size_t row0 = 0, o = 0;
     const int warps = DAG_STREAMS / spw;
@@ -751,43 +770,59 @@ std::vector<DagDevRec> dag_device_records(const DagPlan &plan)
     return out;
 }
 
-int g_dag_atoms = 16;   // atoms per graph block (8 or 16)
+size_t dag_ring_bytes(int atoms)
+{
+    return atoms == 16 ? DagGeom<16>::ring_bytes() : DagGeom<8>::ring_bytes();
+}
 
-template <int ATOMS>
+template <int ATOMS, bool GR>
 static cudaError_t launch_dag_geom(const DagPlan &plan, const DagDevRec *recs,
                                    const int *phase_row0, int nslot, int natoms, int npad,
                                    const int *types, const double *species_coeffs,
                                    const double *basic, double *adjoint, double *site_energy,
-                                   int *err_flag, cudaStream_t s)
+                                   double *gscratch, int *err_flag, cudaStream_t s)
 {
     using G = DagGeom<ATOMS>;
-    const int blocks = (natoms + ATOMS - 1) / ATOMS;
-    const size_t smem = G::ring_bytes() + sizeof(double) * (size_t)plan.nrows * ATOMS;
-    cudaError_t err = cudaFuncSetAttribute(k_dag<ATOMS>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int ngroups = (natoms + ATOMS - 1) / ATOMS;
+    const int blocks = GR ? std::min(ngroups, plan.grid) : ngroups;
+    const size_t smem = G::ring_bytes() + (GR ? 0 : sizeof(double) * (size_t)plan.nrows * ATOMS);
+    auto kern = k_dag<ATOMS, GR>;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem);
+    if (err == cudaSuccess && GR)   // leave the rest of the SM's memory to L1
+        err = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 25);
     if (err != cudaSuccess)
         return err;
-    k_dag<ATOMS><<<blocks, G::THREADS, smem, s>>>(recs, phase_row0, plan.n_fwd, plan.n_rev,
-                                                  plan.one_row, plan.zero_row, nslot, natoms,
-                                                  npad, types, species_coeffs, basic, adjoint,
-                                                  site_energy, err_flag);
+    kern<<<blocks, G::THREADS, smem, s>>>(recs, phase_row0, plan.n_fwd, plan.n_rev, plan.one_row,
+                                          plan.zero_row, plan.nrows, nslot, natoms, npad, types,
+                                          species_coeffs, basic, adjoint, site_energy, gscratch,
+                                          err_flag);
     return cudaGetLastError();
 }
 
 cudaError_t launch_dag(const DagPlan &plan, const DagDevRec *recs, const int *phase_row0, int nslot,
                        int natoms, int npad, const int *types, const double *species_coeffs,
-                       const double *basic, double *adjoint, double *site_energy, int *err_flag,
-                       cudaStream_t s)
+                       const double *basic, double *adjoint, double *site_energy,
+                       double *gscratch, int *err_flag, cudaStream_t s)
 {
     if (natoms == 0)
         return cudaSuccess;
     if (plan.n_fwd + plan.n_rev > DAG_MAX_PHASES)
         return cudaErrorInvalidValue;
-    if (g_dag_atoms == 16)
-        return launch_dag_geom<16>(plan, recs, phase_row0, nslot, natoms, npad, types,
-                                   species_coeffs, basic, adjoint, site_energy, err_flag, s);
-    return launch_dag_geom<8>(plan, recs, phase_row0, nslot, natoms, npad, types, species_coeffs,
-                              basic, adjoint, site_energy, err_flag, s);
+    if (plan.global_rows) {
+        if (plan.atoms != 16 || !gscratch || plan.grid < 1)
+            return cudaErrorInvalidValue;
+        return launch_dag_geom<16, true>(plan, recs, phase_row0, nslot, natoms, npad, types,
+                                         species_coeffs, basic, adjoint, site_energy, gscratch,
+                                         err_flag, s);
+    }
+    if (plan.atoms == 16)
+        return launch_dag_geom<16, false>(plan, recs, phase_row0, nslot, natoms, npad, types,
+                                          species_coeffs, basic, adjoint, site_energy, nullptr,
+                                          err_flag, s);
+    return launch_dag_geom<8, false>(plan, recs, phase_row0, nslot, natoms, npad, types,
+                                     species_coeffs, basic, adjoint, site_energy, nullptr,
+                                     err_flag, s);
 }
 
 // ----------------------------------------------------------------------------

@@ -547,8 +547,8 @@ struct DagGradGeom {
     static constexpr size_t ring_bytes() { return (size_t)WARPS * 2 * SLOT_BYTES; }
 };
 
-template <bool FWD>
-__device__ __forceinline__ void dag_grad_segment(unsigned rec_addr, unsigned rowA, int n,
+template <bool FWD, bool GR>
+__device__ __forceinline__ void dag_grad_segment(unsigned rec_addr, const Rows<GR> &rowA, int n,
                                                  double &acc, double &accd, double dlde,
                                                  bool valid, unsigned gmask, int q, double *gsm,
                                                  double *adjoint2, int npad, int atom)
@@ -574,7 +574,7 @@ __device__ __forceinline__ void dag_grad_segment(unsigned rec_addr, unsigned row
                 if (valid)
                     adjoint2[(size_t)out * npad + atom] = accd;
             } else {
-                sts_d2(rowA + out, acc, accd);
+                rowA.st(out, acc, accd);
             }
             acc = 0.0;
             accd = 0.0;
@@ -592,8 +592,8 @@ __device__ __forceinline__ void dag_grad_segment(unsigned rec_addr, unsigned row
         double2 x[4], y[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            x[u] = lds_d2(rowA + w[u].x);
-            y[u] = lds_d2(rowA + w[u].y);
+            x[u] = rowA.ld(w[u].x);
+            y[u] = rowA.ld(w[u].y);
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -609,7 +609,7 @@ __device__ __forceinline__ void dag_grad_segment(unsigned rec_addr, unsigned row
         const unsigned ra = rec_addr + k * REC_STRIDE;
         const uint4 w = lds128(ra);
         const unsigned of = lds32(ra + 16);
-        const double2 x = lds_d2(rowA + w.x), y = lds_d2(rowA + w.y);
+        const double2 x = rowA.ld(w.x), y = rowA.ld(w.y);
         const double c = __hiloint2double((int)w.w, (int)w.z);
         const double cx = c * x.x;
         acc = fma(cx, y.x, acc);
@@ -619,13 +619,16 @@ __device__ __forceinline__ void dag_grad_segment(unsigned rec_addr, unsigned row
     }
 }
 
+// GR: rows in the global scratch slice of this block (graphs larger than
+// shared memory)
+template <bool GR>
 __global__ void __launch_bounds__(DagGradGeom::THREADS)
     k_dag_grad(const DagDevRec *__restrict__ recs, const int *__restrict__ phase_row0, int n_fwd,
                int n_rev, int one_row, int zero_row, int one_adj_row, int nrows, int nslot,
                int natoms, int npad, const double *__restrict__ basic,
                const double *__restrict__ tangent, const double *__restrict__ dlde_atom,
                int n_energy, double *__restrict__ adjoint2, double *__restrict__ energy_partials,
-               int *__restrict__ err_flag)
+               double *__restrict__ gscratch, int *__restrict__ err_flag)
 {
     using G = DagGradGeom;
     extern __shared__ __align__(128) unsigned char dsm[];
@@ -635,8 +638,10 @@ __global__ void __launch_bounds__(DagGradGeom::THREADS)
     const int lane = tid & 31, warp = tid >> 5;
     const int nph = n_fwd + n_rev;
     unsigned char *ring = dsm + (size_t)warp * 2 * G::SLOT_BYTES;
-    double *rows = reinterpret_cast<double *>(dsm + G::ring_bytes());   // [nrows][ATOMS][2]
-    double *gsm = rows + (size_t)nrows * G::ATOMS * 2;                  // [n_energy]
+    double *srows = reinterpret_cast<double *>(dsm + G::ring_bytes());
+    double *rows = GR ? gscratch + (size_t)blockIdx.x * nrows * G::ATOMS * 2
+                      : srows;                                       // [nrows][ATOMS][2]
+    double *gsm = GR ? srows : srows + (size_t)nrows * G::ATOMS * 2;  // [n_energy]
     for (int i = tid; i <= nph; i += blockDim.x)
         ph0[i] = phase_row0[i];
     for (int i = tid; i < n_energy; i += blockDim.x)
@@ -646,10 +651,13 @@ __global__ void __launch_bounds__(DagGradGeom::THREADS)
         mbar_init(&bar[warp][1], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    const unsigned rows_u32 = smem_u32(rows);
     const int g = lane / G::LPS, q = lane - g * G::LPS;
     const unsigned gmask = 0xffu << (g * G::LPS);
-    const unsigned rowA = rows_u32 + q * 16;
+    Rows<GR> rowA;
+    if constexpr (GR)
+        rowA.base = reinterpret_cast<char *>(rows + 2 * q);
+    else
+        rowA.base = smem_u32(srows) + q * 16;
     const unsigned ring_u32 = smem_u32(ring) + g * sizeof(DagDevRec);
     auto phase_src = [&](int ph) {
         const int rows_p = ph0[ph + 1] - ph0[ph];
@@ -725,10 +733,10 @@ __global__ void __launch_bounds__(DagGradGeom::THREADS)
                 const int n = min(G::CH, rows_p - c * G::CH);
                 const unsigned rec_addr = ring_u32 + slot * G::SLOT_BYTES;
                 if (fwd)
-                    dag_grad_segment<true>(rec_addr, rowA, n, acc, accd, dlde, valid, gmask, q,
+                    dag_grad_segment<true, GR>(rec_addr, rowA, n, acc, accd, dlde, valid, gmask, q,
                                            gsm, adjoint2, npad, atom);
                 else
-                    dag_grad_segment<false>(rec_addr, rowA, n, acc, accd, dlde, valid, gmask, q,
+                    dag_grad_segment<false, GR>(rec_addr, rowA, n, acc, accd, dlde, valid, gmask, q,
                                             gsm, adjoint2, npad, atom);
                 __syncwarp();
                 if (lane == 0) {
@@ -788,24 +796,34 @@ std::vector<DagDevRec> dag_grad_records(const DagPlan &plan)
     return out;
 }
 
-size_t dag_grad_smem_bytes(const DagPlan &plan)
+size_t dag_grad_smem_bytes(const DagPlan &plan, bool global_rows)
 {
     using G = DagGradGeom;
-    return G::ring_bytes() + (size_t)(plan.nrows + 1) * G::ROW_BYTES +
+    return G::ring_bytes() + (global_rows ? 0 : (size_t)(plan.nrows + 1) * G::ROW_BYTES) +
            sizeof(double) * plan.energy_moments.size();
+}
+
+size_t dag_grad_scratch_doubles(const DagPlan &plan)
+{
+    using G = DagGradGeom;
+    return plan.grad_global_rows
+               ? (size_t)plan.grad_grid * (plan.nrows + 1) * G::ATOMS * 2
+               : 0;
 }
 
 int dag_grad_grid(const DagPlan &plan, int natoms)
 {
     using G = DagGradGeom;
     const int ngroups = (natoms + G::ATOMS - 1) / G::ATOMS;
+    if (plan.grad_global_rows)
+        return std::max(1, std::min(ngroups, plan.grad_grid));
     int dev = 0, sms = 148, per = 1;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const size_t smem = dag_grad_smem_bytes(plan);
-    if (cudaFuncSetAttribute(k_dag_grad, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    const size_t smem = dag_grad_smem_bytes(plan, false);
+    if (cudaFuncSetAttribute(k_dag_grad<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem) == cudaSuccess)
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_dag_grad, G::THREADS, smem);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_dag_grad<false>, G::THREADS, smem);
     per = per < 1 ? 1 : per;
     return std::max(1, std::min(ngroups, sms * per));
 }
@@ -813,22 +831,30 @@ int dag_grad_grid(const DagPlan &plan, int natoms)
 cudaError_t launch_dag_grad(const DagPlan &plan, const DagDevRec *recs, const int *phase_row0,
                             int grid, int nslot, int natoms, int npad, const double *basic,
                             const double *tangent, const double *dlde_atom, double *adjoint2,
-                            double *energy_partials, int *err_flag, cudaStream_t s)
+                            double *energy_partials, double *gscratch, int *err_flag,
+                            cudaStream_t s)
 {
     using G = DagGradGeom;
     if (natoms == 0)
         return cudaSuccess;
     if (plan.n_fwd + plan.n_rev > DAG_MAX_PHASES)
         return cudaErrorInvalidValue;
-    const size_t smem = dag_grad_smem_bytes(plan);
-    cudaError_t err = cudaFuncSetAttribute(k_dag_grad, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    const bool gr = plan.grad_global_rows;
+    if (gr && (!gscratch || grid > plan.grad_grid))
+        return cudaErrorInvalidValue;
+    const size_t smem = dag_grad_smem_bytes(plan, gr);
+    auto kern = gr ? k_dag_grad<true> : k_dag_grad<false>;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)smem);
+    if (err == cudaSuccess && gr)   // leave the rest of the SM's memory to L1
+        err = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 25);
     if (err != cudaSuccess)
         return err;
-    k_dag_grad<<<grid, G::THREADS, smem, s>>>(
-        recs, phase_row0, plan.n_fwd, plan.n_rev, plan.one_row, plan.zero_row, plan.nrows,
-        plan.nrows + 1, nslot, natoms, npad, basic, tangent, dlde_atom,
-        (int)plan.energy_moments.size(), adjoint2, energy_partials, err_flag);
+    kern<<<grid, G::THREADS, smem, s>>>(recs, phase_row0, plan.n_fwd, plan.n_rev, plan.one_row,
+                                        plan.zero_row, plan.nrows, plan.nrows + 1, nslot, natoms,
+                                        npad, basic, tangent, dlde_atom,
+                                        (int)plan.energy_moments.size(), adjoint2,
+                                        energy_partials, gscratch, err_flag);
     return cudaGetLastError();
 }
 

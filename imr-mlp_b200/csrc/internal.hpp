@@ -79,7 +79,7 @@ struct alignas(16) DagDevRec {
 constexpr int DAG_CHUNK_ROWS = MTPB_DAG_CHUNK_ROWS;   // record rows per shared chunk
 
 struct DagPlan {
-    int nrows = 0;           // shared-memory rows (one double per atom each)
+    int nrows = 0;           // rows (one double per atom each)
     int one_row = 0;         // row holding 1.0
     int zero_row = 0;        // row holding 0.0
     int scratch_row = 0;     // row receiving stores that nothing reads
@@ -90,6 +90,12 @@ struct DagPlan {
     // record closes (-1 for every other record), parallel to recs
     std::vector<int> rec_energy;
     std::vector<int> energy_moments;   // moment ids with a scalar coefficient
+    // execution geometry, chosen when the plan is uploaded (dag_configure)
+    int atoms = 16;            // atoms per graph block (8 or 16)
+    bool global_rows = false;  // rows in global scratch (graph too large for shared memory)
+    int grid = 0;              // persistent blocks with global rows (one per SM)
+    bool grad_global_rows = false;   // the same choice for the dual graph (grad.cu)
+    int grad_grid = 0;
 };
 
 // Edge-kernel parameters (device pointers).
@@ -111,12 +117,12 @@ struct EdgeArgs {
 cudaError_t launch_moments_fwd(int shape, const EdgeArgs &a, double *basic, cudaStream_t s);
 cudaError_t launch_moments_rev(int shape, const EdgeArgs &a, const double *adjoint, double *dx,
                                double *dy, double *dz, cudaStream_t s);
-extern int g_dag_atoms;   // graph kernel atoms per block (8 or 16)
+size_t dag_ring_bytes(int atoms);
 std::vector<DagDevRec> dag_device_records(const DagPlan &plan);
 cudaError_t launch_dag(const DagPlan &plan, const DagDevRec *recs, const int *phase_row0,
                        int nslot, int natoms, int npad, const int *types,
                        const double *species_coeffs, const double *basic, double *adjoint,
-                       double *site_energy, int *err_flag, cudaStream_t s);
+                       double *site_energy, double *gscratch, int *err_flag, cudaStream_t s);
 cudaError_t launch_group_maxdeg(int natoms, const int *offsets, int *group_maxdeg,
                                 cudaStream_t s);
 cudaError_t launch_force_gather(int natoms, int ntotal, const int *offsets, const int *in_offsets,
@@ -138,11 +144,13 @@ cudaError_t launch_edge_grad(int shape, const EdgeArgs &a, const double *wx, con
                              const double *wz, const double *adjoint, const double *adjoint2,
                              double *uv, cudaStream_t s);
 std::vector<DagDevRec> dag_grad_records(const DagPlan &plan);
-size_t dag_grad_smem_bytes(const DagPlan &plan);
+size_t dag_grad_smem_bytes(const DagPlan &plan, bool global_rows);
+size_t dag_grad_scratch_doubles(const DagPlan &plan);
 int dag_grad_grid(const DagPlan &plan, int natoms);
 cudaError_t launch_dag_grad(const DagPlan &plan, const DagDevRec *recs, const int *phase_row0,
                             int grid, int nslot, int natoms, int npad, const double *basic,
                             const double *tangent, const double *dlde_atom, double *adjoint2,
-                            double *energy_partials, int *err_flag, cudaStream_t s);
+                            double *energy_partials, double *gscratch, int *err_flag,
+                            cudaStream_t s);
 
 } // namespace mtpb

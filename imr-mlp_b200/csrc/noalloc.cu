@@ -216,6 +216,9 @@ int noalloc_compute(mtpb_context *c, const mtpb_csr_request *r)
         return fail(MTPB_ERR_UNSUPPORTED, "model basis too large for the no-allocation path "
                                           "(at most " + std::to_string(NOALLOC_MAX_SLOTS) +
                                               " basic-moment slots)");
+    if (c->plan.global_rows)
+        return fail(MTPB_ERR_UNSUPPORTED, "moment graph too large for shared memory: the "
+                                          "no-allocation path has no room for its rows");
     if (!r->offsets || (NT > 0 && (!r->types || !r->x)) || (NC > 0 && !r->neighbors))
         return fail(MTPB_ERR_ARGUMENT, "offsets, neighbors, types and x are required");
     int rc = set_device(c);
@@ -272,7 +275,7 @@ int noalloc_compute(mtpb_context *c, const mtpb_csr_request *r)
     CUDA_TRY(launch_group_maxdeg(NC, r->offsets, maxdeg, s), "group_maxdeg");
     CUDA_TRY(launch_moments_fwd(c->shape, a, basic, s), "moments forward");
     CUDA_TRY(launch_dag(c->plan, c->d_recs, c->d_phase_row0, c->nslot, NC, c->npad, r->types,
-                        c->d_species, basic, adjoint, site_e, c->d_err, s),
+                        c->d_species, basic, adjoint, site_e, nullptr, c->d_err, s),
              "moment graph");
     CUDA_TRY(launch_moments_rev(c->shape, a, adjoint, dx, dy, dz, s), "moments reverse");
     CUDA_TRY(launch_force_gather(NC, NT, r->offsets, in_off, in_edges, dx, dy, dz, rx, ry, rz,

@@ -221,9 +221,9 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
     plan.scratch_row = next++;
     plan.nrows = next;
     plan.energy_moments = energy_moments;
-    if ((size_t)plan.nrows * 8 * sizeof(double) > 200 * 1024 || plan.nrows > 65535) {
+    if (plan.nrows > 65535) {
         if (err)
-            *err = "moment graph too large for the shared-memory plan (" +
+            *err = "moment graph too large for 16-bit row indices (" +
                    std::to_string(plan.nrows) + " rows)";
         return false;
     }

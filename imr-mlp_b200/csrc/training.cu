@@ -411,8 +411,6 @@ int upload_training_program(mtpb_context *c)
 {
     TrainingState &t = c->train;
     const DagPlan &plan = c->plan;
-    if (dag_grad_smem_bytes(plan) > 227 * 1024)
-        return fail(MTPB_ERR_UNSUPPORTED, "moment graph too large for the gradient plan");
     std::vector<DagDevRec> recs = dag_grad_records(plan);
     t.recs = c->arena.get<DagDevRec>("train_dag", recs.size() + 1);
     // moment coefficient s -> its scalar moment in the graph's energy list
@@ -486,6 +484,10 @@ int loss_grad_compute(mtpb_context *c, const mtpb_labels *labels, const mtpb_los
     const int ne = (int)c->plan.energy_moments.size();
     const int grid = dag_grad_grid(c->plan, N);
     double *epart = c->arena.get<double>("train_energy_part", (size_t)grid * ne + 1);
+    const size_t nscr = dag_grad_scratch_doubles(c->plan);
+    double *gscratch = nscr ? c->arena.get<double>("train_dag_rows", nscr) : nullptr;
+    if (nscr && !gscratch)
+        return fail(MTPB_ERR_MEMORY, "device allocation for the dual graph rows failed");
     int rg_grid = 0;
     {
         int dev = 0, sms = 148;
@@ -529,7 +531,8 @@ int loss_grad_compute(mtpb_context *c, const mtpb_labels *labels, const mtpb_los
                            c->nb.rz);
     CUDA_TRY(launch_moments_tangent(c->shape, a, wx, wy, wz, tangent, c->stream), "tangent");
     CUDA_TRY(launch_dag_grad(c->plan, c->train.recs, c->d_phase_row0, grid, c->nslot, N, c->npad,
-                             basic, tangent, dlde_atom, adjoint2, epart, c->d_err, c->stream),
+                             basic, tangent, dlde_atom, adjoint2, epart, gscratch, c->d_err,
+                             c->stream),
              "dual graph");
     CUDA_TRY(launch_edge_grad(c->shape, a, wx, wy, wz, adjoint, adjoint2, uv, c->stream),
              "edge gradient");

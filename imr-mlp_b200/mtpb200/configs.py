@@ -21,11 +21,13 @@ FCC_BASIS = np.array([[0.0, 0.0, 0.0], [0.5, 0.5, 0.0], [0.5, 0.0, 0.5], [0.0, 0
 BCC_BASIS = np.array([[0.0, 0.0, 0.0], [0.5, 0.5, 0.5]])
 
 
-def _supercell(basis: np.ndarray, reps: int, a: float):
-    g = np.arange(reps)
-    cells = np.stack(np.meshgrid(g, g, g, indexing="ij"), -1).reshape(-1, 3)
+def _supercell(basis: np.ndarray, reps, a: float):
+    """reps: cells per direction (int, or three ints for a non-cubic box)."""
+    r = (reps, reps, reps) if np.isscalar(reps) else tuple(int(v) for v in reps)
+    g = [np.arange(v) for v in r]
+    cells = np.stack(np.meshgrid(*g, indexing="ij"), -1).reshape(-1, 3)
     frac = (cells[:, None, :] + basis[None, :, :]).reshape(-1, 3)
-    return frac * a, np.eye(3) * (a * reps)
+    return frac * a, np.diag(np.array(r, dtype=np.float64) * a)
 
 
 def ni3al_l12(reps: int, a: float, sigma: float, seed: int) -> Dict[str, np.ndarray]:
@@ -71,13 +73,26 @@ def config2(n_struct: int = 4096, seed: int = 2) -> List[Dict[str, np.ndarray]]:
     return out
 
 
+def config4_shapes():
+    """(lattice, cells per direction, lattice constant) of the config-4
+    supercells: every fcc (a = 3.55) and bcc (a = 2.86) box of 2..6 cells per
+    direction, sorted dimensions, with 64..216 atoms."""
+    out = []
+    for kind, per, a in (("fcc", 4, 3.55), ("bcc", 2, 2.86)):
+        for n1 in range(2, 7):
+            for n2 in range(n1, 7):
+                for n3 in range(n2, 7):
+                    if 64 <= per * n1 * n2 * n3 <= 216:
+                        out.append((kind, (n1, n2, n3), a))
+    return out
+
+
 def config4_structures(n_struct: int = 8192, seed: int = 4) -> List[Dict[str, np.ndarray]]:
-    """Ni/Al fcc or bcc supercells of 64-216 atoms, random composition,
-    symmetric strain U(-0.03, 0.03), sigma=0.1."""
+    """Ni/Al fcc or bcc supercells of 64-216 atoms (config4_shapes, drawn
+    uniformly), random composition, symmetric strain U(-0.03, 0.03),
+    sigma=0.1."""
     rng = np.random.default_rng(seed)
-    choices = [("fcc", 3, 3.55), ("fcc", 4, 3.55),   # 108, 256 -> 256 exceeds; filtered
-               ("bcc", 4, 2.86), ("bcc", 5, 2.86), ("fcc", 3, 3.52), ("bcc", 4, 2.88)]
-    choices = [c for c in choices if 64 <= (4 if c[0] == "fcc" else 2) * c[1] ** 3 <= 216]
+    choices = config4_shapes()
     out = []
     for _ in range(n_struct):
         kind, reps, a = choices[int(rng.integers(0, len(choices)))]
@@ -90,6 +105,16 @@ def config4_structures(n_struct: int = 8192, seed: int = 4) -> List[Dict[str, np
         out.append({"cell": cell, "pbc": np.array([1, 1, 1], dtype=np.int32),
                     "positions": np.ascontiguousarray(pos), "types": types})
     return out
+
+
+def level24_model(species_count: int = 2, rmin: float = 2.0, rmax: float = 5.0,
+                  rb_size: int = 8, seed: int = 24) -> MTPModel:
+    """Generated level-24 basis (basisgen) with seeded U(-0.1, 0.1)
+    coefficients: the stand-in for the level-24 models of configs 4 and 5."""
+    from .basisgen import generate
+    m = generate(24, species_count=species_count, min_dist=rmin, max_dist=rmax,
+                 rb_size=rb_size)
+    return seeded_coefficients(m, seed)
 
 
 def seeded_coefficients(model: MTPModel, seed: int, low: float = -0.1,
