@@ -9,9 +9,20 @@ steps (steps between rebuilds upload positions and refresh the edge vectors
 from the stored periodic images).  Synthetic seeded data; the working set
 (~6 GB) is far larger than the 126 MB L2, so no L2 flush is needed.
 
+The same line carries a "train" object for the second half of the metric,
+"train configs/sec": config 4 of BASELINE.json, 8192 Ni/Al fcc/bcc supercells
+of 64-216 atoms (seed 4), a seeded level-24 student MTP (generated basis, see
+mtpb200/basisgen.py) fitted to labels of a seeded level-24 teacher plus
+Gaussian noise (1 meV/atom on E/N, 10 meV/A per force component, 0.1 GPa per
+stress component as virial), weights E 1, F 0.01, S 0.001 with the reference's
+default powers.  One step = loss and coefficient gradient over all 8192
+configurations (EFS pass, loss, gradient kernels, reductions).
+
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 Multi-GPU: launched by torch.distributed.run, one rank per GPU; every rank
-evaluates its own copy of the box (independent replicas, weak scaling).
+evaluates its own copy of the box (independent replicas, weak scaling); the
+training leg shards the 8192 configurations over the ranks and sums loss,
+metrics and gradient with an NCCL all-reduce (strong scaling).
 """
 from __future__ import annotations
 
@@ -32,6 +43,10 @@ MODEL = os.path.join(ROOT, "tests", "golden", "models", "l20_k2.mtp")
 METRIC = "MTP EFS atoms/sec (1M-atom, level 20)"
 UNIT = "atoms/s"
 REBUILD_EVERY = 10
+TRAIN_METRIC = "MTP train configs/sec (config 4: 8192 configs of 64-216 atoms, level 24)"
+TRAIN_UNIT = "configs/s"
+TRAIN_WEIGHTS = (1.0, 0.01, 0.001, 1.0, 0.0, 1.0)   # E, F, S and the default powers
+EV_PER_GPA_A3 = 1.0 / 160.21766208                    # 1 GPa * 1 A^3 in eV
 
 # DRAM traffic per atom of the dominant kernel, from the ncu capture
 # summarised in profiles/ (scaled from the 131k-atom capture by atom count).
@@ -47,6 +62,10 @@ def parse():
     ap.add_argument("--reps", type=int, default=64, help="fcc cells per box edge")
     ap.add_argument("--ref-reps", type=int, default=10,
                     help="box edge (cells) of the bounded CPU sample")
+    ap.add_argument("--train-configs", type=int, default=8192)
+    ap.add_argument("--train-steps", type=int, default=5)
+    ap.add_argument("--train-warmup", type=int, default=3)
+    ap.add_argument("--no-train", action="store_true", help="skip the training leg")
     ap.add_argument("--profile", action="store_true",
                     help="device loop only (no e2e loop, peak probe or CPU baseline): the "
                          "command used for ncu captures")
@@ -239,6 +258,193 @@ def cpu_reference_sample(model, reps, steps, warmup, threads):
 
 
 # ---------------------------------------------------------------------------
+# Training workload (config 4)
+# ---------------------------------------------------------------------------
+def train_problem(n_configs):
+    from mtpb200 import configs
+    sts = configs.config4_structures(n_configs, seed=4)
+    teacher = configs.level24_model(seed=41)
+    student = configs.level24_model(seed=42)
+    return sts, teacher, student
+
+
+def noisy_labels(sts, energy, forces, stress, seed=44):
+    """Teacher outputs plus Gaussian noise: 1 meV/atom on E/N, 10 meV/A per
+    force component, 0.1 GPa per stress component (virial = sigma V)."""
+    rng = np.random.default_rng(seed)
+    n = np.array([len(s["types"]) for s in sts], dtype=np.float64)
+    vol = np.array([abs(np.linalg.det(s["cell"])) for s in sts])
+    te = energy + rng.normal(0.0, 1e-3, len(sts)) * n
+    tf = forces + rng.normal(0.0, 0.01, forces.shape)
+    ts = stress.reshape(-1, 9) + rng.normal(0.0, 0.1, (len(sts), 9)) * \
+        (vol * EV_PER_GPA_A3)[:, None]
+    return te, np.ascontiguousarray(tf), np.ascontiguousarray(ts)
+
+
+def _cpu_train_worker(job):
+    """One process of the CPU training baseline: loss and gradient of a shard
+    with the C restatement (oracle port), neighbour lists built untimed."""
+    model, sts, te, tf, ts = job
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    sys.path.insert(0, os.path.join(ROOT, "imr-mlp_b200"))
+    from oracle import Oracle, concat_lists  # test infrastructure: baseline leg only
+    from mtpb200 import configs
+    O = Oracle()
+    offs, _, _, _, types = configs.batch(sts)
+    nl = concat_lists([O.neighbors(s["cell"], s["pbc"], s["positions"], model.cutoff)
+                       for s in sts], offs)
+    t0 = time.perf_counter()
+    loss, metrics, grad = O.loss_grad(model, offs, types, nl, te, tf, ts, TRAIN_WEIGHTS)
+    return time.perf_counter() - t0, loss, grad
+
+
+def cpu_train_sample(student, sts, labels, threads, per_worker=8):
+    """Oracle port of the reference trainer's loss and gradient over a bounded
+    sample (per_worker configurations on each of `threads` spawned
+    processes); configs/s = sample size / slowest worker."""
+    import concurrent.futures as cf
+    import multiprocessing as mp
+    te, tf, ts = labels
+    n = min(len(sts), per_worker * threads)
+    offs = np.cumsum([0] + [len(s["types"]) for s in sts[:n]])
+    jobs = []
+    for w in range(threads):
+        idx = list(range(w * per_worker, min(n, (w + 1) * per_worker)))
+        if not idx:
+            break
+        jobs.append((student, [sts[i] for i in idx], te[idx],
+                     np.concatenate([tf[offs[i]:offs[i + 1]] for i in idx]), ts[idx]))
+    with cf.ProcessPoolExecutor(max_workers=len(jobs),
+                                mp_context=mp.get_context("spawn")) as ex:
+        res = list(ex.map(_cpu_train_worker, jobs))
+    slowest = max(r[0] for r in res)
+    atoms = int(offs[n])
+    return {"value": n / slowest, "unit": TRAIN_UNIT, "cores": len(jobs), "kind": "port",
+            "sample": f"{n} config-4 structures ({atoms} atoms), level-24 student, oracle port "
+                      f"of AddLossGard + AccumulateEFSCombinationGard, {len(jobs)} processes "
+                      f"x {per_worker} configs; slowest process {slowest:.2f} s",
+            "ms_per_config": slowest / per_worker * 1e3}
+
+
+def train_flops(model, edges_per_atom, records):
+    """Executed FLOPs per atom of the gradient kernels (FMA = 2)."""
+    numax = [v for v in model.basis_shape() if v >= 0]
+    nmu, R = len(numax), model.rb_size
+    chains = shape_chains(numax)
+    stage = 25 + 8 * max(R - 2, 0) + 4 * R * nmu + 20 + nmu
+    tan = edge = 0
+    for b, c, L, cnts in chains:
+        tan += 6 + 4 * (L - 1) + 4 * sum(cnts)
+        edge += 6 + 4 * (L - 1) + 6 * sum(cnts)
+    return {"tangent_per_atom": (stage + tan) * edges_per_atom,
+            "edge_per_atom": (35 + edge) * edges_per_atom,
+            "dual_graph_per_atom": 8.0 * records,
+            "radial_per_atom": (4 * R + 4 * R * nmu) * edges_per_atom}
+
+
+def run_train(args, torch, dist, ws, rank, local, dev, stream):
+    """Training leg on every rank; returns the JSON object on rank 0."""
+    from mtpb200 import MTPGpuDirect, StructureBatch
+    sts, teacher, student = train_problem(args.train_configs)
+    mine = sts[rank::ws]
+    batch = StructureBatch.from_structures(mine)
+    with MTPGpuDirect(teacher, local) as tg:   # labels (untimed)
+        e, f, st, _ = tg.efs(batch)
+    te, tf, ts = noisy_labels(mine, e, f, st)
+    gpu = MTPGpuDirect(student, local)
+    gpu.set_stream(stream.cuda_stream)
+    gpu.build_neighbors(batch)
+    ncoef = student.coeff_count
+    te_d, tf_d, ts_d = (torch.from_numpy(a).to(dev) for a in (te, tf, ts))
+    out = torch.zeros(8 + ncoef, dtype=torch.float64, device=dev)
+    loss_d, metrics_d, grad_d = out[0:1], out[1:8], out[8:]
+    total = len(sts)
+
+    def step():
+        gpu.loss_grad_device(te_d, tf_d, ts_d, loss_d, metrics_d, grad_d, TRAIN_WEIGHTS,
+                             norm_count=total)
+        if ws > 1:
+            dist.all_reduce(out)
+
+    for _ in range(args.train_warmup):
+        step()
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    t0.record(stream)
+    for _ in range(args.train_steps):
+        step()
+        launches += gpu.last_launch_count() + (1 if ws > 1 else 0)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    if ws > 1:
+        dist.barrier()
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    tms = gpu.last_train_timings()
+    ems = gpu.last_timings()
+    loss = float(loss_d.item())
+    # end to end through the host API: labels H2D and loss/metrics/gradient
+    # D2H every step (single GPU only: the shards' sum needs the device path)
+    e2e = None
+    if ws == 1:
+        for _ in range(2):
+            gpu.loss_grad(te, tf, ts, TRAIN_WEIGHTS, total)
+        torch.cuda.synchronize()
+        h0 = time.perf_counter()
+        for _ in range(args.train_steps):
+            gpu.loss_grad(te, tf, ts, TRAIN_WEIGHTS, total)
+        h_ms = (time.perf_counter() - h0) * 1e3
+        e2e = {"value": total * args.train_steps / (h_ms / 1e3), "unit": TRAIN_UNIT,
+               "h2d_bytes_per_step": int(te.nbytes + tf.nbytes + ts.nbytes),
+               "d2h_bytes_per_step": int(8 * (8 + ncoef)),
+               "timer": "host wall clock around the blocking host-memory calls"}
+    N = batch.n_atoms
+    edges = gpu.neighbor_count()
+    gpu.close()
+    if rank != 0:
+        return None
+    recs = dag_record_count(student)
+    fl = train_flops(student, edges / N, recs)
+    names = {2: ("k_grad_moments<tangent>", fl["tangent_per_atom"]),
+             3: ("k_dag_grad", fl["dual_graph_per_atom"]),
+             4: ("k_grad_moments<edge>", fl["edge_per_atom"])}
+    dom = max(names, key=lambda i: tms[i])
+    kname, kflops = names[dom]
+    achieved = kflops * N / (tms[dom] / 1e3) / 1e12
+    res = {
+        "metric": TRAIN_METRIC, "value": total * args.train_steps / (ms / 1e3),
+        "unit": TRAIN_UNIT, "n_gpus": ws, "steps": args.train_steps,
+        "warmup": args.train_warmup, "ms_per_step": ms / args.train_steps,
+        "higher_is_better": True, "scaling": "strong", "dtype": "f64",
+        "data": "synthetic (seeded config-4 structures, teacher labels plus seeded noise)",
+        "config": {"workload": f"config 4: {total} configurations, level-24 generated basis "
+                               f"(nb {student.alpha_index_basic_count}, T "
+                               f"{student.alpha_index_times_count}, S "
+                               f"{student.alpha_scalar_moments}), K=2, R=8, r_cut=5",
+                   "atoms_per_gpu": N, "edges_per_gpu": edges,
+                   "parallelism": f"dp{ws}" if ws > 1 else "single",
+                   "weights": TRAIN_WEIGHTS, "loss": loss,
+                   "l2": "working set ~25 GB per GPU, larger than L2 (no flush)"},
+        "kernel_ms": {"efs_pass": float(tms[0]), "efs_moments_fwd": float(ems[1]),
+                      "efs_graph": float(ems[2]), "efs_moments_rev": float(ems[3]),
+                      "efs_gather_reduce": float(ems[4]), "loss_weights_buckets": float(tms[1]),
+                      "tangent_moments": float(tms[2]), "dual_graph": float(tms[3]),
+                      "edge_records": float(tms[4]), "radial_reduce": float(tms[5])},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "fp64", "kernel": kname, "achieved": achieved, "unit": "TFLOP/s",
+                     "flops_per_atom": kflops},
+        "e2e": e2e,
+    }
+    return res, (student, sts, (te, tf, ts))
+
+
+# ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
 def run_ours(args):
@@ -352,6 +558,7 @@ def run_ours(args):
     d2h = N * 24 + 8 + 72
     e2e_ok = abs(float(out["energy"][0]) - energy) <= 1e-9 * max(1.0, abs(energy))
 
+    train = None if args.no_train else run_train(args, torch, dist, ws, rank, local, dev, stream)
     peak = fp64_peak_tflops(torch, dev) if rank == 0 else None
     if ws > 1:
         dist.barrier()
@@ -399,12 +606,23 @@ def run_ours(args):
         "clocks": clocks,
         "energy_eV": energy,
     }
+    threads = os.cpu_count() or 1
     try:
-        threads = os.cpu_count() or 1
         line["cpu_baseline"] = cpu_reference_sample(model, args.ref_reps, 3, 1, threads)
     except Exception as exc:   # reference build absent on this machine
         line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": 0, "kind": "reference",
                                 "sample": f"unavailable: {exc}"}
+    if train is not None:
+        tline, (student, tsts, labels) = train
+        tline["roofline"]["peak"] = peak
+        tline["roofline"]["frac"] = tline["roofline"]["achieved"] / peak if peak else None
+        if ws == 1:
+            try:
+                tline["cpu_baseline"] = cpu_train_sample(student, tsts, labels, threads)
+            except Exception as exc:
+                tline["cpu_baseline"] = {"value": None, "unit": TRAIN_UNIT, "cores": 0,
+                                         "kind": "port", "sample": f"unavailable: {exc}"}
+        line["train"] = tline
     return line
 
 
@@ -417,7 +635,10 @@ def run_reference(args):
     threads = os.cpu_count() or 1
     r = cpu_reference_sample(model, args.ref_reps, max(args.steps, 1), max(args.warmup, 0),
                              threads)
-    return {"metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": ws,
+    train = None
+    if not args.no_train:
+        train = reference_train_line(args, threads, ws)
+    line = {"metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
             "data": "synthetic (seeded Ni3Al L1_2 box, seeded level-20 coefficients)",
@@ -427,6 +648,37 @@ def run_reference(args):
             "impl": "reference", "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores",
                                                                    "kind", "sample")},
             "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    if train is not None:
+        line["train"] = train
+    return line
+
+
+def reference_train_line(args, threads, ws):
+    """CPU training baseline for the reference arm: teacher labels from the
+    oracle EFS (untimed), then the oracle port's loss and gradient on all
+    host cores.  The reference's own trainer (train/train_mtp.cpp) does not
+    compile here, so the port stands in for it."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import Oracle  # test infrastructure: reference arm only
+    n = min(args.train_configs, 8 * threads)
+    sts, teacher, student = train_problem(n)
+    O = Oracle()
+    es, fs, ss = [], [], []
+    for x in sts:
+        nl = O.neighbors(x["cell"], x["pbc"], x["positions"], teacher.cutoff)
+        e, _, f, w = O.efs(teacher, x["types"], nl)
+        es.append(e)
+        fs.append(f)
+        ss.append(w.reshape(9))
+    labels = noisy_labels(sts, np.array(es), np.concatenate(fs), np.stack(ss))
+    r = cpu_train_sample(student, sts, labels, threads)
+    return {"metric": TRAIN_METRIC, "value": r["value"], "unit": TRAIN_UNIT, "n_gpus": ws,
+            "ms_per_step": r["ms_per_config"] * args.train_configs / r["cores"],
+            "higher_is_better": True, "scaling": "strong", "dtype": "f64",
+            "impl": "reference", "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores",
+                                                                   "kind", "sample")},
+            "e2e": {"value": r["value"], "unit": TRAIN_UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
 
 

@@ -362,6 +362,9 @@ int mtpb_destroy(mtpb_context *c)
     for (auto &ev : c->ev)
         if (ev)
             cudaEventDestroy(ev);
+    for (auto &ev : c->train.ev)
+        if (ev)
+            cudaEventDestroy(ev);
     if (c->own_stream)
         cudaStreamDestroy(c->own_stream);
     delete c;
@@ -769,6 +772,22 @@ int mtpb_last_timings(const mtpb_context *c, double *ms)
     for (int i = 0; i < 5; ++i) {
         CUDA_TRY(cudaEventElapsedTime(&t[i], c->ev[i], c->ev[i + 1]), "elapsed");
         ms[i] = t[i];
+    }
+    return MTPB_OK;
+}
+
+int mtpb_last_train_timings(const mtpb_context *c, double *ms)
+{
+    if (!c || !ms)
+        return fail(MTPB_ERR_ARGUMENT, "NULL argument");
+    if (!c->train.ev_valid)
+        return fail(MTPB_ERR_STATE, "no mtpb_loss_grad call has been timed");
+    CUDA_TRY(cudaSetDevice(c->device), "cudaSetDevice");
+    CUDA_TRY(cudaEventSynchronize(c->train.ev[6]), "event sync");
+    for (int i = 0; i < 6; ++i) {
+        float t = 0.f;
+        CUDA_TRY(cudaEventElapsedTime(&t, c->train.ev[i], c->train.ev[i + 1]), "elapsed");
+        ms[i] = t;
     }
     return MTPB_OK;
 }

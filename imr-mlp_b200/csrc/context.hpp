@@ -26,6 +26,8 @@ struct TrainingState {
     long bucket_epoch = -1;           // edge_epoch the pair buckets belong to
     int *perm = nullptr;              // edges sorted by species pair
     long *bounds = nullptr;           // bucket start positions [K*K+2]
+    cudaEvent_t ev[7] = {};           // timing events of the last call
+    bool ev_valid = false;
 };
 int upload_training_program(mtpb_context *c);
 

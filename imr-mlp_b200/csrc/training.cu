@@ -457,10 +457,17 @@ int loss_grad_compute(mtpb_context *c, const mtpb_labels *labels, const mtpb_los
         return rc;
     if (!c->train.ready && (rc = upload_training_program(c)))
         return rc;
+    cudaEvent_t *tev = c->train.ev;
+    if (!tev[0])
+        for (int i = 0; i < 7; ++i)
+            CUDA_TRY(cudaEventCreate(&tev[i]), "cudaEventCreate");
+    c->train.ev_valid = false;
+    CUDA_TRY(cudaEventRecord(tev[0], c->stream), "event");
     // EFS pass: energies, forces, virials, basic moments and their adjoints
     mtpb_efs_output none{nullptr, nullptr, nullptr, nullptr};
     if ((rc = mtpb_efs_compute(c, MTPB_MEMORY_DEVICE, &none)))
         return rc;
+    CUDA_TRY(cudaEventRecord(tev[1], c->stream), "event");
     const double *d_energy = c->arena.get<double>("energy", S + 1);
     const double *d_forces = c->arena.get<double>("forces", 3 * (size_t)N + 1);
     const double *d_stress = c->arena.get<double>("stress", 9 * (size_t)S + 9);
@@ -527,15 +534,19 @@ int loss_grad_compute(mtpb_context *c, const mtpb_labels *labels, const mtpb_los
     }
     if ((rc = pair_buckets(c)))
         return rc;
+    CUDA_TRY(cudaEventRecord(tev[2], c->stream), "event");
     EdgeArgs a = edge_args(c, N, c->d_types, c->nb.offsets, c->nb.nbr, c->nb.rx, c->nb.ry,
                            c->nb.rz);
     CUDA_TRY(launch_moments_tangent(c->shape, a, wx, wy, wz, tangent, c->stream), "tangent");
+    CUDA_TRY(cudaEventRecord(tev[3], c->stream), "event");
     CUDA_TRY(launch_dag_grad(c->plan, c->train.recs, c->d_phase_row0, grid, c->nslot, N, c->npad,
                              basic, tangent, dlde_atom, adjoint2, epart, gscratch, c->d_err,
                              c->stream),
              "dual graph");
+    CUDA_TRY(cudaEventRecord(tev[4], c->stream), "event");
     CUDA_TRY(launch_edge_grad(c->shape, a, wx, wy, wz, adjoint, adjoint2, uv, c->stream),
              "edge gradient");
+    CUDA_TRY(cudaEventRecord(tev[5], c->stream), "event");
     c->launches += c->shape == SHAPE_L24 ? 4 : 3;
     const size_t rg_smem = sizeof(double) * RG_THREADS * (2 * m.R + 2 * nmu);
     CUDA_TRY(cudaFuncSetAttribute(k_radial_grad, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -567,7 +578,8 @@ int loss_grad_compute(mtpb_context *c, const mtpb_labels *labels, const mtpb_los
     if (grad)
         CUDA_TRY(cudaMemcpyAsync(grad, d_grad, sizeof(double) * ncoef, kind, c->stream),
                  "copy gradient");
-    CUDA_TRY(cudaEventRecord(c->ev[5], c->stream), "event");
+    CUDA_TRY(cudaEventRecord(tev[6], c->stream), "event");
+    c->train.ev_valid = true;
     if (memory == MTPB_MEMORY_HOST) {
         CUDA_TRY(cudaStreamSynchronize(c->stream), "gradient");
         if ((rc = check_device_error(c)))

@@ -303,6 +303,22 @@ class MTPGpuDirect:
                                        _lib.MEMORY_HOST, _dp(loss), _dp(metrics), _dp(grad)))
         return float(loss[0]), metrics, grad
 
+    def loss_grad_device(self, labels_energy, labels_forces, labels_stress, loss, metrics, grad,
+                         weights=(1.0, 0.01, 0.0001, 1.0, 0.0, 1.0), norm_count: int = 0):
+        """mtpb_loss_grad with device arrays (torch CUDA tensors; a label may be
+        None): loss[1], metrics[7] and grad[coeff_count] are written on the
+        context stream without a host synchronisation."""
+        lab = _lib.Labels(_tdp(labels_energy), _tdp(labels_forces), _tdp(labels_stress))
+        w = _lib.LossWeights(*weights)
+        _check(self.lib.mtpb_loss_grad(self.ctx, C.byref(lab), C.byref(w), int(norm_count),
+                                       _lib.MEMORY_DEVICE, _tdp(loss), _tdp(metrics),
+                                       _tdp(grad)))
+
+    def last_train_timings(self):
+        t = np.zeros(6)
+        _check(self.lib.mtpb_last_train_timings(self.ctx, _dp(t)))
+        return t
+
     # ---- diagnostics ----------------------------------------------------
     def last_timings(self):
         t = np.zeros(5)

@@ -95,6 +95,7 @@ SIGNATURES = [
     ("mtpb_loss_grad", C.c_int, [C.c_void_p, C.POINTER(Labels), C.POINTER(LossWeights), C.c_int,
                                  C.c_int, _dp, _dp, _dp]),
     ("mtpb_last_timings", C.c_int, [C.c_void_p, _dp]),
+    ("mtpb_last_train_timings", C.c_int, [C.c_void_p, _dp]),
     ("mtpb_last_launch_count", C.c_int, [C.c_void_p, _ip]),
     ("mtpb_get_site_moments", C.c_int, [C.c_void_p, _dp, _dp]),
     ("mtpb_get_edge_derivatives", C.c_int, [C.c_void_p, _dp]),

@@ -264,6 +264,12 @@ int mtpb_loss_grad(mtpb_context *ctx, const mtpb_labels *labels, const mtpb_loss
  * [2] moment graph, [3] reverse moments, [4] force gather and reductions. */
 int mtpb_last_timings(const mtpb_context *ctx, double *ms5);
 
+/* Device-side timing of the last mtpb_loss_grad call, milliseconds: [0] EFS
+ * pass, [1] loss terms, edge weights and species-pair buckets, [2] tangent
+ * moments, [3] dual moment graph, [4] per-edge channel records, [5] radial
+ * gradient, reductions and assembly.  No reference counterpart (diagnostic). */
+int mtpb_last_train_timings(const mtpb_context *ctx, double *ms6);
+
 /* Kernel launches issued by the last compute call. */
 int mtpb_last_launch_count(const mtpb_context *ctx, int *launches);
 
