@@ -16,7 +16,7 @@ template <> struct ShapeCfg<ShapeS1> { static constexpr int NW = 2; };
 template <> struct ShapeCfg<ShapeS2> { static constexpr int NW = 2; };
 template <> struct ShapeCfg<ShapeL16> { static constexpr int NW = 4; };
 template <> struct ShapeCfg<ShapeL20> { static constexpr int NW = 8; };
-template <> struct ShapeCfg<ShapeL24> { static constexpr int NW = 16; };
+template <> struct ShapeCfg<ShapeL24> { static constexpr int NW = 12; };
 template <> struct ShapeCfg<ShapePS> { static constexpr int NW = 4; };
 
 __device__ __forceinline__ double &SV(double *st, int row, int k, int lane)
