@@ -19,9 +19,11 @@ default powers.  One step = loss and coefficient gradient over all 8192
 configurations (EFS pass, loss, gradient kernels, reductions).
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
-Multi-GPU: launched by torch.distributed.run, one rank per GPU; every rank
-evaluates its own copy of the box (independent replicas, weak scaling); the
-training leg shards the 8192 configurations over the ranks and sums loss,
+Multi-GPU: launched by torch.distributed.run, one rank per GPU; the box is
+split into x-slabs, one per rank (mtpb200/slab.py): every step all-gathers the
+positions, evaluates the rank's own centres against the whole periodic box,
+reduce-scatters the partial forces and all-reduces energy and virial (strong
+scaling: total atoms of the one box per second); the training leg shards the 8192 configurations over the ranks and sums loss,
 metrics and gradient with an NCCL all-reduce (strong scaling).
 """
 from __future__ import annotations
@@ -461,6 +463,14 @@ def run_ours(args):
                                 device_id=dev)
     model = read_mtp(MODEL)
     st = configs.config3(reps=args.reps)
+    slab = ws > 1   # one box over all ranks: slabs along x, collectives per step
+    if slab:
+        from mtpb200.slab import SlabExchange, SlabLayout
+        L = SlabLayout(st["cell"], st["positions"], ws)
+        pos_slab = np.ascontiguousarray(st["positions"][L.order])
+        types_slab = np.ascontiguousarray(st["types"][L.order]).astype(np.int32)
+        st = dict(st, positions=L.to_local(pos_slab, rank), types=L.to_local(types_slab, rank))
+        n_own = int(L.counts[rank])
     batch = StructureBatch.from_structures([st])
     N = batch.n_atoms
     gpu = MTPGpuDirect(model, local)
@@ -468,6 +478,10 @@ def run_ours(args):
     stream = torch.cuda.Stream(dev)
     torch.cuda.set_stream(stream)
     gpu.set_stream(stream.cuda_stream)
+    if slab:
+        gpu.set_center_count(n_own)
+        X = SlabExchange(L, rank, dist, dev)
+        own_d = torch.from_numpy(pos_slab[L.starts[rank]:L.starts[rank + 1]]).to(dev)
 
     # device-resident inputs and outputs
     offs_d = torch.from_numpy(batch.atom_offsets).to(dev)
@@ -478,21 +492,21 @@ def run_ours(args):
     energy_d = torch.zeros(1, dtype=torch.float64, device=dev)
     forces_d = torch.zeros((N, 3), dtype=torch.float64, device=dev)
     stress_d = torch.zeros((1, 9), dtype=torch.float64, device=dev)
+    totals_d = torch.zeros(10, dtype=torch.float64, device=dev)
+    f_own = None
 
     def step(k):
-        gpu.efs_device(offs_d, cells_d, pbc_d, pos_d, types_d, energy_d, forces_d, stress_d,
+        nonlocal f_own
+        x = pos_d
+        if slab:   # (1) positions of every slab, in this rank's rotated order
+            x = L.to_local(X.gather_positions(own_d), rank)
+        gpu.efs_device(offs_d, cells_d, pbc_d, x, types_d, energy_d, forces_d, stress_d,
                        reuse_neighbors=(k % REBUILD_EVERY) != 0)
-
-    def barrier():
-        if ws > 1:
-            dist.barrier()
-
-    def max_over_ranks(x):
-        if ws == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        if slab:   # (3) sum partial forces into the owners, totals everywhere
+            f_own = X.reduce_forces(L.to_slab(forces_d, rank))
+            totals_d[0:1].copy_(energy_d)
+            totals_d[1:].copy_(stress_d.view(-1))
+            X.reduce_totals(totals_d)
 
     for k in range(args.warmup):
         step(k)
@@ -523,7 +537,7 @@ def run_ours(args):
     step(0)
     torch.cuda.synchronize()
     build_ms = gpu.last_timings()[0]
-    energy = float(energy_d.item())
+    energy = float(totals_d[0].item()) if slab else float(energy_d.item())
 
     if args.profile:
         if rank == 0:
@@ -534,29 +548,51 @@ def run_ours(args):
         return None
     # end-to-end through the public host API: pinned host buffers, H2D of the
     # positions every step (types and cell too on rebuild steps), D2H of the
-    # energy, forces and virial every step
-    pos_h = torch.from_numpy(batch.positions).pin_memory()
-    types_h = torch.from_numpy(batch.types).pin_memory()
-    hb = StructureBatch(batch.atom_offsets, batch.cells, None, pos_h.numpy(), types_h.numpy())
-    out = {"energy": torch.zeros(1, dtype=torch.float64).pin_memory().numpy(),
-           "forces": torch.zeros((N, 3), dtype=torch.float64).pin_memory().numpy(),
-           "stress": torch.zeros((1, 9), dtype=torch.float64).pin_memory().numpy()}
+    # energy, forces and virial every step; with slabs each rank copies its own
+    # slab in and its own forces and the totals out
+    n_rebuild = sum(1 for k in range(args.steps) if k % REBUILD_EVERY == 0)
+    if slab:
+        own_h = torch.from_numpy(pos_slab[L.starts[rank]:L.starts[rank + 1]].copy()).pin_memory()
+        f_h = torch.zeros((n_own, 3), dtype=torch.float64).pin_memory()
+        t_h = torch.zeros(10, dtype=torch.float64).pin_memory()
+
+        def e2e_step(k):
+            own_d.copy_(own_h, non_blocking=True)
+            step(k)
+            f_h.copy_(f_own, non_blocking=True)
+            t_h.copy_(totals_d, non_blocking=True)
+            stream.synchronize()
+
+        h2d = n_own * 24
+        d2h = n_own * 24 + 80
+    else:
+        pos_h = torch.from_numpy(batch.positions).pin_memory()
+        types_h = torch.from_numpy(batch.types).pin_memory()
+        hb = StructureBatch(batch.atom_offsets, batch.cells, None, pos_h.numpy(),
+                            types_h.numpy())
+        out = {"energy": torch.zeros(1, dtype=torch.float64).pin_memory().numpy(),
+               "forces": torch.zeros((N, 3), dtype=torch.float64).pin_memory().numpy(),
+               "stress": torch.zeros((1, 9), dtype=torch.float64).pin_memory().numpy()}
+
+        def e2e_step(k):
+            gpu.efs_structures(hb, reuse_neighbors=(k % REBUILD_EVERY) != 0, out=out)
+
+        h2d = (N * 24 * args.steps + n_rebuild * (N * 4 + 9 * 8 + 8)) / args.steps
+        d2h = N * 24 + 8 + 72
     for k in range(args.warmup):
-        gpu.efs_structures(hb, reuse_neighbors=(k % REBUILD_EVERY) != 0, out=out)
+        e2e_step(k)
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for k in range(args.steps):
-        gpu.efs_structures(hb, reuse_neighbors=(k % REBUILD_EVERY) != 0, out=out)
+        e2e_step(k)
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-    n_rebuild = sum(1 for k in range(args.steps) if k % REBUILD_EVERY == 0)
-    h2d = (N * 24 * args.steps + n_rebuild * (N * 4 + 9 * 8 + 8)) / args.steps
-    d2h = N * 24 + 8 + 72
-    e2e_ok = abs(float(out["energy"][0]) - energy) <= 1e-9 * max(1.0, abs(energy))
+    e2e_energy = float(t_h[0]) if slab else float(out["energy"][0])
+    e2e_ok = abs(e2e_energy - energy) <= 1e-9 * max(1.0, abs(energy))
 
     train = None if args.no_train else run_train(args, torch, dist, ws, rank, local, dev, stream)
     peak = fp64_peak_tflops(torch, dev) if rank == 0 else None
@@ -572,22 +608,26 @@ def run_ours(args):
              3: ("k_moments<rev>", fm["rev_per_atom"])}
     dom = max(names, key=lambda i: kernel_ms[i])
     kname, kflops = names[dom]
-    achieved = kflops * N / (kernel_ms[dom] / 1e3) / 1e12
-    total_atoms = N * ws * args.steps
+    n_centers = n_own if slab else N
+    achieved = kflops * n_centers / (kernel_ms[dom] / 1e3) / 1e12
+    total_atoms = N * (1 if slab else ws) * args.steps
     value = total_atoms / (ms / 1e3)
     step_ms = float(kernel_ms[1:].sum())
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "scaling": "strong" if slab else "weak", "vs_baseline": None, "dtype": "f64",
         "data": "synthetic (seeded Ni3Al L1_2 box, seeded level-20 coefficients)",
         "config": {"workload": f"config 3: {N}-atom Ni3Al box, level-20 MTP, EFS steps with a "
-                               f"neighbour rebuild every {REBUILD_EVERY} steps",
-                   "atoms_per_gpu": N, "edges_per_gpu": edges, "level": 20, "species": 2,
-                   "rb_size": 8, "r_cut": 5.0, "skin": 0.0,
-                   "parallelism": f"replicas{ws}" if ws > 1 else "single",
+                               f"neighbour rebuild every {REBUILD_EVERY} steps"
+                               + (f"; one box over {ws} GPUs in x-slabs (all-gather of "
+                                  "positions, reduce-scatter of partial forces, all-reduce "
+                                  "of energy and virial every step)" if slab else ""),
+                   "atoms_per_gpu": n_centers, "edges_per_gpu": edges, "level": 20,
+                   "species": 2, "rb_size": 8, "r_cut": 5.0, "skin": 0.0,
+                   "parallelism": f"slab{ws}" if slab else "single",
                    "l2": "working set ~6 GB per GPU, larger than L2 (no flush)"},
-        "e2e": {"value": N * ws * args.steps / (e2e_ms / 1e3), "unit": UNIT,
+        "e2e": {"value": total_atoms / (e2e_ms / 1e3), "unit": UNIT,
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "matches_device_energy": e2e_ok},
         "gpu_launches": int(launches),

@@ -425,6 +425,15 @@ int mtpb_set_skin(mtpb_context *c, double skin)
     return MTPB_OK;
 }
 
+int mtpb_set_center_count(mtpb_context *c, int center_count)
+{
+    if (!c || center_count < 0)
+        return fail(MTPB_ERR_ARGUMENT, "center_count must be >= 0");
+    c->center_count_req = center_count;
+    c->have_list = false;
+    return MTPB_OK;
+}
+
 int mtpb_build_neighbors(mtpb_context *c, const mtpb_structures *in, int memory)
 {
     if (!c)
@@ -531,9 +540,15 @@ int mtpb_build_neighbors(mtpb_context *c, const mtpb_structures *in, int memory)
                 return fail(MTPB_ERR_ARGUMENT, "atom " + std::to_string(i) +
                                                    " has a species index outside 0..K-1");
     }
+    const int NC = c->center_count_req > 0 ? c->center_count_req : N;
+    if (NC > N)
+        return fail(MTPB_ERR_ARGUMENT, "center count " + std::to_string(NC) +
+                                           " exceeds the batch's " + std::to_string(N) +
+                                           " atoms");
     NbBuildInput bi;
     bi.nstruct = S;
     bi.natoms = N;
+    bi.ncenter = NC;
     bi.total_cells = cells;
     bi.atom_offsets = d_aoff;
     bi.structs = d_ns;
@@ -553,16 +568,17 @@ int mtpb_build_neighbors(mtpb_context *c, const mtpb_structures *in, int memory)
         CUDA_TRY(cudaMemcpyAsync(c->d_x_build, d_pos, sizeof(double) * 3 * N,
                                  cudaMemcpyDeviceToDevice, c->stream),
                  "keep positions");
-    c->natoms = N;
+    c->natoms = NC;   // centres: atoms [0, NC)
     c->ntotal = N;
     c->nstruct = S;
     c->d_types = d_types;
     c->d_offsets = res.offsets;
-    // reduction segments: <= 1024 atoms of one structure each
+    // reduction segments: <= 1024 centres of one structure each
     std::vector<int> sb, se, s0(S + 1, 0);
     for (int s = 0; s < S; ++s) {
         s0[s] = (int)sb.size();
-        const int a0 = c->h_atom_offsets[s], a1 = c->h_atom_offsets[s + 1];
+        const int a0 = std::min(c->h_atom_offsets[s], NC);
+        const int a1 = std::min(c->h_atom_offsets[s + 1], NC);
         if (a0 == a1) {
             sb.push_back(a0);
             se.push_back(a1);
@@ -651,7 +667,7 @@ int mtpb_efs_compute(mtpb_context *c, int memory, const mtpb_efs_output *out)
     if (rc)
         return rc;
     const bool dev = memory == MTPB_MEMORY_DEVICE;
-    const int N = c->natoms, S = c->nstruct;
+    const int N = c->natoms, NT = c->ntotal, S = c->nstruct;   // centres, all atoms
     const long E = c->nedges;
     c->launches = c->nb_built_this_call ? c->pending_launches : 0;
     c->pending_launches = 0;
@@ -661,7 +677,7 @@ int mtpb_efs_compute(mtpb_context *c, int memory, const mtpb_efs_output *out)
     double *dx = c->arena.get<double>("dx", E + 1), *dy = c->arena.get<double>("dy", E + 1),
            *dz = c->arena.get<double>("dz", E + 1);
     double *forces = (dev && out && out->forces) ? out->forces
-                                                 : c->arena.get<double>("forces", 3 * (size_t)N + 1);
+                                                 : c->arena.get<double>("forces", 3 * (size_t)NT + 1);
     double *avir = c->arena.get<double>("atom_virial", 9 * (size_t)N + 1);
     double *partials = c->arena.get<double>("partials", 10 * (size_t)c->nseg + 10);
     double *energy = (dev && out && out->energy) ? out->energy
@@ -674,7 +690,7 @@ int mtpb_efs_compute(mtpb_context *c, int memory, const mtpb_efs_output *out)
                      site_energy, dx, dy, dz);
     if (rc)
         return rc;
-    CUDA_TRY(launch_force_gather(N, N, c->nb.offsets, c->nb.in_offsets, c->nb.in_edges, dx, dy, dz,
+    CUDA_TRY(launch_force_gather(N, NT, c->nb.offsets, c->nb.in_offsets, c->nb.in_edges, dx, dy, dz,
                                  c->nb.rx, c->nb.ry, c->nb.rz, forces, avir, 0, c->stream),
              "force gather");
     CUDA_TRY(launch_segment_reduce(c->nseg, c->d_seg_begin, c->d_seg_end, site_energy, avir, N,
@@ -691,7 +707,7 @@ int mtpb_efs_compute(mtpb_context *c, int memory, const mtpb_efs_output *out)
         if (out->energy && !dev)
             CUDA_TRY(cudaMemcpyAsync(out->energy, energy, sizeof(double) * S, k, c->stream), "copy");
         if (out->forces && !dev)
-            CUDA_TRY(cudaMemcpyAsync(out->forces, forces, sizeof(double) * 3 * N, k, c->stream),
+            CUDA_TRY(cudaMemcpyAsync(out->forces, forces, sizeof(double) * 3 * NT, k, c->stream),
                      "copy");
         if (out->stress && !dev)
             CUDA_TRY(cudaMemcpyAsync(out->stress, stress, sizeof(double) * 9 * S, k, c->stream),
@@ -737,7 +753,7 @@ int mtpb_efs_structures(mtpb_context *c, const mtpb_structures *in, int memory,
     } else {
         if ((rc = set_device(c)))
             return rc;
-        const int N = c->natoms;
+        const int N = c->ntotal;
         const double *x = in->positions;
         if (memory != MTPB_MEMORY_DEVICE && N) {
             double *p = c->arena.get<double>("in_positions", 3 * (size_t)N);

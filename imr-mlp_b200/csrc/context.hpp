@@ -62,7 +62,8 @@ struct mtpb_context {
     int *d_phase_row0 = nullptr;
     int *d_err = nullptr;   // device error flag (bounded waits that gave up)
     // current batch (structures path)
-    int nstruct = 0, natoms = 0, ntotal = 0;
+    int nstruct = 0, natoms = 0, ntotal = 0;   // natoms = centres, ntotal = all atoms
+    int center_count_req = 0;                  // mtpb_set_center_count (0 = all atoms)
     long nedges = 0;
     bool have_list = false;
     std::vector<int> h_atom_offsets;

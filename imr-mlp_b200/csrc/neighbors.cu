@@ -335,6 +335,7 @@ cudaError_t build_neighbors(const NbBuildInput &in, DeviceArena &arena, NbResult
                             cudaStream_t s)
 {
     const int N = in.natoms;
+    const int NC = in.ncenter < 0 ? N : in.ncenter;   // centres: atoms [0, NC)
     const int T = 256;
     cudaError_t err;
 #define CK(x)                                                                                      \
@@ -351,8 +352,8 @@ cudaError_t build_neighbors(const NbBuildInput &in, DeviceArena &arena, NbResult
     int *cell_start = arena.get<int>("nb_cell_start", in.total_cells + 1);
     int *cell_cursor = arena.get<int>("nb_cell_cursor", in.total_cells + 1);
     int *cell_atoms = arena.get<int>("nb_cell_atoms", N);
-    int *counts = arena.get<int>("nb_counts", N + 1);
-    int *offsets = arena.get<int>("offsets", N + 1);
+    int *counts = arena.get<int>("nb_counts", NC + 1);
+    int *offsets = arena.get<int>("offsets", NC + 1);
     if (!struct_of || !wx || !wy || !wz || !cell_of || !cell_count || !cell_start ||
         !cell_cursor || !cell_atoms || !counts || !offsets)
         return cudaErrorMemoryAllocation;
@@ -361,10 +362,11 @@ cudaError_t build_neighbors(const NbBuildInput &in, DeviceArena &arena, NbResult
     res.wz = wz;
     res.offsets = offsets;
     res.struct_of = struct_of;
-    if (N == 0) {
+    if (N == 0 || NC == 0) {
         CK(cudaMemsetAsync(offsets, 0, sizeof(int), s));
         res.nedges = 0;
-        return cudaSuccess;
+        if (N == 0)
+            return cudaSuccess;
     }
     CK(cudaMemsetAsync(cell_count, 0, sizeof(int) * (in.total_cells + 1), s));
     CK(cudaMemsetAsync(cell_cursor, 0, sizeof(int) * (in.total_cells + 1), s));
@@ -376,13 +378,14 @@ cudaError_t build_neighbors(const NbBuildInput &in, DeviceArena &arena, NbResult
     k_fill_cells<<<nblk(N, T), T, 0, s>>>(N, cell_of, cell_start, cell_cursor, cell_atoms);
     k_sort_segments<<<nblk(in.total_cells, T), T, 0, s>>>(in.total_cells, cell_start,
                                                           cell_atoms);
-    k_neighbors<false><<<nblk(N, 128), 128, 0, s>>>(N, in.structs, struct_of, wx, wy, wz, cell_of,
-                                                    cell_start, cell_atoms, counts, nullptr,
-                                                    nullptr, nullptr, nullptr, nullptr, nullptr);
+    if (NC > 0)
+        k_neighbors<false><<<nblk(NC, 128), 128, 0, s>>>(
+            NC, in.structs, struct_of, wx, wy, wz, cell_of, cell_start, cell_atoms, counts,
+            nullptr, nullptr, nullptr, nullptr, nullptr, nullptr);
     CK(cudaGetLastError());
-    CK(exclusive_scan(counts, offsets, N, arena, s));
+    CK(exclusive_scan(counts, offsets, NC, arena, s));
     int E = 0;
-    CK(cudaMemcpyAsync(&E, offsets + N, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(&E, offsets + NC, sizeof(int), cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
     res.nedges = E;
     int *nbr = arena.get<int>("nbr", (size_t)E + 1);
@@ -392,14 +395,16 @@ cudaError_t build_neighbors(const NbBuildInput &in, DeviceArena &arena, NbResult
     double *rz = arena.get<double>("rz", (size_t)E + 1);
     if (!nbr || !shift || !rx || !ry || !rz)
         return cudaErrorMemoryAllocation;
-    k_neighbors<true><<<nblk(N, 128), 128, 0, s>>>(N, in.structs, struct_of, wx, wy, wz, cell_of,
-                                                   cell_start, cell_atoms, nullptr, offsets, nbr,
-                                                   shift, rx, ry, rz);
+    if (NC > 0)
+        k_neighbors<true><<<nblk(NC, 128), 128, 0, s>>>(NC, in.structs, struct_of, wx, wy, wz,
+                                                        cell_of, cell_start, cell_atoms, nullptr,
+                                                        offsets, nbr, shift, rx, ry, rz);
     CK(cudaGetLastError());
     int *center = arena.get<int>("edge_center", (size_t)E + 1);
     if (!center)
         return cudaErrorMemoryAllocation;
-    k_edge_centers<<<nblk(N, 128), 128, 0, s>>>(N, offsets, center);
+    if (NC > 0)
+        k_edge_centers<<<nblk(NC, 128), 128, 0, s>>>(NC, offsets, center);
     res.center = center;
     res.nbr = nbr;
     res.shift = shift;

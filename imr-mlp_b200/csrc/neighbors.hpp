@@ -75,6 +75,7 @@ struct NbStruct {
 struct NbBuildInput {
     int nstruct = 0;
     int natoms = 0;
+    int ncenter = -1;   // centres are atoms [0, ncenter); -1: all atoms
     int total_cells = 0;
     const int *atom_offsets = nullptr;  // device [nstruct+1]
     const NbStruct *structs = nullptr;  // device [nstruct]

@@ -444,6 +444,9 @@ int loss_grad_compute(mtpb_context *c, const mtpb_labels *labels, const mtpb_los
         return fail(MTPB_ERR_STATE, "build the neighbour list first (mtpb_build_neighbors)");
     if (norm_count < 0)
         return fail(MTPB_ERR_ARGUMENT, "norm_count must be >= 0");
+    if (c->natoms != c->ntotal)
+        return fail(MTPB_ERR_STATE, "the loss needs every atom as a centre "
+                                    "(mtpb_set_center_count(ctx, 0) before the build)");
     const ModelHost &m = c->model;
     const int K = m.K, KK = K * K, S = c->nstruct, N = c->natoms;
     const long E = c->nedges;

@@ -179,6 +179,11 @@ class MTPGpuDirect:
         _check(self.lib.mtpb_set_skin(self.ctx, float(skin)))
 
     # ---- structures path ------------------------------------------------
+    def set_center_count(self, n: int):
+        """Centres = the first n atoms of later builds (0 = all atoms)."""
+        _check(self.lib.mtpb_set_center_count(self.ctx, int(n)))
+        self._centers = int(n)
+
     def build_neighbors(self, batch: StructureBatch):
         self._batch = batch
         st = batch.c_struct()
@@ -202,16 +207,18 @@ class MTPGpuDirect:
 
     def compute(self, site_energy: bool = False):
         """EFS of the last built batch: (energy[S], forces[N,3], stress[S,3,3],
-        site_energy[N] or None)."""
+        site_energy[centres] or None); with a centre count the forces are the
+        partial sums of those centres' site terms."""
         b = self._batch
         S, N = b.n_structures, b.n_atoms
+        nc = min(getattr(self, "_centers", 0) or N, N)
         e = np.zeros(max(S, 1))
         f = np.zeros((max(N, 1), 3))
         st = np.zeros((max(S, 1), 9))
-        se = np.zeros(max(N, 1)) if site_energy else None
+        se = np.zeros(max(nc, 1)) if site_energy else None
         out = _lib.EfsOutput(_dp(e), _dp(f), _dp(st), _dp(se))
         _check(self.lib.mtpb_efs_compute(self.ctx, _lib.MEMORY_HOST, C.byref(out)))
-        return e[:S], f[:N], st[:S].reshape(S, 3, 3), (se[:N] if se is not None else None)
+        return e[:S], f[:N], st[:S].reshape(S, 3, 3), (se[:nc] if se is not None else None)
 
     def efs_structures(self, batch: StructureBatch, reuse_neighbors: bool = False,
                        out=None):

@@ -96,6 +96,7 @@ SIGNATURES = [
                                  C.c_int, _dp, _dp, _dp]),
     ("mtpb_last_timings", C.c_int, [C.c_void_p, _dp]),
     ("mtpb_last_train_timings", C.c_int, [C.c_void_p, _dp]),
+    ("mtpb_set_center_count", C.c_int, [C.c_void_p, C.c_int]),
     ("mtpb_last_launch_count", C.c_int, [C.c_void_p, _ip]),
     ("mtpb_get_site_moments", C.c_int, [C.c_void_p, _dp, _dp]),
     ("mtpb_get_edge_derivatives", C.c_int, [C.c_void_p, _dp]),

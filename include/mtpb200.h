@@ -122,6 +122,14 @@ int mtpb_set_skin(mtpb_context *ctx, double skin);
 
 /* ---- structures: neighbour build + EFS ---------------------------------- */
 
+/* Centres of the structures path: subsequent builds evaluate the site terms of
+ * the first center_count atoms of the batch only (0 = every atom), with
+ * neighbours drawn from all atoms.  Forces are then partial sums for all atoms
+ * (the ghost contributions of MTPGpuBatchRequest, mtp_gpu_direct.h:451-517),
+ * energies and virials cover the centres.  Used by domain decompositions that
+ * reduce the partial forces across ranks; mtpb_loss_grad needs all atoms. */
+int mtpb_set_center_count(mtpb_context *ctx, int center_count);
+
 /* Builds the neighbour lists of all structures on the GPU (replaces
  * Neighborhoods(atoms, cutoff), base/neighborhood.cpp:149-157) and keeps them
  * in the context.  Per-atom neighbour sets equal the reference builder's bit
