@@ -508,6 +508,17 @@ def run_ours(args):
             totals_d[1:].copy_(stress_d.view(-1))
             X.reduce_totals(totals_d)
 
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if ws == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     for k in range(args.warmup):
         step(k)
     torch.cuda.synchronize()
