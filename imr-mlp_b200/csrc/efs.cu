@@ -557,29 +557,51 @@ __device__ __forceinline__ void dag_segment(unsigned rec_addr, const Rows<GR> &r
             acc[1] = 0.0;
         }
     };
-    int k = 0;
-    for (; k + 4 <= n; k += 4) {
-        uint4 w[4];
+    // groups of four records: the records and operand values of the next group
+    // are loaded before the current group is accumulated, so that shared-memory
+    // latency overlaps the FP64 work (rows written in this phase are never read
+    // in it, so the loads may pass the stores of earlier groups)
+    struct Grp {
+        double c[4];
         unsigned of[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            w[u] = lds128(rec_addr + (k + u) * REC_STRIDE);
-            of[u] = lds32(rec_addr + (k + u) * REC_STRIDE + 16);
-        }
         double2 x[4], y[4];
+    };
+    auto load = [&](Grp &g, int k) {
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            x[u] = rowsA.ld(w[u].x);
-            y[u] = rowsA.ld(w[u].y);
+            const uint4 w = lds128(rec_addr + (k + u) * REC_STRIDE);
+            g.of[u] = lds32(rec_addr + (k + u) * REC_STRIDE + 16);
+            g.c[u] = __hiloint2double((int)w.w, (int)w.z);
+            g.x[u] = rowsA.ld(w.x);
+            g.y[u] = rowsA.ld(w.y);
         }
+    };
+    auto accumulate = [&](const Grp &g) {
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            const double c = __hiloint2double((int)w[u].w, (int)w[u].z);
-            acc[0] = fma(c * x[u].x, y[u].x, acc[0]);
-            acc[1] = fma(c * x[u].y, y[u].y, acc[1]);
-            if (of[u])
-                rare(of[u], c);
+            acc[0] = fma(g.c[u] * g.x[u].x, g.y[u].x, acc[0]);
+            acc[1] = fma(g.c[u] * g.x[u].y, g.y[u].y, acc[1]);
+            if (g.of[u])
+                rare(g.of[u], g.c[u]);
         }
+    };
+    int k = 0;
+    if (n == G::CH && G::CH == 16) {   // full ring slot: fixed two-stage schedule
+        Grp a, b;
+        load(a, 0);
+        load(b, 4);
+        accumulate(a);
+        load(a, 8);
+        accumulate(b);
+        load(b, 12);
+        accumulate(a);
+        accumulate(b);
+        return;
+    }
+    for (; k + 4 <= n; k += 4) {
+        Grp a;
+        load(a, k);
+        accumulate(a);
     }
     for (; k < n; ++k) {
         const uint4 w = lds128(rec_addr + k * REC_STRIDE);

@@ -580,30 +580,51 @@ __device__ __forceinline__ void dag_grad_segment(unsigned rec_addr, const Rows<G
             accd = 0.0;
         }
     };
-    int k = 0;
-    for (; k + 4 <= n; k += 4) {
-        uint4 w[4];
+    // two-stage schedule as in the value graph (efs.cu dag_segment): the next
+    // group's records and operands are loaded before the current group is
+    // accumulated
+    struct Grp {
+        double c[4];
         unsigned of[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            w[u] = lds128(rec_addr + (k + u) * REC_STRIDE);
-            of[u] = lds32(rec_addr + (k + u) * REC_STRIDE + 16);
-        }
         double2 x[4], y[4];
+    };
+    auto load = [&](Grp &g, int k) {
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            x[u] = rowA.ld(w[u].x);
-            y[u] = rowA.ld(w[u].y);
+            const uint4 w = lds128(rec_addr + (k + u) * REC_STRIDE);
+            g.of[u] = lds32(rec_addr + (k + u) * REC_STRIDE + 16);
+            g.c[u] = __hiloint2double((int)w.w, (int)w.z);
+            g.x[u] = rowA.ld(w.x);
+            g.y[u] = rowA.ld(w.y);
         }
+    };
+    auto accumulate = [&](const Grp &g, int k) {
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            const double c = __hiloint2double((int)w[u].w, (int)w[u].z);
-            const double cx = c * x[u].x;
-            acc = fma(cx, y[u].x, acc);
-            accd = fma(cx, y[u].y, fma(c * x[u].y, y[u].x, accd));
-            if (of[u])
-                rare(of[u], rec_addr + (k + u) * REC_STRIDE);
+            const double cx = g.c[u] * g.x[u].x;
+            acc = fma(cx, g.y[u].x, acc);
+            accd = fma(cx, g.y[u].y, fma(g.c[u] * g.x[u].y, g.y[u].x, accd));
+            if (g.of[u])
+                rare(g.of[u], rec_addr + (k + u) * REC_STRIDE);
         }
+    };
+    int k = 0;
+    if (n == G::CH && G::CH == 16) {
+        Grp a, b;
+        load(a, 0);
+        load(b, 4);
+        accumulate(a, 0);
+        load(a, 8);
+        accumulate(b, 4);
+        load(b, 12);
+        accumulate(a, 8);
+        accumulate(b, 12);
+        return;
+    }
+    for (; k + 4 <= n; k += 4) {
+        Grp a;
+        load(a, k);
+        accumulate(a, k);
     }
     for (; k < n; ++k) {
         const unsigned ra = rec_addr + k * REC_STRIDE;
