@@ -367,7 +367,7 @@ __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, 
 }
 
 template <class S, bool REV>
-__global__ void __launch_bounds__(ShapeCfg<S>::NW * 32)
+__global__ void __launch_bounds__(ShapeCfg<S>::NW * 32, ShapeCfg<S>::NW <= 4 ? 2 : 1)
     k_moments(EdgeArgs p, double *basic, const double *adjoint, double *dx, double *dy,
               double *dz)
 {

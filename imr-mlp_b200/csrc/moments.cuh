@@ -15,7 +15,7 @@ template <class S> struct ShapeCfg;
 template <> struct ShapeCfg<ShapeS1> { static constexpr int NW = 2; };
 template <> struct ShapeCfg<ShapeS2> { static constexpr int NW = 2; };
 template <> struct ShapeCfg<ShapeL16> { static constexpr int NW = 4; };
-template <> struct ShapeCfg<ShapeL20> { static constexpr int NW = 8; };
+template <> struct ShapeCfg<ShapeL20> { static constexpr int NW = 4; };
 template <> struct ShapeCfg<ShapeL24> { static constexpr int NW = 12; };
 template <> struct ShapeCfg<ShapePS> { static constexpr int NW = 4; };
 
