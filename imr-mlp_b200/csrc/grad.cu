@@ -32,11 +32,11 @@
 
 namespace mtpb {
 
-// warps of the gradient edge kernels and edge slots per staged chunk; the
-// level-24 shape runs 12 warps so that a thread may hold 168 registers (the
-// value and weighted adjoints of its chains)
+// warps of the gradient edge kernels and edge slots per staged chunk: the
+// level-20 shape runs 8 warps and the level-24 shape 12, so that a thread
+// may hold the value and weighted adjoints of its chains in registers
 template <class S> struct GradCfg {
-    static constexpr int NW = ShapeCfg<S>::NW > 12 ? 12 : ShapeCfg<S>::NW;
+    static constexpr int NW = S::NSLOT > 400 ? 12 : S::NSLOT > 200 ? 8 : ShapeCfg<S>::NW;
     static constexpr int KSG = S::NMU >= 6 ? 4 : 8;
 };
 

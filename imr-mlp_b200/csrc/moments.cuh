@@ -11,6 +11,10 @@ constexpr int KS = 8;     // edge slots staged per chunk
 constexpr int STR = 36;   // row stride of the staging arrays (doubles): conflict-free
                           // writes from (lane, slot) pairs and reads by lane
 
+// Warps per block of the moment kernels.  Shapes up to level 20 run 4 warps
+// and two blocks per SM: the warps that share a scheduler then run the same
+// unrolled chain code (8 different bodies per SM thrashed the instruction
+// cache).
 template <class S> struct ShapeCfg;
 template <> struct ShapeCfg<ShapeS1> { static constexpr int NW = 2; };
 template <> struct ShapeCfg<ShapeS2> { static constexpr int NW = 2; };
