@@ -68,6 +68,9 @@ def parse():
     ap.add_argument("--train-steps", type=int, default=5)
     ap.add_argument("--train-warmup", type=int, default=3)
     ap.add_argument("--no-train", action="store_true", help="skip the training leg")
+    ap.add_argument("--profile-train", action="store_true",
+                    help="training leg only, device loop only (the command used for ncu "
+                         "captures of the gradient kernels)")
     ap.add_argument("--profile", action="store_true",
                     help="device loop only (no e2e loop, peak probe or CPU baseline): the "
                          "command used for ncu captures")
@@ -394,7 +397,7 @@ def run_train(args, torch, dist, ws, rank, local, dev, stream):
     # end to end through the host API: labels H2D and loss/metrics/gradient
     # D2H every step (single GPU only: the shards' sum needs the device path)
     e2e = None
-    if ws == 1:
+    if ws == 1 and not args.profile_train:
         for _ in range(2):
             gpu.loss_grad(te, tf, ts, TRAIN_WEIGHTS, total)
         torch.cuda.synchronize()
@@ -733,8 +736,23 @@ def reference_train_line(args, threads, ws):
                     "d2h_bytes_per_step": 0}}
 
 
+def run_profile_train(args):
+    import torch
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    res = run_train(args, torch, None, 1, 0, 0, dev, stream)
+    line = res[0]
+    return {"profile_run": True, "train_ms_per_step": line["ms_per_step"],
+            "kernel_ms": line["kernel_ms"], "atoms": line["config"]["atoms_per_gpu"]}
+
+
 def main():
     args = parse()
+    if args.profile_train:
+        print(json.dumps(run_profile_train(args)), flush=True)
+        return
     line = run_reference(args) if args.impl == "reference" else run_ours(args)
     if line is not None:
         print(json.dumps(line), flush=True)
