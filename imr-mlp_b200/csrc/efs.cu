@@ -58,7 +58,7 @@ __device__ __forceinline__ void stage_chunk(const EdgeArgs &p, const StageView &
                                             int chunk)
 {
     constexpr int NMU = S::NMU;
-    for (int item = threadIdx.x; item < 32 * KS; item += NW * 32) {
+    for (int item = threadIdx.x; item < 32 * KS; item += blockDim.x) {
         const int lane = item / KS;
         const int k = item - lane * KS;
         const int atom = atom0 + lane;
@@ -227,9 +227,11 @@ __device__ __forceinline__ void fwd_warp(const EdgeArgs &p, const StageView &v, 
 
 // ----------------------------------------------------------------------------
 // Reverse: per-edge dE_i/dr_ij of 32 atoms.  Each warp adds its chains'
-// share; the shares are summed in fixed warp order (deterministic).
+// share; the shares are summed in fixed warp order (deterministic).  NW is
+// the size of the chain partition, W the warp's index in it and NWB the warps
+// of this block; the first part stores the sums, later parts add to them.
 // ----------------------------------------------------------------------------
-template <class S, int NW, int W>
+template <class S, int NW, int W, int NWB, bool FIRST>
 __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, int atom0,
                                          int maxdeg, const double *adjoint, double *dx,
                                          double *dy, double *dz)
@@ -333,7 +335,7 @@ __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, 
                 H = fma(q, fma(xh, h1, double(b + c) * h0), H);
             });
             const double t = V - H * rinv;
-            double *part = v.part + (size_t)W * 3 * KS * 32;
+            double *part = v.part + (size_t)(W % NWB) * 3 * KS * 32;
             part[(0 * KS + k) * 32 + lane] = fma(xh, t, Gx * rinv);
             part[(1 * KS + k) * 32 + lane] = fma(yh, t, Gy * rinv);
             part[(2 * KS + k) * 32 + lane] = fma(zh, t, Gz * rinv);
@@ -341,7 +343,7 @@ __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, 
         __syncthreads();
         // sum the warps' shares in warp order and store per edge (thread ->
         // (slot, lane) so that the shared reads are lane-contiguous)
-        for (int item = threadIdx.x; item < 32 * KS; item += NW * 32) {
+        for (int item = threadIdx.x; item < 32 * KS; item += NWB * 32) {
             const int k = item >> 5;
             const int ln = item & 31;
             const int at = atom0 + ln;
@@ -352,22 +354,30 @@ __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, 
                 continue;
             double sx = 0.0, sy = 0.0, sz = 0.0;
 #pragma unroll
-            for (int w = 0; w < NW; ++w) {
+            for (int w = 0; w < NWB; ++w) {
                 const double *pw = v.part + (size_t)w * 3 * KS * 32;
                 sx += pw[(0 * KS + k) * 32 + ln];
                 sy += pw[(1 * KS + k) * 32 + ln];
                 sz += pw[(2 * KS + k) * 32 + ln];
             }
-            dx[e] = sx;
-            dy[e] = sy;
-            dz[e] = sz;
+            if constexpr (FIRST) {
+                dx[e] = sx;
+                dy[e] = sy;
+                dz[e] = sz;
+            } else {
+                dx[e] += sx;
+                dy[e] += sy;
+                dz[e] += sz;
+            }
         }
         __syncthreads();
     }
 }
 
-template <class S, bool REV>
-__global__ void __launch_bounds__(ShapeCfg<S>::NW * 32, ShapeCfg<S>::NW <= 4 ? 2 : 1)
+// PART: which block of NW warps of the NW * NPART chain partition this launch
+// runs
+template <class S, bool REV, int PART>
+__global__ void __launch_bounds__(ShapeCfg<S>::NW * 32, blocks_per_sm<S>())
     k_moments(EdgeArgs p, double *basic, const double *adjoint, double *dx, double *dy,
               double *dz)
 {
@@ -398,13 +408,15 @@ __global__ void __launch_bounds__(ShapeCfg<S>::NW * 32, ShapeCfg<S>::NW <= 4 ? 2
     const int atom0 = group * 32;
     const int maxdeg = __ldg(p.group_maxdeg + group);
     const int warp = threadIdx.x >> 5;
+    constexpr int NWT = NW * ShapeCfg<S>::NPART;
     static_for<NW>([&](auto iw) {
-        constexpr int W = decltype(iw)::value;
-        if (warp == W) {
+        constexpr int WL = decltype(iw)::value;
+        constexpr int W = PART * NW + WL;
+        if (warp == WL) {
             if constexpr (REV)
-                rev_warp<S, NW, W>(p, v, atom0, maxdeg, adjoint, dx, dy, dz);
+                rev_warp<S, NWT, W, NW, PART == 0>(p, v, atom0, maxdeg, adjoint, dx, dy, dz);
             else
-                fwd_warp<S, NW, W>(p, v, atom0, maxdeg, basic);
+                fwd_warp<S, NWT, W>(p, v, atom0, maxdeg, basic);
         }
     });
 }
@@ -419,13 +431,19 @@ template <class S, bool REV> static cudaError_t launch_shape(const EdgeArgs &a, 
     if (groups == 0)
         return cudaSuccess;
     const size_t smem = sizeof(double) * smem_doubles<S, REV>(a.K, a.R);
-    auto kern = k_moments<S, REV>;
-    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)smem);
-    if (err != cudaSuccess)
-        return err;
-    kern<<<groups, NW * 32, smem, s>>>(a, basic, adjoint, dx, dy, dz);
-    return cudaGetLastError();
+    cudaError_t err = cudaSuccess;
+    static_for<ShapeCfg<S>::NPART>([&](auto ip) {
+        constexpr int P = decltype(ip)::value;
+        if (err != cudaSuccess)
+            return;
+        auto kern = k_moments<S, REV, P>;
+        err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (err == cudaSuccess) {
+            kern<<<groups, NW * 32, smem, s>>>(a, basic, adjoint, dx, dy, dz);
+            err = cudaGetLastError();
+        }
+    });
+    return err;
 }
 
 template <bool REV> static cudaError_t dispatch(int shape, const EdgeArgs &a, double *basic,

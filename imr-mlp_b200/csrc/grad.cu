@@ -33,11 +33,15 @@
 namespace mtpb {
 
 // warps of the gradient edge kernels and edge slots per staged chunk: the
-// level-20 shape runs 8 warps and the level-24 shape 12, so that a thread
-// may hold the value and weighted adjoints of its chains in registers
+// level-20 shape runs 8 warps; the level-24 shape partitions its chains over
+// 12 warps (so that a thread may hold the value and weighted adjoints of its
+// chains in registers) run as three launches of 4 warps, three blocks per SM
+// (one unrolled body per scheduler)
 template <class S> struct GradCfg {
-    static constexpr int NW = S::NSLOT > 400 ? 12 : S::NSLOT > 200 ? 8 : ShapeCfg<S>::NW;
+    static constexpr int NW = S::NSLOT > 400 ? 4 : S::NSLOT > 200 ? 8 : ShapeCfg<S>::NW;
+    static constexpr int NPART = S::NSLOT > 400 ? 3 : 1;
     static constexpr int KSG = S::NMU >= 6 ? 4 : 8;
+    static constexpr int BLOCKS = NPART > 1 ? 3 : 1;   // blocks per SM
 };
 
 template <int KSG> __device__ __forceinline__ double &SG(double *st, int row, int k, int lane)
@@ -80,7 +84,7 @@ __device__ __forceinline__ void grad_stage(const EdgeArgs &p, const double *__re
 {
     constexpr int NMU = S::NMU;
     constexpr int KSG = GradCfg<S>::KSG;
-    for (int item = threadIdx.x; item < 32 * KSG; item += NW * 32) {
+    for (int item = threadIdx.x; item < 32 * KSG; item += blockDim.x) {
         const int lane = item / KSG;
         const int k = item - lane * KSG;
         const int atom = atom0 + lane;
@@ -283,9 +287,11 @@ __device__ __forceinline__ void tan_warp(const EdgeArgs &p, const double *wx, co
 // its chains' share of U_mu = A_mu + P_mu and S_mu; the shares are summed in
 // warp order and stored as uv[e] = {U_0..U_{NMU-1}, s S_0 .. s S_{NMU-1}}.
 // PASS 0 does all terms; where the two adjoint sets do not fit the registers
-// PASS 1 stores the terms of a (U = P) and PASS 2 adds A_mu to U.
+// PASS 1 stores the terms of a (U = P) and PASS 2 adds A_mu to U.  NW is the
+// size of the chain partition, W the warp's index in it, NWB the warps of the
+// block; only the first part of the first pass stores, the others add.
 // ----------------------------------------------------------------------------
-template <class S, int NW, int W, int PASS>
+template <class S, int NW, int W, int PASS, int NWB, bool FIRST>
 __device__ __forceinline__ void edge_grad_warp(const EdgeArgs &p, const double *wx,
                                                const double *wy, const double *wz,
                                                const GradView &v, int atom0, int maxdeg,
@@ -327,7 +333,7 @@ __device__ __forceinline__ void edge_grad_warp(const EdgeArgs &p, const double *
         }
     }
     const int nchunks = (maxdeg + KSG - 1) / KSG;
-    double *part = v.part + (size_t)W * 2 * NMU * KSG * 32;
+    double *part = v.part + (size_t)(W % NWB) * 2 * NMU * KSG * 32;
     for (int ch = 0; ch < nchunks; ++ch) {
         grad_stage<S, NW, false>(p, wx, wy, wz, v, atom0, ch);
         __syncthreads();
@@ -382,7 +388,7 @@ __device__ __forceinline__ void edge_grad_warp(const EdgeArgs &p, const double *
             }
         }
         __syncthreads();
-        for (int item = threadIdx.x; item < 32 * KSG; item += NW * 32) {
+        for (int item = threadIdx.x; item < 32 * KSG; item += NWB * 32) {
             const int k = item >> 5;
             const int ln = item & 31;
             const int at = atom0 + ln;
@@ -397,21 +403,23 @@ __device__ __forceinline__ void edge_grad_warp(const EdgeArgs &p, const double *
             for (int m = 0; m < (HA ? 2 * NMU : NMU); ++m) {
                 double t = 0.0;
 #pragma unroll
-                for (int w = 0; w < NW; ++w)
+                for (int w = 0; w < NWB; ++w)
                     t += v.part[(size_t)w * 2 * NMU * KSG * 32 + (m * KSG + k) * 32 + ln];
-                if constexpr (PASS == 2)
-                    o[m] += t;
+                const double val = m < NMU ? t : t * sw;
+                if constexpr (PASS != 2 && FIRST)
+                    o[m] = val;
                 else
-                    o[m] = m < NMU ? t : t * sw;
+                    o[m] += val;
             }
         }
         __syncthreads();
     }
 }
 
-// MODE 0: tangent basics; 1-3: edge records with PASS = MODE - 1
-template <class S, int MODE>
-__global__ void __launch_bounds__(GradCfg<S>::NW * 32)
+// MODE 0: tangent basics; 1-3: edge records with PASS = MODE - 1; PART: which
+// block of NW warps of the chain partition this launch runs
+template <class S, int MODE, int PART>
+__global__ void __launch_bounds__(GradCfg<S>::NW * 32, GradCfg<S>::BLOCKS)
     k_grad_moments(EdgeArgs p, const double *__restrict__ wx, const double *__restrict__ wy,
                    const double *__restrict__ wz, const double *__restrict__ adjoint,
                    const double *__restrict__ adjoint2, double *__restrict__ out)
@@ -445,14 +453,17 @@ __global__ void __launch_bounds__(GradCfg<S>::NW * 32)
     const int atom0 = group * 32;
     const int maxdeg = __ldg(p.group_maxdeg + group);
     const int warp = threadIdx.x >> 5;
+    constexpr int NWT = NW * GradCfg<S>::NPART;
     static_for<NW>([&](auto iw) {
-        constexpr int W = decltype(iw)::value;
-        if (warp == W) {
+        constexpr int WL = decltype(iw)::value;
+        constexpr int W = PART * NW + WL;
+        if (warp == WL) {
             if constexpr (TAN)
-                tan_warp<S, NW, W>(p, wx, wy, wz, v, atom0, maxdeg, out);
+                tan_warp<S, NWT, W>(p, wx, wy, wz, v, atom0, maxdeg, out);
             else
-                edge_grad_warp<S, NW, W, MODE - 1>(p, wx, wy, wz, v, atom0, maxdeg, adjoint,
-                                                   adjoint2, out);
+                edge_grad_warp<S, NWT, W, MODE - 1, NW, PART == 0>(p, wx, wy, wz, v, atom0,
+                                                                   maxdeg, adjoint, adjoint2,
+                                                                   out);
         }
     });
 }
@@ -467,13 +478,19 @@ static cudaError_t launch_grad_shape(const EdgeArgs &a, const double *wx, const 
     if (groups == 0)
         return cudaSuccess;
     const size_t smem = sizeof(double) * grad_smem_doubles<S, MODE == 0>(a.K, a.R);
-    auto kern = k_grad_moments<S, MODE>;
-    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)smem);
-    if (err != cudaSuccess)
-        return err;
-    kern<<<groups, NW * 32, smem, s>>>(a, wx, wy, wz, adjoint, adjoint2, out);
-    return cudaGetLastError();
+    cudaError_t err = cudaSuccess;
+    static_for<GradCfg<S>::NPART>([&](auto ip) {
+        constexpr int P = decltype(ip)::value;
+        if (err != cudaSuccess)
+            return;
+        auto kern = k_grad_moments<S, MODE, P>;
+        err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (err == cudaSuccess) {
+            kern<<<groups, NW * 32, smem, s>>>(a, wx, wy, wz, adjoint, adjoint2, out);
+            err = cudaGetLastError();
+        }
+    });
+    return err;
 }
 
 template <int MODE>

@@ -11,17 +11,26 @@ constexpr int KS = 8;     // edge slots staged per chunk
 constexpr int STR = 36;   // row stride of the staging arrays (doubles): conflict-free
                           // writes from (lane, slot) pairs and reads by lane
 
-// Warps per block of the moment kernels.  Shapes up to level 20 run 4 warps
-// and two blocks per SM: the warps that share a scheduler then run the same
-// unrolled chain code (8 different bodies per SM thrashed the instruction
-// cache).
+// Warps per block of the moment kernels.  Blocks run 4 warps and two or
+// three blocks share an SM: the warps that share a scheduler then run the
+// same unrolled chain code (8 or 12 different bodies per SM thrashed the
+// instruction cache).
 template <class S> struct ShapeCfg;
-template <> struct ShapeCfg<ShapeS1> { static constexpr int NW = 2; };
-template <> struct ShapeCfg<ShapeS2> { static constexpr int NW = 2; };
-template <> struct ShapeCfg<ShapeL16> { static constexpr int NW = 4; };
-template <> struct ShapeCfg<ShapeL20> { static constexpr int NW = 4; };
-template <> struct ShapeCfg<ShapeL24> { static constexpr int NW = 12; };
-template <> struct ShapeCfg<ShapePS> { static constexpr int NW = 4; };
+template <> struct ShapeCfg<ShapeS1> { static constexpr int NW = 2, NPART = 1; };
+template <> struct ShapeCfg<ShapeS2> { static constexpr int NW = 2, NPART = 1; };
+template <> struct ShapeCfg<ShapeL16> { static constexpr int NW = 4, NPART = 1; };
+template <> struct ShapeCfg<ShapeL20> { static constexpr int NW = 4, NPART = 1; };
+// level 24: the chains are partitioned over 12 warps (register budget) and
+// run as three launches ("parts") of 4 warps, three blocks per SM, so that
+// every scheduler still runs a single unrolled body
+template <> struct ShapeCfg<ShapeL24> { static constexpr int NW = 4, NPART = 3; };
+template <> struct ShapeCfg<ShapePS> { static constexpr int NW = 4, NPART = 1; };
+
+// blocks per SM requested by __launch_bounds__
+template <class S> constexpr int blocks_per_sm()
+{
+    return ShapeCfg<S>::NW > 4 ? 1 : ShapeCfg<S>::NPART > 1 ? 3 : 2;
+}
 
 __device__ __forceinline__ double &SV(double *st, int row, int k, int lane)
 {

@@ -175,11 +175,11 @@ template <class S, int NW> struct Partition {
 
 // ---- compile-time loop helper -------------------------------------------
 template <class F, int... Is>
-__device__ __forceinline__ void static_for_impl(F &&f, std::integer_sequence<int, Is...>)
+__host__ __device__ __forceinline__ void static_for_impl(F &&f, std::integer_sequence<int, Is...>)
 {
     (f(std::integral_constant<int, Is>{}), ...);
 }
-template <int N, class F> __device__ __forceinline__ void static_for(F &&f)
+template <int N, class F> __host__ __device__ __forceinline__ void static_for(F &&f)
 {
     if constexpr (N > 0)
         static_for_impl(f, std::make_integer_sequence<int, N>{});
