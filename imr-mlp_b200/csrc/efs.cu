@@ -377,7 +377,7 @@ __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, 
 // PART: which block of NW warps of the NW * NPART chain partition this launch
 // runs
 template <class S, bool REV, int PART>
-__global__ void __launch_bounds__(ShapeCfg<S>::NW * 32, blocks_per_sm<S>())
+__global__ void __launch_bounds__(ShapeCfg<S>::NW * 32, KCfg<S, REV>::BLOCKS)
     k_moments(EdgeArgs p, double *basic, const double *adjoint, double *dx, double *dy,
               double *dz)
 {
@@ -408,7 +408,7 @@ __global__ void __launch_bounds__(ShapeCfg<S>::NW * 32, blocks_per_sm<S>())
     const int atom0 = group * 32;
     const int maxdeg = __ldg(p.group_maxdeg + group);
     const int warp = threadIdx.x >> 5;
-    constexpr int NWT = NW * ShapeCfg<S>::NPART;
+    constexpr int NWT = NW * KCfg<S, REV>::NPART;
     static_for<NW>([&](auto iw) {
         constexpr int WL = decltype(iw)::value;
         constexpr int W = PART * NW + WL;
@@ -432,7 +432,7 @@ template <class S, bool REV> static cudaError_t launch_shape(const EdgeArgs &a, 
         return cudaSuccess;
     const size_t smem = sizeof(double) * smem_doubles<S, REV>(a.K, a.R);
     cudaError_t err = cudaSuccess;
-    static_for<ShapeCfg<S>::NPART>([&](auto ip) {
+    static_for<KCfg<S, REV>::NPART>([&](auto ip) {
         constexpr int P = decltype(ip)::value;
         if (err != cudaSuccess)
             return;
