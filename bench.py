@@ -68,6 +68,8 @@ def parse():
     ap.add_argument("--train-steps", type=int, default=5)
     ap.add_argument("--train-warmup", type=int, default=3)
     ap.add_argument("--no-train", action="store_true", help="skip the training leg")
+    ap.add_argument("--no-batch", action="store_true",
+                    help="skip the batched-EFS legs (configs 2 and 5)")
     ap.add_argument("--profile-train", action="store_true",
                     help="training leg only, device loop only (the command used for ncu "
                          "captures of the gradient kernels)")
@@ -260,6 +262,127 @@ def cpu_reference_sample(model, reps, steps, warmup, threads):
                       f"{REBUILD_EVERY} of one neighbour build ({t_build * 1e3:.1f} ms); "
                       "MPI unavailable, OpenMP only",
             "ms_per_step": t_step * 1e3}
+
+
+# ---------------------------------------------------------------------------
+# Batched EFS workloads (configs 2 and 5)
+# ---------------------------------------------------------------------------
+BATCH_STEPS = 5
+
+
+def batch_problem(name):
+    """(structures, model, description) of a batched-EFS configuration."""
+    from mtpb200 import configs, read_mtp
+    if name == "config2":
+        model = read_mtp(os.path.join(ROOT, "tests", "golden", "models", "l20_k3.mtp"))
+        return (configs.config2(4096, seed=2), model,
+                "config 2: 4096 Ni/Al/Cr fcc alloys of 32/108/256 atoms, level 20, K=3")
+    model = configs.level24_model(species_count=3, rmin=0.8, rmax=6.0, rb_size=10, seed=55)
+    return (configs.config5(1000, seed=5), model,
+            "config 5: 1000 Ru(0001)/water interfaces of 336 atoms, level-24 generated basis, "
+            "K=3, R=10, r_cut=6")
+
+
+def shard_lpt(sizes, nranks):
+    """Greedy longest-processing-time assignment of structures to ranks by
+    size (edge counts are proportional to atom counts within a config)."""
+    order = np.argsort(-np.asarray(sizes), kind="stable")
+    load = np.zeros(nranks)
+    owner = np.zeros(len(sizes), dtype=np.int64)
+    for i in order:
+        r = int(np.argmin(load))
+        owner[i] = r
+        load[r] += sizes[i]
+    return owner
+
+
+def cpu_batch_sample(model, sts, threads, n_sample):
+    """Reference CPU path per structure (Neighborhoods build + MLIPCore over
+    OpenMP centres), the calc_efs loop, on the first n_sample structures."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import ReferenceEFS  # test infrastructure: baseline leg only
+    from mtpb200 import format_mtp
+    ref = ReferenceEFS(format_mtp(model), model.species_count, threads=threads)
+    t_total = 0.0
+    atoms = 0
+    for x in sts[:n_sample]:
+        t0 = time.perf_counter()
+        prob = ref.build(x["cell"], x["pbc"], x["positions"], x["types"])
+        ref.compute(prob)
+        t_total += time.perf_counter() - t0
+        atoms += len(x["types"])
+    ref.close()
+    n = min(n_sample, len(sts))
+    return {"value": n / t_total, "unit": "configs/s", "cores": threads, "kind": "reference",
+            "sample": f"first {n} structures ({atoms} atoms): reference Neighborhoods + "
+                      "MLIPCore::compute (OpenMP over centres) per structure",
+            "atoms_per_s": atoms / t_total}
+
+
+def run_batch(name, args, torch, dist, ws, rank, local, dev, stream):
+    """Batched EFS of one configuration: structures sharded over the ranks
+    (no data-path collective; one all-reduce of the energy total per step),
+    neighbour lists built every step as a calc_efs pass does."""
+    from mtpb200 import MTPGpuDirect, StructureBatch
+    sts, model, desc = batch_problem(name)
+    sizes = [len(x["types"]) for x in sts]
+    owner = shard_lpt(sizes, ws)
+    mine = [x for x, o in zip(sts, owner) if o == rank]
+    b = StructureBatch.from_structures(mine)
+    gpu = MTPGpuDirect(model, local)
+    gpu.set_stream(stream.cuda_stream)
+    S, N = b.n_structures, b.n_atoms
+    t = {k: torch.from_numpy(v).to(dev) for k, v in
+         dict(off=b.atom_offsets, cells=b.cells, pbc=np.ones((S, 3), np.int32),
+              pos=b.positions, types=b.types).items()}
+    e_d = torch.zeros(S, dtype=torch.float64, device=dev)
+    f_d = torch.zeros((N, 3), dtype=torch.float64, device=dev)
+    s_d = torch.zeros((S, 9), dtype=torch.float64, device=dev)
+    tot = torch.zeros(1, dtype=torch.float64, device=dev)
+
+    def step():
+        gpu.efs_device(t["off"], t["cells"], t["pbc"], t["pos"], t["types"], e_d, f_d, s_d)
+        if ws > 1:
+            torch.sum(e_d, dim=0, keepdim=True, out=tot)
+            dist.all_reduce(tot)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    t0.record(stream)
+    for _ in range(BATCH_STEPS):
+        step()
+        launches += gpu.last_launch_count()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    if ws > 1:
+        m = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        ms = float(m.item())
+    km = gpu.last_timings()
+    edges = gpu.neighbor_count()
+    gpu.close()
+    if rank != 0:
+        return None
+    total = len(sts)
+    res = {"metric": f"MTP batched EFS configs/sec ({name})", "value": total * BATCH_STEPS /
+           (ms / 1e3), "unit": "configs/s", "atoms_per_s": sum(sizes) * BATCH_STEPS / (ms / 1e3),
+           "n_gpus": ws, "steps": BATCH_STEPS, "warmup": 3, "ms_per_step": ms / BATCH_STEPS,
+           "scaling": "strong", "dtype": "f64",
+           "config": {"workload": desc + "; one step = neighbour build and EFS of every "
+                                         "structure", "structures_per_gpu": S,
+                      "atoms_per_gpu": N, "edges_per_gpu": edges,
+                      "parallelism": f"shards{ws} (LPT by atoms)" if ws > 1 else "single"},
+           "kernel_ms": {"neighbor_build": float(km[0]), "moments_fwd": float(km[1]),
+                         "graph": float(km[2]), "moments_rev": float(km[3]),
+                         "gather_reduce": float(km[4])},
+           "gpu_launches": int(launches)}
+    return res, (model, sts)
 
 
 # ---------------------------------------------------------------------------
@@ -609,6 +732,8 @@ def run_ours(args):
     e2e_ok = abs(e2e_energy - energy) <= 1e-9 * max(1.0, abs(energy))
 
     train = None if args.no_train else run_train(args, torch, dist, ws, rank, local, dev, stream)
+    batches = [] if args.no_batch else [run_batch(nm, args, torch, dist, ws, rank, local, dev,
+                                                  stream) for nm in ("config2", "config5")]
     peak = fp64_peak_tflops(torch, dev) if rank == 0 else None
     if ws > 1:
         dist.barrier()
@@ -677,6 +802,17 @@ def run_ours(args):
                 tline["cpu_baseline"] = {"value": None, "unit": TRAIN_UNIT, "cores": 0,
                                          "kind": "port", "sample": f"unavailable: {exc}"}
         line["train"] = tline
+    for res in batches:
+        if res is None:
+            continue
+        bline, (bmodel, bsts) = res
+        if ws == 1:
+            try:
+                bline["cpu_baseline"] = cpu_batch_sample(bmodel, bsts, threads, 32)
+            except Exception as exc:
+                bline["cpu_baseline"] = {"value": None, "unit": "configs/s", "cores": 0,
+                                         "kind": "reference", "sample": f"unavailable: {exc}"}
+        line.setdefault("batch", []).append(bline)
     return line
 
 
@@ -705,6 +841,17 @@ def run_reference(args):
                     "d2h_bytes_per_step": 0}}
     if train is not None:
         line["train"] = train
+    if not args.no_batch:
+        for nm in ("config2", "config5"):
+            sts, bmodel, desc = batch_problem(nm)
+            r = cpu_batch_sample(bmodel, sts, threads, 32)
+            line.setdefault("batch", []).append({
+                "metric": f"MTP batched EFS configs/sec ({nm})", "value": r["value"],
+                "unit": "configs/s", "atoms_per_s": r["atoms_per_s"], "n_gpus": ws,
+                "impl": "reference", "config": {"workload": desc},
+                "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": r["value"], "unit": "configs/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}})
     return line
 
 

@@ -107,6 +107,58 @@ def config4_structures(n_struct: int = 8192, seed: int = 4) -> List[Dict[str, np
     return out
 
 
+def _rotation(rng):
+    q, _ = np.linalg.qr(rng.normal(size=(3, 3)))
+    return q * np.sign(np.linalg.det(q))
+
+
+def ru_water_interface(seed: int) -> Dict[str, np.ndarray]:
+    """hcp Ru(0001) 6x6x4 slab (144 Ru, a = 2.706, c = 4.282, ABAB stacking)
+    under a 15 A region holding 64 H2O (O-H 0.96 A, H-O-H 104.5 deg) at
+    1.0 g/cm^3 (a 4x4 in-plane grid of 4 staggered layers, random
+    orientations, starting 2 A above the top Ru layer), then 10 A of vacuum;
+    Gaussian sigma 0.05 on every atom.  Types: Ru 0, O 1, H 2."""
+    rng = np.random.default_rng(seed)
+    a, c = 2.706, 4.282
+    a1 = np.array([a, 0.0, 0.0])
+    a2 = np.array([0.5 * a, 0.5 * np.sqrt(3.0) * a, 0.0])
+    dz = 0.5 * c
+    ru = []
+    for layer in range(4):
+        shift = (0.0, 0.0) if layer % 2 == 0 else (1.0 / 3.0, 1.0 / 3.0)
+        for i in range(6):
+            for j in range(6):
+                ru.append((i + shift[0]) * a1 + (j + shift[1]) * a2 + np.array([0, 0, layer * dz]))
+    ru = np.array(ru)
+    top = 3 * dz
+    area = 36 * a * a * 0.5 * np.sqrt(3.0)
+    height = 64 * 18.015 / 6.02214076e23 / 1.0 * 1e24 / area   # A, at 1.0 g/cm^3
+    theta = np.deg2rad(104.5) / 2
+    mol = np.array([[0.0, 0.0, 0.0], [0.96 * np.sin(theta), 0.0, 0.96 * np.cos(theta)],
+                    [-0.96 * np.sin(theta), 0.0, 0.96 * np.cos(theta)]])
+    waters, wtypes = [], []
+    for layer in range(4):
+        st = 0.5 if layer % 2 else 0.0
+        for i in range(4):
+            for j in range(4):
+                o = (1.5 * (i + st)) * a1 + (1.5 * (j + st)) * a2 + \
+                    np.array([0, 0, top + 2.0 + (layer + 0.5) * height / 4])
+                waters.append(o + mol @ _rotation(rng).T)
+                wtypes += [1, 2, 2]
+    pos = np.concatenate([ru, np.concatenate(waters)])
+    pos = pos + rng.normal(0.0, 0.05, size=pos.shape)
+    cell = np.array([6 * a1, 6 * a2, [0.0, 0.0, top + 15.0 + 10.0]])
+    types = np.concatenate([np.zeros(len(ru), np.int32), np.array(wtypes, np.int32)])
+    return {"cell": cell, "pbc": np.array([1, 1, 1], dtype=np.int32),
+            "positions": np.ascontiguousarray(pos), "types": types}
+
+
+def config5(n_copies: int = 1000, seed: int = 5) -> List[Dict[str, np.ndarray]]:
+    """n_copies independently perturbed Ru(0001)/water interfaces (336 atoms
+    each)."""
+    return [ru_water_interface(seed * 100003 + k) for k in range(n_copies)]
+
+
 def level24_model(species_count: int = 2, rmin: float = 2.0, rmax: float = 5.0,
                   rb_size: int = 8, seed: int = 24) -> MTPModel:
     """Generated level-24 basis (basisgen) with seeded U(-0.1, 0.1)
