@@ -70,3 +70,20 @@ def test_level24_stand_in_against_oracle(oracle):
     rl, rm, rg = oracle.loss_grad(m, offs, types, concat_lists(lists, offs), *lab, WEIGHTS)
     assert abs(loss - rl) <= 1e-10 * max(1.0, abs(rl))
     assert np.max(np.abs(grad - rg)) <= 1e-9 * max(1.0, np.max(np.abs(rg)))
+
+
+def test_config5_interface_against_oracle(oracle):
+    """Level-24 stand-in with K=3, R=10, rmin 0.8, r_cut 6 on one
+    Ru(0001)/water interface (configuration 5)."""
+    from mtpb200 import MTPGpuDirect, StructureBatch
+    m = configs.level24_model(species_count=3, rmin=0.8, rmax=6.0, rb_size=10, seed=55)
+    st = configs.ru_water_interface(7)
+    with MTPGpuDirect(m, 0) as gpu:
+        e, f, s, se = gpu.efs(StructureBatch.from_structures([st]), site_energy=True)
+    nl = oracle.neighbors(st["cell"], st["pbc"], st["positions"], m.cutoff)
+    re, rse, rf, rs = oracle.efs(m, st["types"], nl)
+    n = len(st["types"])
+    assert abs(e[0] - re) / n < TOL_E_ATOM
+    assert np.max(np.abs(se - rse)) < TOL_E_ATOM
+    assert np.max(np.abs(f - rf)) < TOL_F
+    assert np.max(np.abs(s[0] - rs)) < TOL_W
