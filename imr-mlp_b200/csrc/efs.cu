@@ -579,6 +579,7 @@ __device__ __forceinline__ void dag_segment(unsigned rec_addr, const Rows<GR> &r
     // are loaded before the current group is accumulated, so that shared-memory
     // latency overlaps the FP64 work (rows written in this phase are never read
     // in it, so the loads may pass the stores of earlier groups)
+    constexpr unsigned RS = ATOMS == 16 ? 7 : 6;   // log2 of the row size in bytes
     struct Grp {
         double c[4];
         unsigned of[4];
@@ -588,10 +589,10 @@ __device__ __forceinline__ void dag_segment(unsigned rec_addr, const Rows<GR> &r
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const uint4 w = lds128(rec_addr + (k + u) * REC_STRIDE);
-            g.of[u] = lds32(rec_addr + (k + u) * REC_STRIDE + 16);
+            g.of[u] = w.y;
             g.c[u] = __hiloint2double((int)w.w, (int)w.z);
-            g.x[u] = rowsA.ld(w.x);
-            g.y[u] = rowsA.ld(w.y);
+            g.x[u] = rowsA.ld((w.x & 0xffffu) << RS);
+            g.y[u] = rowsA.ld((w.x >> 16) << RS);
         }
     };
     auto accumulate = [&](const Grp &g) {
@@ -604,16 +605,15 @@ __device__ __forceinline__ void dag_segment(unsigned rec_addr, const Rows<GR> &r
         }
     };
     int k = 0;
-    if (n == G::CH && G::CH == 16) {   // full ring slot: fixed two-stage schedule
-        Grp a, b;
-        load(a, 0);
-        load(b, 4);
-        accumulate(a);
-        load(a, 8);
-        accumulate(b);
-        load(b, 12);
-        accumulate(a);
-        accumulate(b);
+    if (n == G::CH) {   // full ring slot: two-stage schedule over CH/4 groups
+        Grp g[2];
+        load(g[0], 0);
+#pragma unroll
+        for (int i = 0; i < G::CH / 4; ++i) {
+            if (i + 1 < G::CH / 4)
+                load(g[(i + 1) & 1], 4 * (i + 1));
+            accumulate(g[i & 1]);
+        }
         return;
     }
     for (; k + 4 <= n; k += 4) {
@@ -623,13 +623,12 @@ __device__ __forceinline__ void dag_segment(unsigned rec_addr, const Rows<GR> &r
     }
     for (; k < n; ++k) {
         const uint4 w = lds128(rec_addr + k * REC_STRIDE);
-        const unsigned of = lds32(rec_addr + k * REC_STRIDE + 16);
-        const double2 x = rowsA.ld(w.x), y = rowsA.ld(w.y);
+        const double2 x = rowsA.ld((w.x & 0xffffu) << RS), y = rowsA.ld((w.x >> 16) << RS);
         const double c = __hiloint2double((int)w.w, (int)w.z);
         acc[0] = fma(c * x.x, y.x, acc[0]);
         acc[1] = fma(c * x.y, y.y, acc[1]);
-        if (of)
-            rare(of, c);
+        if (w.y)
+            rare(w.y, c);
     }
 }
 
@@ -776,8 +775,8 @@ __global__ void __launch_bounds__(DagGeom<ATOMS>::THREADS)
 }
 
 // Device records of a plan: warp-major per phase ([phase][warp][row][SPW
-// streams]) for the selected block geometry, with the operand rows turned
-// into shared-memory byte offsets.
+// streams]) for the selected block geometry; store targets become byte
+// offsets, operand rows stay indices.
 std::vector<DagDevRec> dag_device_records(const DagPlan &plan)
 {
     const int spw = plan.atoms == 16 ? DagGeom<16>::SPW : DagGeom<8>::SPW;
@@ -791,8 +790,7 @@ std::vector<DagDevRec> dag_device_records(const DagPlan &plan)
                 for (int s = 0; s < spw; ++s) {
                     const DagRec &in = plan.recs[(row0 + r) * DAG_STREAMS + w * spw + s];
                     DagDevRec d{};
-                    d.off1 = (in.s12 & 0xffffu) * row_bytes;
-                    d.off2 = (in.s12 >> 16) * row_bytes;
+                    d.rows = in.s12;   // row indices; the kernel scales them
                     d.c = in.c;
                     const unsigned flags = in.outf >> 16, out_ = in.outf & 0xffffu;
                     unsigned f = 0;

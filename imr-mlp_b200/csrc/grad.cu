@@ -550,7 +550,7 @@ cudaError_t launch_edge_grad(int shape, const EdgeArgs &a, const double *wx, con
 // moment row) give a and abar = dLdE a + sum c (abar_id m_o + a_id D_w m_o),
 // whose seeds dLdE * coefficient come from one_adj_row.  ENERGY records add
 // dLdE m + D_w m of their scalar moment to the block's gradient (the record's
-// pad word names it); reverse END|GLOBAL records store abar of a basic moment.
+// coefficient names it); reverse END|GLOBAL records store abar of a basic moment.
 // ----------------------------------------------------------------------------
 struct DagGradGeom {
     static constexpr int ATOMS = 8;
@@ -572,17 +572,18 @@ __device__ __forceinline__ void dag_grad_segment(unsigned rec_addr, const Rows<G
 {
     using G = DagGradGeom;
     constexpr unsigned REC_STRIDE = G::SPW * sizeof(DagDevRec);
-    auto rare = [&](unsigned outf, unsigned rec) {
+    constexpr unsigned RS = 7;   // log2 of the row size in bytes (8 atoms x 16 B)
+    // ENERGY records multiply the zero row by itself; their coefficient holds
+    // the index of the scalar moment in the energy list
+    auto rare = [&](unsigned outf, double c) {
         if constexpr (FWD) {
             if (outf & DEV_ENERGY) {
                 double val = valid ? fma(dlde, acc, accd) : 0.0;
                 val += __shfl_xor_sync(gmask, val, 4);
                 val += __shfl_xor_sync(gmask, val, 2);
                 val += __shfl_xor_sync(gmask, val, 1);
-                if (q == 0) {
-                    const unsigned idx = lds32(rec + 20);
-                    gsm[idx] += val;
-                }
+                if (q == 0)
+                    gsm[(int)c] += val;
             }
         }
         if (outf & DEV_END) {
@@ -609,51 +610,48 @@ __device__ __forceinline__ void dag_grad_segment(unsigned rec_addr, const Rows<G
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const uint4 w = lds128(rec_addr + (k + u) * REC_STRIDE);
-            g.of[u] = lds32(rec_addr + (k + u) * REC_STRIDE + 16);
+            g.of[u] = w.y;
             g.c[u] = __hiloint2double((int)w.w, (int)w.z);
-            g.x[u] = rowA.ld(w.x);
-            g.y[u] = rowA.ld(w.y);
+            g.x[u] = rowA.ld((w.x & 0xffffu) << RS);
+            g.y[u] = rowA.ld((w.x >> 16) << RS);
         }
     };
-    auto accumulate = [&](const Grp &g, int k) {
+    auto accumulate = [&](const Grp &g) {
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const double cx = g.c[u] * g.x[u].x;
             acc = fma(cx, g.y[u].x, acc);
             accd = fma(cx, g.y[u].y, fma(g.c[u] * g.x[u].y, g.y[u].x, accd));
             if (g.of[u])
-                rare(g.of[u], rec_addr + (k + u) * REC_STRIDE);
+                rare(g.of[u], g.c[u]);
         }
     };
     int k = 0;
-    if (n == G::CH && G::CH == 16) {
-        Grp a, b;
-        load(a, 0);
-        load(b, 4);
-        accumulate(a, 0);
-        load(a, 8);
-        accumulate(b, 4);
-        load(b, 12);
-        accumulate(a, 8);
-        accumulate(b, 12);
+    if (n == G::CH) {
+        Grp g[2];
+        load(g[0], 0);
+#pragma unroll
+        for (int i = 0; i < G::CH / 4; ++i) {
+            if (i + 1 < G::CH / 4)
+                load(g[(i + 1) & 1], 4 * (i + 1));
+            accumulate(g[i & 1]);
+        }
         return;
     }
     for (; k + 4 <= n; k += 4) {
         Grp a;
         load(a, k);
-        accumulate(a, k);
+        accumulate(a);
     }
     for (; k < n; ++k) {
-        const unsigned ra = rec_addr + k * REC_STRIDE;
-        const uint4 w = lds128(ra);
-        const unsigned of = lds32(ra + 16);
-        const double2 x = rowA.ld(w.x), y = rowA.ld(w.y);
+        const uint4 w = lds128(rec_addr + k * REC_STRIDE);
+        const double2 x = rowA.ld((w.x & 0xffffu) << RS), y = rowA.ld((w.x >> 16) << RS);
         const double c = __hiloint2double((int)w.w, (int)w.z);
         const double cx = c * x.x;
         acc = fma(cx, y.x, acc);
         accd = fma(cx, y.y, fma(c * x.y, y.x, accd));
-        if (of)
-            rare(of, ra);
+        if (w.y)
+            rare(w.y, c);
     }
 }
 
@@ -794,7 +792,8 @@ __global__ void __launch_bounds__(DagGradGeom::THREADS)
 
 // Device records of the dual graph: warp-major per phase for 4 streams per
 // warp, 128-byte rows, reverse-phase operands of the constant one taken from
-// one_adj_row (row index plan.nrows), and the energy index in pad[0].
+// one_adj_row (row index plan.nrows), and the energy index as the coefficient
+// of ENERGY records.
 std::vector<DagDevRec> dag_grad_records(const DagPlan &plan)
 {
     using G = DagGradGeom;
@@ -813,8 +812,7 @@ std::vector<DagDevRec> dag_grad_records(const DagPlan &plan)
                     int s1 = (int)(in.s12 & 0xffffu), s2 = (int)(in.s12 >> 16);
                     if (rev && s1 == plan.one_row)
                         s1 = one_adj;
-                    d.off1 = (unsigned)s1 * G::ROW_BYTES;
-                    d.off2 = (unsigned)s2 * G::ROW_BYTES;
+                    d.rows = (unsigned)s1 | ((unsigned)s2 << 16);
                     d.c = in.c;
                     const unsigned flags = in.outf >> 16, out_ = in.outf & 0xffffu;
                     unsigned f = 0;
@@ -826,7 +824,8 @@ std::vector<DagDevRec> dag_grad_records(const DagPlan &plan)
                         f |= DEV_ENERGY;
                     d.outf = f ? (f | ((flags & DAG_GLOBAL) ? out_ : out_ * G::ROW_BYTES)) : 0u;
                     const int e = plan.rec_energy.empty() ? -1 : plan.rec_energy[idx];
-                    d.pad[0] = e < 0 ? 0u : (unsigned)e;
+                    if (flags & DAG_ENERGY)   // product 0 * 0: the coefficient is free
+                        d.c = e < 0 ? 0.0 : (double)e;
                     out[o++] = d;
                 }
         row0 += rows_p;

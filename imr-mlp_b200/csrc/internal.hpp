@@ -63,18 +63,17 @@ inline DagRec make_rec(int s1, int s2, int out, unsigned flags, double c)
 #define MTPB_DAG_STREAMS 32
 #endif
 #ifndef MTPB_DAG_CHUNK_ROWS
-#define MTPB_DAG_CHUNK_ROWS 16
+#define MTPB_DAG_CHUNK_ROWS 32
 #endif
 constexpr int DAG_STREAMS = MTPB_DAG_STREAMS;         // record streams per block
 
-// Device form of a record (32 bytes): shared-memory byte offsets of the two
-// operand rows, the coefficient, and a word that is zero for plain product
-// records and otherwise holds flags << 28 | out.
+// Device form of a record (16 bytes): the two operand row indices (16 bits
+// each), a word that is zero for plain product records and otherwise holds
+// flags << 28 | out, and the coefficient.
 struct alignas(16) DagDevRec {
-    unsigned off1, off2;
-    double c;
+    unsigned rows;   // s1 | s2 << 16
     unsigned outf;
-    unsigned pad[3];
+    double c;
 };
 constexpr int DAG_CHUNK_ROWS = MTPB_DAG_CHUNK_ROWS;   // record rows per shared chunk
 

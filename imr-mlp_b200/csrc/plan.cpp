@@ -221,7 +221,7 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
     plan.scratch_row = next++;
     plan.nrows = next;
     plan.energy_moments = energy_moments;
-    if (plan.nrows > 65535) {
+    if (plan.nrows >= 65535) {   // the dual graph adds one row
         if (err)
             *err = "moment graph too large for 16-bit row indices (" +
                    std::to_string(plan.nrows) + " rows)";
