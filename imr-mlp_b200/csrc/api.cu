@@ -190,7 +190,7 @@ EdgeArgs edge_args(const mtpb_context *c, int ncenter, const int *types, const i
 // forward moments -> graph -> reverse moments for ncenter centres.
 int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offsets,
                 const int *nbr, const double *rx, const double *ry, const double *rz,
-                double *site_energy, double *dx, double *dy, double *dz)
+                double *site_energy, double *dx, double *dy, double *dz, bool reverse)
 {
     c->npad = ((ncenter + 31) / 32) * 32;
     c->d_group_maxdeg = c->arena.get<int>("group_maxdeg", c->npad / 32 + 1);
@@ -203,7 +203,7 @@ int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offse
     EdgeArgs a = edge_args(c, ncenter, types, offsets, nbr, rx, ry, rz);
     CUDA_TRY(cudaEventRecord(c->ev[1], c->stream), "event");
     CUDA_TRY(launch_moments_fwd(c->shape, a, basic, c->stream), "moments forward");
-    c->launches++;
+    c->launches += moment_kernel_parts(c->shape, false);
     CUDA_TRY(cudaEventRecord(c->ev[2], c->stream), "event");
     double *gscratch = nullptr;
     if (c->plan.global_rows) {
@@ -217,8 +217,11 @@ int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offse
              "moment graph");
     c->launches++;
     CUDA_TRY(cudaEventRecord(c->ev[3], c->stream), "event");
-    CUDA_TRY(launch_moments_rev(c->shape, a, adjoint, dx, dy, dz, c->stream), "moments reverse");
-    c->launches++;
+    if (reverse) {   // energy-only calls stop at the site energies and adjoints
+        CUDA_TRY(launch_moments_rev(c->shape, a, adjoint, dx, dy, dz, c->stream),
+                 "moments reverse");
+        c->launches += moment_kernel_parts(c->shape, true);
+    }
     CUDA_TRY(cudaEventRecord(c->ev[4], c->stream), "event");
     return MTPB_OK;
 }
@@ -657,7 +660,10 @@ int mtpb_get_neighbors(const mtpb_context *c, int *offsets, int *nbr, double *ri
     return MTPB_OK;
 }
 
-int mtpb_efs_compute(mtpb_context *c, int memory, const mtpb_efs_output *out)
+} // extern "C"
+
+int mtpb::efs_compute(mtpb_context *c, int memory, const mtpb_efs_output *out,
+                      bool forces_needed)
 {
     if (!c)
         return fail(MTPB_ERR_ARGUMENT, "ctx is NULL");
@@ -687,18 +693,22 @@ int mtpb_efs_compute(mtpb_context *c, int memory, const mtpb_efs_output *out)
     if (!site_energy || !dx || !dy || !dz || !forces || !avir || !partials || !energy || !stress)
         return fail(MTPB_ERR_MEMORY, "device allocation failed");
     rc = run_moments(c, N, c->d_types, c->nb.offsets, c->nb.nbr, c->nb.rx, c->nb.ry, c->nb.rz,
-                     site_energy, dx, dy, dz);
+                     site_energy, dx, dy, dz, forces_needed);
     if (rc)
         return rc;
-    CUDA_TRY(launch_force_gather(N, NT, c->nb.offsets, c->nb.in_offsets, c->nb.in_edges, dx, dy, dz,
-                                 c->nb.rx, c->nb.ry, c->nb.rz, forces, avir, 0, c->stream),
-             "force gather");
-    CUDA_TRY(launch_segment_reduce(c->nseg, c->d_seg_begin, c->d_seg_end, site_energy, avir, N,
-                                   partials, c->stream),
+    if (forces_needed) {
+        CUDA_TRY(launch_force_gather(N, NT, c->nb.offsets, c->nb.in_offsets, c->nb.in_edges, dx,
+                                     dy, dz, c->nb.rx, c->nb.ry, c->nb.rz, forces, avir, 0,
+                                     c->stream),
+                 "force gather");
+        c->launches++;
+    }
+    CUDA_TRY(launch_segment_reduce(c->nseg, c->d_seg_begin, c->d_seg_end, site_energy,
+                                   forces_needed ? avir : nullptr, N, partials, c->stream),
              "segment reduce");
     CUDA_TRY(launch_struct_reduce(S, c->d_struct_seg0, partials, energy, stress, c->stream),
              "structure reduce");
-    c->launches += 3;
+    c->launches += 2;
     CUDA_TRY(cudaEventRecord(c->ev[5], c->stream), "event");
     c->ev_valid = true;
     c->nb_built_this_call = false;
@@ -725,7 +735,18 @@ int mtpb_efs_compute(mtpb_context *c, int memory, const mtpb_efs_output *out)
         CUDA_TRY(cudaGetLastError(), "EFS");
     }
     c->have_efs = true;
+    c->have_dedr = forces_needed;
     return MTPB_OK;
+}
+
+extern "C" {
+
+int mtpb_efs_compute(mtpb_context *c, int memory, const mtpb_efs_output *out)
+{
+    // an output without forces and stress asks for energies only (the
+    // energy-only branch of calc_efs and the trainer): no reverse pass
+    const bool forces = !out || out->forces || out->stress;
+    return efs_compute(c, memory, out, forces);
 }
 
 int mtpb_efs_structures(mtpb_context *c, const mtpb_structures *in, int memory,
@@ -847,7 +868,7 @@ int mtpb_get_edge_derivatives(const mtpb_context *c, double *dedr)
 {
     if (!c || !dedr)
         return fail(MTPB_ERR_ARGUMENT, "NULL argument");
-    if (!c->have_efs)
+    if (!c->have_efs || !c->have_dedr)
         return fail(MTPB_ERR_STATE, "no EFS result available");
     CUDA_TRY(cudaSetDevice(c->device), "cudaSetDevice");
     const long E = c->nedges;

@@ -84,6 +84,7 @@ struct mtpb_context {
     int launches = 0;
     int pending_launches = 0;   // neighbour build / refresh launches of this call
     bool have_efs = false;
+    bool have_dedr = false;   // the last EFS call ran the reverse pass
     long edge_epoch = 0;
     int dag_atoms_env = 0;   // MTPB_DAG_ATOMS override of the graph block width
     bool force_global_rows = false;   // MTPB_DAG_GLOBAL_ROWS=1   // advanced whenever the edge list or its vectors change
@@ -99,7 +100,8 @@ EdgeArgs edge_args(const mtpb_context *c, int ncenter, const int *types, const i
                    const int *nbr, const double *rx, const double *ry, const double *rz);
 int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offsets,
                 const int *nbr, const double *rx, const double *ry, const double *rz,
-                double *site_energy, double *dx, double *dy, double *dz);
+                double *site_energy, double *dx, double *dy, double *dz, bool reverse = true);
+int efs_compute(mtpb_context *c, int memory, const mtpb_efs_output *out, bool forces_needed);
 int csr_compute(mtpb_context *c, const mtpb_csr_request *req, int memory);
 int lammps_compute(mtpb_context *c, const mtpb_lammps_request *req);
 int loss_grad_compute(mtpb_context *c, const mtpb_labels *labels, const mtpb_loss_weights *w,

@@ -461,6 +461,20 @@ template <bool REV> static cudaError_t dispatch(int shape, const EdgeArgs &a, do
     }
 }
 
+// launches issued by one launch_moments_fwd / launch_moments_rev call
+int moment_kernel_parts(int shape, bool rev)
+{
+    switch (shape) {
+    case SHAPE_S1: return rev ? KCfg<ShapeS1, true>::NPART : KCfg<ShapeS1, false>::NPART;
+    case SHAPE_S2: return rev ? KCfg<ShapeS2, true>::NPART : KCfg<ShapeS2, false>::NPART;
+    case SHAPE_L16: return rev ? KCfg<ShapeL16, true>::NPART : KCfg<ShapeL16, false>::NPART;
+    case SHAPE_L20: return rev ? KCfg<ShapeL20, true>::NPART : KCfg<ShapeL20, false>::NPART;
+    case SHAPE_L24: return rev ? KCfg<ShapeL24, true>::NPART : KCfg<ShapeL24, false>::NPART;
+    case SHAPE_PS: return rev ? KCfg<ShapePS, true>::NPART : KCfg<ShapePS, false>::NPART;
+    default: return 1;
+    }
+}
+
 cudaError_t launch_moments_fwd(int shape, const EdgeArgs &a, double *basic, cudaStream_t s)
 {
     return dispatch<false>(shape, a, basic, nullptr, nullptr, nullptr, nullptr, s);

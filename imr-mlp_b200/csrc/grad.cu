@@ -523,6 +523,13 @@ static cudaError_t grad_dispatch(int shape, const EdgeArgs &a, const double *wx,
     }
 }
 
+// launches issued by one launch_moments_tangent / launch_edge_grad call
+int grad_kernel_launches(int shape, bool edge)
+{
+    const int parts = shape == SHAPE_L24 ? GradCfg<ShapeL24>::NPART : 1;
+    return edge && shape == SHAPE_L24 ? 2 * parts : parts;
+}
+
 cudaError_t launch_moments_tangent(int shape, const EdgeArgs &a, const double *wx,
                                    const double *wy, const double *wz, double *tangent,
                                    cudaStream_t s)

@@ -112,7 +112,9 @@ struct EdgeArgs {
     const PairParams *pairs;       // [K*K]
 };
 
-// launchers (efs.cu)
+// launchers (efs.cu); moment_kernel_parts = launches per call
+int moment_kernel_parts(int shape, bool rev);
+int grad_kernel_launches(int shape, bool edge);
 cudaError_t launch_moments_fwd(int shape, const EdgeArgs &a, double *basic, cudaStream_t s);
 cudaError_t launch_moments_rev(int shape, const EdgeArgs &a, const double *adjoint, double *dx,
                                double *dy, double *dz, cudaStream_t s);

@@ -466,9 +466,15 @@ int loss_grad_compute(mtpb_context *c, const mtpb_labels *labels, const mtpb_los
             CUDA_TRY(cudaEventCreate(&tev[i]), "cudaEventCreate");
     c->train.ev_valid = false;
     CUDA_TRY(cudaEventRecord(tev[0], c->stream), "event");
-    // EFS pass: energies, forces, virials, basic moments and their adjoints
+    // EFS pass: energies, forces, virials, basic moments and their adjoints;
+    // without force and stress terms (the trainer's energy_only branch,
+    // train_mtp.cpp:3858-3864) the reverse pass and the tangent moments are
+    // skipped: the edge weights are then zero
+    const bool use_f = labels->forces != nullptr && w->weight_force > 0;
+    const bool use_s = labels->stress != nullptr && w->weight_stress > 0;
+    const bool energy_only = !use_f && !use_s;
     mtpb_efs_output none{nullptr, nullptr, nullptr, nullptr};
-    if ((rc = mtpb_efs_compute(c, MTPB_MEMORY_DEVICE, &none)))
+    if ((rc = efs_compute(c, MTPB_MEMORY_DEVICE, &none, !energy_only)))
         return rc;
     CUDA_TRY(cudaEventRecord(tev[1], c->stream), "event");
     const double *d_energy = c->arena.get<double>("energy", S + 1);
@@ -528,19 +534,27 @@ int loss_grad_compute(mtpb_context *c, const mtpb_labels *labels, const mtpb_los
         CUDA_TRY(cudaGetLastError(), "loss");
         c->launches++;
     }
-    if (E > 0) {
+    if (E > 0 && !energy_only) {
         k_edge_weights<<<(unsigned)((E + 255) / 256), 256, 0, c->stream>>>(
             E, c->nb.center, c->nb.nbr, c->nb.struct_of, c->nb.rx, c->nb.ry, c->nb.rz, dldf, dlds,
             wx, wy, wz);
         CUDA_TRY(cudaGetLastError(), "edge weights");
         c->launches++;
+    } else if (E > 0) {
+        for (double *p : {wx, wy, wz})
+            CUDA_TRY(cudaMemsetAsync(p, 0, sizeof(double) * E, c->stream), "zero weights");
     }
     if ((rc = pair_buckets(c)))
         return rc;
     CUDA_TRY(cudaEventRecord(tev[2], c->stream), "event");
     EdgeArgs a = edge_args(c, N, c->d_types, c->nb.offsets, c->nb.nbr, c->nb.rx, c->nb.ry,
                            c->nb.rz);
-    CUDA_TRY(launch_moments_tangent(c->shape, a, wx, wy, wz, tangent, c->stream), "tangent");
+    if (energy_only)
+        CUDA_TRY(cudaMemsetAsync(tangent, 0, sizeof(double) * (size_t)c->nslot * c->npad,
+                                 c->stream),
+                 "zero tangent");
+    else
+        CUDA_TRY(launch_moments_tangent(c->shape, a, wx, wy, wz, tangent, c->stream), "tangent");
     CUDA_TRY(cudaEventRecord(tev[3], c->stream), "event");
     CUDA_TRY(launch_dag_grad(c->plan, c->train.recs, c->d_phase_row0, grid, c->nslot, N, c->npad,
                              basic, tangent, dlde_atom, adjoint2, epart, gscratch, c->d_err,
@@ -550,7 +564,8 @@ int loss_grad_compute(mtpb_context *c, const mtpb_labels *labels, const mtpb_los
     CUDA_TRY(launch_edge_grad(c->shape, a, wx, wy, wz, adjoint, adjoint2, uv, c->stream),
              "edge gradient");
     CUDA_TRY(cudaEventRecord(tev[5], c->stream), "event");
-    c->launches += c->shape == SHAPE_L24 ? 4 : 3;
+    c->launches += (energy_only ? 0 : grad_kernel_launches(c->shape, false)) + 1 +
+                   grad_kernel_launches(c->shape, true);
     const size_t rg_smem = sizeof(double) * RG_THREADS * (2 * m.R + 2 * nmu);
     CUDA_TRY(cudaFuncSetAttribute(k_radial_grad, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)rg_smem),

@@ -147,7 +147,9 @@ int mtpb_get_neighbors(const mtpb_context *ctx, int *offsets, int *nbr, double *
 /* Energy, forces, virial (and site energies) of the structures whose
  * neighbour list was built last; replaces PotMTP::getEFS(Atoms&,
  * AnyNeighborhoods&) (potential_mtp.cpp:1899-1933).  Positions are taken from
- * that build.  Outputs are `memory`-side arrays. */
+ * that build.  Outputs are `memory`-side arrays.  An output with neither
+ * forces nor stress asks for energies only (PotMTP::CalcE, the trainer's
+ * energy_only branch): the reverse pass is skipped. */
 int mtpb_efs_compute(mtpb_context *ctx, int memory, const mtpb_efs_output *out);
 
 /* Convenience: build + compute in one call (PotMTP::getEFS(Atoms&),

@@ -185,3 +185,20 @@ def test_neighbor_reuse_unchanged_positions_bit_identical(model_l20):
         gpu.efs_structures(b, reuse_neighbors=True, out=o2)
     for k in o1:
         assert np.array_equal(o1[k], o2[k])
+
+
+def test_energy_only_call_skips_the_reverse_pass(model_l20_k3):
+    """An output without forces and stress returns the same energies with
+    fewer launches, and no edge derivatives."""
+    from mtpb200 import MTPBError, MTPGpuDirect, StructureBatch
+    sts = configs.config2(3, seed=77)
+    b = StructureBatch.from_structures(sts)
+    with MTPGpuDirect(model_l20_k3, 0) as gpu:
+        e, f, s, se = gpu.efs(b, site_energy=True)
+        full = gpu.last_launch_count()
+        out = dict(energy=np.zeros(len(sts)), site_energy=np.zeros(b.n_atoms))
+        gpu.efs_structures(b, reuse_neighbors=False, out=out)
+        assert gpu.last_launch_count() < full
+        assert np.array_equal(out["energy"], e) and np.array_equal(out["site_energy"], se)
+        with pytest.raises(MTPBError):
+            gpu.edge_derivatives(10)
