@@ -177,6 +177,8 @@ EdgeArgs edge_args(const mtpb_context *c, int ncenter, const int *types, const i
     a.rx = rx;
     a.ry = ry;
     a.rz = rz;
+    // species pairs per edge exist for the lists built by mtpb_build_neighbors
+    a.pair = (nbr == c->nb.nbr && c->nb.pair) ? c->nb.pair : nullptr;
     a.group_maxdeg = c->d_group_maxdeg;
     a.K = c->model.K;
     a.R = c->model.R;
@@ -561,6 +563,15 @@ int mtpb_build_neighbors(mtpb_context *c, const mtpb_structures *in, int memory)
     cudaError_t e = build_neighbors(bi, c->arena, res, c->stream);
     if (e != cudaSuccess)
         return cuda_fail(e, "neighbour build");
+    {   // species pair of every edge, read by the moment kernels' prefetch
+        int *pair = c->arena.get<int>("edge_pair", (size_t)res.nedges + 1);
+        if (!pair)
+            return fail(MTPB_ERR_MEMORY, "device allocation failed");
+        CUDA_TRY(edge_pairs(res.nedges, res.center, res.nbr, d_types, c->model.K, pair,
+                            c->stream),
+                 "edge pairs");
+        res.pair = pair;
+    }
     c->nb = res;
     c->nedges = res.nedges;
     c->d_ns = d_ns;
@@ -614,8 +625,8 @@ int mtpb_build_neighbors(mtpb_context *c, const mtpb_structures *in, int memory)
     c->edge_epoch++;
     c->nb_built_this_call = true;
     // struct ids, wrap/bin, 3 scans (2 kernels each), cell fill and sort,
-    // count, fill, in-edge count, fill and sort
-    c->pending_launches = 17;
+    // count, fill, in-edge count, fill and sort, edge species pairs
+    c->pending_launches = 18;
     return MTPB_OK;
 }
 

@@ -105,6 +105,7 @@ struct EdgeArgs {
     const int *offsets;  // [natoms+1]
     const int *nbr;      // [E]
     const double *rx, *ry, *rz;  // [E]
+    const int *pair;             // [E] species pair it*K+jt (-1: a type is -1), or NULL
     const int *group_maxdeg;     // [ceil(natoms/32)]
     int K, R, mu_total;
     double scaling;

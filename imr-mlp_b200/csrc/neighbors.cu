@@ -454,6 +454,26 @@ cudaError_t refresh_edges(int natoms, const NbStruct *structs, const int *struct
     return cudaGetLastError();
 }
 
+__global__ void k_edge_pairs(long nedges, const int *__restrict__ center,
+                             const int *__restrict__ nbr, const int *__restrict__ types, int K,
+                             int *__restrict__ pair)
+{
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= nedges)
+        return;
+    const int it = types[center[e]], jt = types[nbr[e]];
+    pair[e] = (it >= 0 && jt >= 0) ? it * K + jt : -1;
+}
+
+cudaError_t edge_pairs(long nedges, const int *center, const int *nbr, const int *types, int K,
+                       int *pair, cudaStream_t s)
+{
+    if (nedges == 0)
+        return cudaSuccess;
+    k_edge_pairs<<<nblk(nedges, 256), 256, 0, s>>>(nedges, center, nbr, types, K, pair);
+    return cudaGetLastError();
+}
+
 cudaError_t edge_vectors(int ncenter, const int *offsets, const int *nbr, const double *x,
                          double *rx, double *ry, double *rz, cudaStream_t s)
 {

@@ -93,6 +93,7 @@ struct NbResult {
     const int *in_edges = nullptr;
     const int *struct_of = nullptr;   // [natoms]
     const int *center = nullptr;      // [nedges] centre of every edge
+    const int *pair = nullptr;        // [nedges] species pair it*K+jt, -1 for type -1
 };
 
 cudaError_t build_neighbors(const NbBuildInput &in, DeviceArena &arena, NbResult &res,
@@ -104,6 +105,8 @@ cudaError_t refresh_edges(int natoms, const NbStruct *structs, const int *struct
                           double *ry, double *rz, cudaStream_t s);
 cudaError_t edge_vectors(int ncenter, const int *offsets, const int *nbr, const double *x,
                          double *rx, double *ry, double *rz, cudaStream_t s);
+cudaError_t edge_pairs(long nedges, const int *center, const int *nbr, const int *types, int K,
+                       int *pair, cudaStream_t s);
 cudaError_t exclusive_scan(const int *in, int *out, int n, DeviceArena &arena, cudaStream_t s);
 
 // Host helper: fills the NbStruct of a periodic cell (Eigen-order inverse,
