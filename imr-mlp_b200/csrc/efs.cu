@@ -27,8 +27,6 @@
 
 namespace mtpb {
 
-constexpr int RAW_FIELDS = 4;   // rx, ry, rz, species pair of a prefetched chunk
-
 // staging arrays: 0 xhat, 1 yhat, 2 zhat, 3 1/r, 4.. f_mu, 4+NMU.. f'_mu
 template <class S, bool REV> constexpr int stage_rows()
 {
@@ -41,8 +39,6 @@ template <class S, bool REV> constexpr int smem_doubles(int K, int R)
     int n = stage_rows<S, REV>() * KS * STR;
     if (REV)
         n += NW * 3 * KS * 32;
-    if (KCfg<S, REV>::PF)
-        n += 2 * RAW_FIELDS * KS * 32 + 17;   // raw double buffer, edge offsets
     n += 4 * K * K;             // pair parameters
     n += K * K * S::NMU * R;    // radial coefficients of the used channels
     return n;
@@ -51,63 +47,15 @@ template <class S, bool REV> constexpr int smem_doubles(int K, int R)
 struct StageView {
     double *st;       // [rows][KS][STR]
     double *part;     // [NW][3][KS][32] (reverse only)
-    double *raw;      // [2][RAW_FIELDS][KS][32] (prefetching kernels)
-    int *soff;        // [33] edge offsets of the block's atoms
     const PairParams *pairs;
     const double *radial;  // [K*K][NMU][R]
 };
 
 // Computes the per-edge quantities of one chunk of edge slots for the 32
 // atoms of this block.  Every thread of the block takes part.
-// Raw edge data of one chunk in shared memory (prefetching kernels):
-// raw[field][slot][lane], fields rx, ry, rz and the species pair (an int in
-// the first word; -1 when a type is -1, -2 when the slot has no edge).
-
-__device__ __forceinline__ void cp_async8(double *dst, const void *src)
-{
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async4(void *dst, const void *src)
-{
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src)
-                 : "memory");
-}
-
-// Issues the asynchronous copies of chunk `chunk` into `raw`; soff holds the
-// edge offsets of the block's 33 atom boundaries.
-__device__ __forceinline__ void prefetch_chunk(const EdgeArgs &p, double *raw, const int *soff,
-                                               int atom0, int chunk)
-{
-    for (int item = threadIdx.x; item < 32 * KS; item += blockDim.x) {
-        const int lane = item / KS;
-        const int k = item - lane * KS;
-        const int e = soff[lane] + chunk * KS + k;
-        double *slot = raw + k * 32 + lane;
-        int *pslot = reinterpret_cast<int *>(slot + 3 * KS * 32);
-        if (atom0 + lane < p.natoms && e < soff[lane + 1]) {
-            cp_async8(slot, p.rx + e);
-            cp_async8(slot + KS * 32, p.ry + e);
-            cp_async8(slot + 2 * KS * 32, p.rz + e);
-            if (p.pair) {
-                cp_async4(pslot, p.pair + e);
-            } else {
-                const int it = __ldg(p.types + atom0 + lane);
-                const int jt = __ldg(p.types + __ldg(p.nbr + e));
-                *pslot = (it >= 0 && jt >= 0) ? it * p.K + jt : -1;
-            }
-        } else {
-            *pslot = -2;
-        }
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-}
-
-// PF: the chunk's raw edge data is read from `raw` (filled by prefetch_chunk)
-// instead of global memory.
-template <class S, int NW, bool REV, bool PF = false>
+template <class S, int NW, bool REV>
 __device__ __forceinline__ void stage_chunk(const EdgeArgs &p, const StageView &v, int atom0,
-                                            int chunk, const double *raw = nullptr)
+                                            int chunk)
 {
     constexpr int NMU = S::NMU;
     for (int item = threadIdx.x; item < 32 * KS; item += blockDim.x) {
@@ -124,16 +72,7 @@ __device__ __forceinline__ void stage_chunk(const EdgeArgs &p, const StageView &
         bool have = false;
         double x = 0.0, y = 0.0, z = 0.0;
         int pair = -1;
-        if constexpr (PF) {
-            const double *slot = raw + k * 32 + lane;
-            pair = *reinterpret_cast<const int *>(slot + 3 * KS * 32);
-            have = pair != -2;
-            if (have) {
-                x = slot[0];
-                y = slot[KS * 32];
-                z = slot[2 * KS * 32];
-            }
-        } else if (atom < p.natoms) {
+        if (atom < p.natoms) {
             const int e = __ldg(p.offsets + atom) + chunk * KS + k;
             if (e < __ldg(p.offsets + atom + 1)) {
                 have = true;
@@ -237,22 +176,8 @@ __device__ __forceinline__ void fwd_warp(const EdgeArgs &p, const StageView &v, 
     for (int i = 0; i < NACC; ++i)
         acc[i] = 0.0;
     const int nchunks = (maxdeg + KS - 1) / KS;
-    constexpr bool PF = KCfg<S, false>::PF;
-    constexpr int RAWN = RAW_FIELDS * KS * 32;
-    if constexpr (PF) {
-        if (nchunks > 0)
-            prefetch_chunk(p, v.raw, v.soff, atom0, 0);
-    }
     for (int ch = 0; ch < nchunks; ++ch) {
-        if constexpr (PF) {
-            asm volatile("cp.async.wait_all;" ::: "memory");
-            __syncthreads();
-            stage_chunk<S, NW, false, true>(p, v, atom0, ch, v.raw + (ch & 1) * RAWN);
-            if (ch + 1 < nchunks)
-                prefetch_chunk(p, v.raw + ((ch + 1) & 1) * RAWN, v.soff, atom0, ch + 1);
-        } else {
-            stage_chunk<S, NW, false>(p, v, atom0, ch);
-        }
+        stage_chunk<S, NW, false>(p, v, atom0, ch);
         __syncthreads();
         const int kend = min(KS, maxdeg - ch * KS);
         for (int k = 0; k < kend; ++k) {
@@ -352,22 +277,8 @@ __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, 
             adj[i] = 0.0;
     }
     const int nchunks = (maxdeg + KS - 1) / KS;
-    constexpr bool PF = KCfg<S, true>::PF;
-    constexpr int RAWN = RAW_FIELDS * KS * 32;
-    if constexpr (PF) {
-        if (nchunks > 0)
-            prefetch_chunk(p, v.raw, v.soff, atom0, 0);
-    }
     for (int ch = 0; ch < nchunks; ++ch) {
-        if constexpr (PF) {
-            asm volatile("cp.async.wait_all;" ::: "memory");
-            __syncthreads();
-            stage_chunk<S, NW, true, true>(p, v, atom0, ch, v.raw + (ch & 1) * RAWN);
-            if (ch + 1 < nchunks)
-                prefetch_chunk(p, v.raw + ((ch + 1) & 1) * RAWN, v.soff, atom0, ch + 1);
-        } else {
-            stage_chunk<S, NW, true>(p, v, atom0, ch);
-        }
+        stage_chunk<S, NW, true>(p, v, atom0, ch);
         __syncthreads();
         const int kend = min(KS, maxdeg - ch * KS);
         for (int k = 0; k < kend; ++k) {
@@ -495,14 +406,6 @@ __global__ void __launch_bounds__(ShapeCfg<S>::NW * 32, KCfg<S, REV>::BLOCKS)
     v.part = cur;
     if (REV)
         cur += NW * 3 * KS * 32;
-    if constexpr (KCfg<S, REV>::PF) {
-        v.raw = cur;
-        cur += 2 * RAW_FIELDS * KS * 32;
-        v.soff = reinterpret_cast<int *>(cur);
-        cur += 17;
-        for (int i = threadIdx.x; i <= 32; i += blockDim.x)
-            v.soff[i] = __ldg(p.offsets + min((int)blockIdx.x * 32 + i, p.natoms));
-    }
     PairParams *pairs = reinterpret_cast<PairParams *>(cur);
     cur += 4 * p.K * p.K;
     double *radial = cur;

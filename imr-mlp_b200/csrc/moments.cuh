@@ -34,10 +34,6 @@ template <class S, bool REV> struct KCfg {
     static constexpr int NW = ShapeCfg<S>::NW;
     static constexpr int NPART = REV ? ShapeCfg<S>::NPART_REV : ShapeCfg<S>::NPART;
     static constexpr int BLOCKS = NW > 4 ? 1 : NPART > 1 ? 3 : 2;
-    // cp.async prefetch of the next chunk's edge data: measured slower on the
-    // level-20 box (forward 4.27 -> 5.96 ms, reverse 14.2 -> 15.8 ms: one more
-    // barrier per chunk and many 8-byte copies), so it is off
-    static constexpr bool PF = false;
 };
 
 __device__ __forceinline__ double &SV(double *st, int row, int k, int lane)
