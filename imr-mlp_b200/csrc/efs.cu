@@ -897,51 +897,71 @@ cudaError_t launch_dag(const DagPlan &plan, const DagDevRec *recs, const int *ph
 // Forces and per-atom virial by gather (deterministic, no atomics):
 //   F_k = sum_{e in out(k)} d_e - sum_{e in in(k)} d_e      (getEFS scatter)
 //   W_k = - sum_{e in out(k)} d_e (x) r_e                   (stress_ -= d r)
+// One warp per atom: lanes stride over the atom's out- and in-edges
+// (coalesced edge arrays), then a fixed shuffle tree sums the lanes.
 // ----------------------------------------------------------------------------
-__global__ void k_force_gather(int natoms, int ntotal, const int *__restrict__ offsets,
-                               const int *__restrict__ in_offsets,
-                               const int *__restrict__ in_edges, const double *__restrict__ dx,
-                               const double *__restrict__ dy, const double *__restrict__ dz,
-                               const double *__restrict__ rx, const double *__restrict__ ry,
-                               const double *__restrict__ rz, double *__restrict__ forces,
-                               double *__restrict__ atom_virial, int accumulate)
+__global__ void __launch_bounds__(256)
+    k_force_gather(int natoms, int ntotal, const int *__restrict__ offsets,
+                   const int *__restrict__ in_offsets, const int *__restrict__ in_edges,
+                   const double *__restrict__ dx, const double *__restrict__ dy,
+                   const double *__restrict__ dz, const double *__restrict__ rx,
+                   const double *__restrict__ ry, const double *__restrict__ rz,
+                   double *__restrict__ forces, double *__restrict__ atom_virial,
+                   int accumulate)
 {
-    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    const int k = (int)(((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
     if (k >= ntotal)
-        return;
-    double fx = 0.0, fy = 0.0, fz = 0.0;
-    double w[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+        return;   // whole warps leave together
+    double v[12] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};   // F (3), W (9)
     if (k < natoms) {
-        for (int e = offsets[k]; e < offsets[k + 1]; ++e) {
+        const int e1 = offsets[k + 1];
+        for (int e = offsets[k] + lane; e < e1; e += 32) {
             const double a = dx[e], b = dy[e], c = dz[e];
-            fx += a;
-            fy += b;
-            fz += c;
             const double x = rx[e], y = ry[e], z = rz[e];
-            w[0] -= a * x; w[1] -= a * y; w[2] -= a * z;
-            w[3] -= b * x; w[4] -= b * y; w[5] -= b * z;
-            w[6] -= c * x; w[7] -= c * y; w[8] -= c * z;
+            v[0] += a;
+            v[1] += b;
+            v[2] += c;
+            v[3] -= a * x; v[4] -= a * y; v[5] -= a * z;
+            v[6] -= b * x; v[7] -= b * y; v[8] -= b * z;
+            v[9] -= c * x; v[10] -= c * y; v[11] -= c * z;
         }
     }
-    for (int q = in_offsets[k]; q < in_offsets[k + 1]; ++q) {
+    const int q1 = in_offsets[k + 1];
+    for (int q = in_offsets[k] + lane; q < q1; q += 32) {
         const int e = in_edges[q];
-        fx -= dx[e];
-        fy -= dy[e];
-        fz -= dz[e];
+        v[0] -= dx[e];
+        v[1] -= dy[e];
+        v[2] -= dz[e];
     }
-    if (accumulate) {
-        forces[3 * k] += fx;
-        forces[3 * k + 1] += fy;
-        forces[3 * k + 2] += fz;
-    } else {
-        forces[3 * k] = fx;
-        forces[3 * k + 1] = fy;
-        forces[3 * k + 2] = fz;
+    const bool vir = atom_virial && k < natoms;
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+            v[i] += __shfl_xor_sync(0xffffffffu, v[i], o);
+    if (vir) {
+#pragma unroll
+        for (int i = 3; i < 12; ++i)
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+                v[i] += __shfl_xor_sync(0xffffffffu, v[i], o);
     }
-    if (atom_virial && k < natoms) {
+    if (lane == 0) {
+        if (accumulate) {
+            forces[3 * (size_t)k] += v[0];
+            forces[3 * (size_t)k + 1] += v[1];
+            forces[3 * (size_t)k + 2] += v[2];
+        } else {
+            forces[3 * (size_t)k] = v[0];
+            forces[3 * (size_t)k + 1] = v[1];
+            forces[3 * (size_t)k + 2] = v[2];
+        }
+    }
+    if (vir && lane == 0) {
 #pragma unroll
         for (int i = 0; i < 9; ++i)
-            atom_virial[(size_t)i * natoms + k] = w[i];
+            atom_virial[(size_t)i * natoms + k] = v[3 + i];
     }
 }
 
@@ -953,10 +973,11 @@ cudaError_t launch_force_gather(int natoms, int ntotal, const int *offsets, cons
 {
     if (ntotal == 0)
         return cudaSuccess;
-    const int threads = 128;
-    k_force_gather<<<(ntotal + threads - 1) / threads, threads, 0, s>>>(
-        natoms, ntotal, offsets, in_offsets, in_edges, dx, dy, dz, rx, ry, rz, forces,
-        atom_virial, accumulate);
+    const int threads = 256;   // 8 atoms per block
+    const long blocks = ((long)ntotal * 32 + threads - 1) / threads;
+    k_force_gather<<<(unsigned)blocks, threads, 0, s>>>(natoms, ntotal, offsets, in_offsets,
+                                                        in_edges, dx, dy, dz, rx, ry, rz, forces,
+                                                        atom_virial, accumulate);
     return cudaGetLastError();
 }
 
