@@ -474,7 +474,8 @@ def run_train(args, torch, dist, ws, rank, local, dev, stream):
     """Training leg on every rank; returns the JSON object on rank 0."""
     from mtpb200 import MTPGpuDirect, StructureBatch
     sts, teacher, student = train_problem(args.train_configs)
-    mine = sts[rank::ws]
+    owner = shard_lpt([len(x["types"]) for x in sts], ws)   # whole structures, balanced
+    mine = [x for x, o in zip(sts, owner) if o == rank]
     batch = StructureBatch.from_structures(mine)
     with MTPGpuDirect(teacher, local) as tg:   # labels (untimed)
         e, f, st, _ = tg.efs(batch)
