@@ -50,9 +50,13 @@ TRAIN_UNIT = "configs/s"
 TRAIN_WEIGHTS = (1.0, 0.01, 0.001, 1.0, 0.0, 1.0)   # E, F, S and the default powers
 EV_PER_GPA_A3 = 1.0 / 160.21766208                    # 1 GPa * 1 A^3 in eV
 
-# DRAM traffic per atom of the dominant kernel, from the ncu capture
-# summarised in profiles/ (scaled from the 131k-atom capture by atom count).
-NCU_TRAFFIC_BYTES_PER_ATOM = {"k_moments_rev": None}
+# DRAM traffic (read + write) per atom of each kernel, from the ncu capture
+# summarised in profiles/ncu_moments_graph_config3-131k_l20.md (131,072 atoms;
+# traffic grows with the atom count, so it is scaled by atoms)
+NCU_TRAFFIC_BYTES_PER_ATOM = {"k_moments<fwd>": (180.45e6 + 255.94e6) / 131072,
+                              "k_dag": (310.33e6 + 267.49e6) / 131072,
+                              "k_moments<rev>": (493.33e6 + 134.06e6) / 131072}
+SMEM_BYTES_PER_SM_CLOCK = 128   # shared-memory bandwidth of an SM (nominal)
 
 
 def parse():
@@ -753,6 +757,32 @@ def run_ours(args):
     total_atoms = N * (1 if slab else ws) * args.steps
     value = total_atoms / (ms / 1e3)
     step_ms = float(kernel_ms[1:].sum())
+    fp64_view = {"achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                 "frac": achieved / peak if peak else None, "flops_per_atom": kflops,
+                 "peak_source": "measured by bench.py: cuBLAS DGEMM 8192^3 (torch.matmul "
+                                "float64); MEASURED_PEAKS.json has no FP64 figure"}
+    traffic = NCU_TRAFFIC_BYTES_PER_ATOM[kname] * n_centers
+    if kname == "k_dag":
+        # the graph kernel is bound by its shared-memory operand reads: two
+        # 8-byte rows per real record and atom
+        import torch as _t
+        sms = _t.cuda.get_device_properties(dev).multi_processor_count
+        mhz = clocks.get("sm_mhz") or 1965.0
+        smem_peak = sms * SMEM_BYTES_PER_SM_CLOCK * mhz * 1e6 / 1e9
+        bytes_ = 16.0 * recs * n_centers
+        ach = bytes_ / (kernel_ms[dom] / 1e3) / 1e9
+        roofline = {"bound": "smem", "kernel": kname, "achieved": ach, "peak": smem_peak,
+                    "unit": "GB/s", "frac": ach / smem_peak, "traffic": traffic,
+                    "algorithmic_bytes_per_atom": 16.0 * recs,
+                    "peak_source": f"nominal shared-memory bandwidth: {sms} SMs x "
+                                   f"{SMEM_BYTES_PER_SM_CLOCK} B per clock x {mhz:.0f} MHz "
+                                   "(measured clock); MEASURED_PEAKS.json has no shared-memory "
+                                   "figure",
+                    "traffic_source": "ncu dram__bytes_read+write of the 131k-atom capture, "
+                                      "scaled by atoms",
+                    "fp64": fp64_view}
+    else:
+        roofline = dict(fp64_view, bound="fp64", kernel=kname, traffic=traffic)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
@@ -771,12 +801,7 @@ def run_ours(args):
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "matches_device_energy": e2e_ok},
         "gpu_launches": int(launches),
-        "roofline": {"bound": "fp64", "kernel": kname, "achieved": achieved, "peak": peak,
-                     "unit": "TFLOP/s", "frac": achieved / peak if peak else None,
-                     "traffic": None,
-                     "peak_source": "measured by bench.py: cuBLAS DGEMM 8192^3 (torch.matmul "
-                                    "float64); MEASURED_PEAKS.json has no FP64 figure",
-                     "flops_per_atom": kflops},
+        "roofline": roofline,
         "kernel_ms": {"refresh": float(kernel_ms[0]), "neighbor_build": float(build_ms),
                       "moments_fwd": float(kernel_ms[1]), "graph": float(kernel_ms[2]),
                       "moments_rev": float(kernel_ms[3]), "gather_reduce": float(kernel_ms[4])},
