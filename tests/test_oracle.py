@@ -170,3 +170,21 @@ def test_oracle_gradient_finite_difference(oracle):
         lm = oracle.loss_grad(m.with_coefficients(cm), offs, types, nl, te, tf, ts)[0]
         fd = (lp - lm) / (2 * h)
         assert abs(fd - grad[k]) <= 3e-5 * max(1e-3, abs(fd)) + 3e-9, (k, fd, grad[k])
+
+
+@pytest.mark.parametrize("case", ["level24_k2", "config5_k3_r10"])
+def test_oracle_efs_matches_mlipcore_generated_level24(oracle, reference, case):
+    """The C restatement against the compiled reference MLIPCore on the
+    generated level-24 stand-ins (configs 4 and 5 models)."""
+    if case == "level24_k2":
+        m = configs.level24_model()
+        st = configs.config4_structures(1, seed=33)[0]
+    else:
+        m = configs.level24_model(species_count=3, rmin=0.8, rmax=6.0, rb_size=10, seed=55)
+        st = configs.ru_water_interface(3)
+    nl = oracle.neighbors(st["cell"], st["pbc"], st["positions"], m.cutoff)
+    e, se, f, s = oracle.efs(m, st["types"], nl)
+    e2, se2, f2, _ = reference.mlip_efs(format_mtp(m), st["types"], nl,
+                                        oracle.wrap(st["cell"], st["pbc"], st["positions"]))
+    assert abs(e - e2) < 1e-12 * max(1, abs(e))
+    assert np.max(np.abs(f - f2)) < 1e-11 * max(1.0, np.max(np.abs(f)))
