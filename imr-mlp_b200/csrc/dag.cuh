@@ -46,17 +46,17 @@ constexpr long DAG_WAIT_LIMIT = 1L << 22;   // bounded wait: sets the error flag
 
 // Geometry: ATOMS atoms per block, two atoms per lane; a record stream is
 // served by LPS = ATOMS/2 lanes, a warp serves SPW = 32/LPS streams and the
-// block DAG_STREAMS streams.  Records are laid out warp-major per phase
-// ([phase][warp][row][SPW streams], see dag_warp_major) so that every warp
+// block STREAMS streams.  Records are laid out warp-major per phase
+// ([phase][warp][row][SPW streams], see dag_device_records) so that every warp
 // streams its own contiguous records through a private double-buffered ring
 // filled by TMA bulk copies: warps only meet at the phase barriers.
-template <int ATOMS> struct DagGeom {
+template <int ATOMS, int STREAMS> struct DagGeom {
     static constexpr int APT = 2;
     static constexpr int LPS = ATOMS / APT;
     static constexpr int SPW = 32 / LPS;
-    static constexpr int WARPS = DAG_STREAMS / SPW;
+    static constexpr int WARPS = STREAMS / SPW;
     static constexpr int THREADS = WARPS * 32;
-    static constexpr int CH = DAG_CHUNK_ROWS;                // rows per ring slot
+    static constexpr int CH = dag_chunk_rows(STREAMS);       // rows per ring slot
     static constexpr unsigned SLOT_BYTES = CH * SPW * sizeof(DagDevRec);
     static constexpr size_t ring_bytes() { return (size_t)WARPS * 2 * SLOT_BYTES; }
 };

@@ -577,12 +577,12 @@ cudaError_t launch_group_maxdeg(int natoms, const int *offsets, int *group_maxde
 // Runs n consecutive records of one stream.  All records belong to one
 // phase, so a row written here is never read here and record loads may move
 // ahead of stores.
-template <int ATOMS, bool FWD, bool GR>
+template <int ATOMS, int STREAMS, bool FWD, bool GR>
 __device__ __forceinline__ void dag_segment(unsigned rec_addr, const Rows<GR> &rowsA, int n,
                                             double *acc, double *E, double *adjoint, int npad,
                                             int natoms, int atom_a)
 {
-    using G = DagGeom<ATOMS>;
+    using G = DagGeom<ATOMS, STREAMS>;
     constexpr unsigned REC_STRIDE = G::SPW * sizeof(DagDevRec);
     auto rare = [&](unsigned outf, double c) {
         if constexpr (FWD) {
@@ -664,8 +664,8 @@ __device__ __forceinline__ void dag_segment(unsigned rec_addr, const Rows<GR> &r
 
 // GR: rows in the global scratch slice of this block (graphs larger than
 // shared memory); the blocks then loop over the atom groups.
-template <int ATOMS, bool GR>
-__global__ void __launch_bounds__(DagGeom<ATOMS>::THREADS)
+template <int ATOMS, bool GR, int STREAMS>
+__global__ void __launch_bounds__(DagGeom<ATOMS, STREAMS>::THREADS)
     k_dag(const DagDevRec *__restrict__ recs, const int *__restrict__ phase_row0, int n_fwd,
           int n_rev, int one_row, int zero_row, int nrows, int nslot, int natoms, int npad,
           const int *__restrict__ types, const double *__restrict__ species_coeffs,
@@ -673,10 +673,10 @@ __global__ void __launch_bounds__(DagGeom<ATOMS>::THREADS)
           double *__restrict__ site_energy, double *__restrict__ gscratch,
           int *__restrict__ err_flag)
 {
-    using G = DagGeom<ATOMS>;
+    using G = DagGeom<ATOMS, STREAMS>;
     extern __shared__ __align__(128) unsigned char dsm[];
     __shared__ unsigned long long bar[G::WARPS][2];
-    __shared__ double epart[DAG_STREAMS][ATOMS];
+    __shared__ double epart[STREAMS][ATOMS];
     __shared__ int ph0[DAG_MAX_PHASES + 1];
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
@@ -702,7 +702,7 @@ __global__ void __launch_bounds__(DagGeom<ATOMS>::THREADS)
     const unsigned ring_u32 = smem_u32(ring) + g * sizeof(DagDevRec);
     auto phase_src = [&](int ph) {
         const int rows_p = ph0[ph + 1] - ph0[ph];
-        return recs + (size_t)ph0[ph] * DAG_STREAMS + (size_t)warp * rows_p * G::SPW;
+        return recs + (size_t)ph0[ph] * STREAMS + (size_t)warp * rows_p * G::SPW;
     };
     auto nchunks = [&](int ph) { return (ph0[ph + 1] - ph0[ph] + G::CH - 1) / G::CH; };
     // lane 0 issues the warp's chunks in consumption order (phase by phase,
@@ -772,10 +772,10 @@ __global__ void __launch_bounds__(DagGeom<ATOMS>::THREADS)
                 const int n = min(G::CH, rows_p - c * G::CH);
                 const unsigned rec_addr = ring_u32 + slot * G::SLOT_BYTES;
                 if (fwd)
-                    dag_segment<ATOMS, true, GR>(rec_addr, rowsA, n, acc, E, adjoint, npad,
+                    dag_segment<ATOMS, STREAMS, true, GR>(rec_addr, rowsA, n, acc, E, adjoint, npad,
                                                  natoms, atom0 + a0);
                 else
-                    dag_segment<ATOMS, false, GR>(rec_addr, rowsA, n, acc, E, adjoint, npad,
+                    dag_segment<ATOMS, STREAMS, false, GR>(rec_addr, rowsA, n, acc, E, adjoint, npad,
                                                   natoms, atom0 + a0);
                 __syncwarp();
                 if (lane == 0) {
@@ -794,7 +794,7 @@ __global__ void __launch_bounds__(DagGeom<ATOMS>::THREADS)
                     double se = 0.0;
                     if (t >= 0) {
                         se = species_coeffs[t];
-                        for (int s2 = 0; s2 < DAG_STREAMS; ++s2)
+                        for (int s2 = 0; s2 < STREAMS; ++s2)
                             se += epart[s2][tid];
                     }
                     site_energy[atom0 + tid] = se;
@@ -809,16 +809,17 @@ __global__ void __launch_bounds__(DagGeom<ATOMS>::THREADS)
 // offsets, operand rows stay indices.
 std::vector<DagDevRec> dag_device_records(const DagPlan &plan)
 {
-    const int spw = plan.atoms == 16 ? DagGeom<16>::SPW : DagGeom<8>::SPW;
+    const int spw = plan.atoms == 16 ? DagGeom<16, 32>::SPW : DagGeom<8, 32>::SPW;
     const unsigned row_bytes = (unsigned)plan.atoms * 8;
     std::vector<DagDevRec> out(plan.recs.size());
     size_t row0 = 0, o = 0;
-    const int warps = DAG_STREAMS / spw;
+    const int S = plan.streams;
+    const int warps = S / spw;
     for (int rows_p : plan.phase_rows) {
         for (int w = 0; w < warps; ++w)
             for (int r = 0; r < rows_p; ++r)
                 for (int s = 0; s < spw; ++s) {
-                    const DagRec &in = plan.recs[(row0 + r) * DAG_STREAMS + w * spw + s];
+                    const DagRec &in = plan.recs[(row0 + r) * S + w * spw + s];
                     DagDevRec d{};
                     d.rows = in.s12;   // row indices; the kernel scales them
                     d.c = in.c;
@@ -840,21 +841,22 @@ std::vector<DagDevRec> dag_device_records(const DagPlan &plan)
 
 size_t dag_ring_bytes(int atoms)
 {
-    return atoms == 16 ? DagGeom<16>::ring_bytes() : DagGeom<8>::ring_bytes();
+    // the same for both stream counts (dag_chunk_rows)
+    return atoms == 16 ? DagGeom<16, 32>::ring_bytes() : DagGeom<8, 32>::ring_bytes();
 }
 
-template <int ATOMS, bool GR>
+template <int ATOMS, bool GR, int STREAMS>
 static cudaError_t launch_dag_geom(const DagPlan &plan, const DagDevRec *recs,
                                    const int *phase_row0, int nslot, int natoms, int npad,
                                    const int *types, const double *species_coeffs,
                                    const double *basic, double *adjoint, double *site_energy,
                                    double *gscratch, int *err_flag, cudaStream_t s)
 {
-    using G = DagGeom<ATOMS>;
+    using G = DagGeom<ATOMS, STREAMS>;
     const int ngroups = (natoms + ATOMS - 1) / ATOMS;
     const int blocks = GR ? std::min(ngroups, plan.grid) : ngroups;
     const size_t smem = G::ring_bytes() + (GR ? 0 : sizeof(double) * (size_t)plan.nrows * ATOMS);
-    auto kern = k_dag<ATOMS, GR>;
+    auto kern = k_dag<ATOMS, GR, STREAMS>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)smem);
     if (err == cudaSuccess && GR)   // leave the rest of the SM's memory to L1
@@ -877,20 +879,23 @@ cudaError_t launch_dag(const DagPlan &plan, const DagDevRec *recs, const int *ph
         return cudaSuccess;
     if (plan.n_fwd + plan.n_rev > DAG_MAX_PHASES)
         return cudaErrorInvalidValue;
+    const bool large = plan.streams == DAG_STREAMS_LARGE;
+    if (plan.streams != DAG_STREAMS && !large)
+        return cudaErrorInvalidValue;
+#define MTPB_DAG_LAUNCH(A, GR, S, SCR)                                                             \
+    launch_dag_geom<A, GR, S>(plan, recs, phase_row0, nslot, natoms, npad, types, species_coeffs, \
+                              basic, adjoint, site_energy, SCR, err_flag, s)
     if (plan.global_rows) {
         if (plan.atoms != 16 || !gscratch || plan.grid < 1)
             return cudaErrorInvalidValue;
-        return launch_dag_geom<16, true>(plan, recs, phase_row0, nslot, natoms, npad, types,
-                                         species_coeffs, basic, adjoint, site_energy, gscratch,
-                                         err_flag, s);
+        return large ? MTPB_DAG_LAUNCH(16, true, 64, gscratch)
+                     : MTPB_DAG_LAUNCH(16, true, 32, gscratch);
     }
     if (plan.atoms == 16)
-        return launch_dag_geom<16, false>(plan, recs, phase_row0, nslot, natoms, npad, types,
-                                          species_coeffs, basic, adjoint, site_energy, nullptr,
-                                          err_flag, s);
-    return launch_dag_geom<8, false>(plan, recs, phase_row0, nslot, natoms, npad, types,
-                                     species_coeffs, basic, adjoint, site_energy, nullptr,
-                                     err_flag, s);
+        return large ? MTPB_DAG_LAUNCH(16, false, 64, nullptr)
+                     : MTPB_DAG_LAUNCH(16, false, 32, nullptr);
+    return large ? MTPB_DAG_LAUNCH(8, false, 64, nullptr) : MTPB_DAG_LAUNCH(8, false, 32, nullptr);
+#undef MTPB_DAG_LAUNCH
 }
 
 // ----------------------------------------------------------------------------

@@ -559,25 +559,28 @@ cudaError_t launch_edge_grad(int shape, const EdgeArgs &a, const double *wx, con
 // dLdE m + D_w m of their scalar moment to the block's gradient (the record's
 // coefficient names it); reverse END|GLOBAL records store abar of a basic moment.
 // ----------------------------------------------------------------------------
-struct DagGradGeom {
+template <int STREAMS> struct DagGradGeomT {
     static constexpr int ATOMS = 8;
     static constexpr int LPS = 8;                 // lanes per stream (one atom each)
     static constexpr int SPW = 32 / LPS;          // streams per warp
-    static constexpr int WARPS = DAG_STREAMS / SPW;
+    static constexpr int WARPS = STREAMS / SPW;
     static constexpr int THREADS = WARPS * 32;
-    static constexpr int CH = DAG_CHUNK_ROWS;
+    static constexpr int CH = dag_chunk_rows(STREAMS);
     static constexpr unsigned SLOT_BYTES = CH * SPW * sizeof(DagDevRec);
     static constexpr unsigned ROW_BYTES = ATOMS * 16;
     static constexpr size_t ring_bytes() { return (size_t)WARPS * 2 * SLOT_BYTES; }
 };
+// ring and row sizes are the same for both stream counts
+using DagGradGeom = DagGradGeomT<DAG_STREAMS>;
+static_assert(DagGradGeomT<DAG_STREAMS_LARGE>::ring_bytes() == DagGradGeom::ring_bytes(), "");
 
-template <bool FWD, bool GR>
+template <bool FWD, bool GR, int STREAMS>
 __device__ __forceinline__ void dag_grad_segment(unsigned rec_addr, const Rows<GR> &rowA, int n,
                                                  double &acc, double &accd, double dlde,
                                                  bool valid, unsigned gmask, int q, double *gsm,
                                                  double *adjoint2, int npad, int atom)
 {
-    using G = DagGradGeom;
+    using G = DagGradGeomT<STREAMS>;
     constexpr unsigned REC_STRIDE = G::SPW * sizeof(DagDevRec);
     constexpr unsigned RS = 7;   // log2 of the row size in bytes (8 atoms x 16 B)
     // ENERGY records multiply the zero row by itself; their coefficient holds
@@ -664,8 +667,8 @@ __device__ __forceinline__ void dag_grad_segment(unsigned rec_addr, const Rows<G
 
 // GR: rows in the global scratch slice of this block (graphs larger than
 // shared memory)
-template <bool GR>
-__global__ void __launch_bounds__(DagGradGeom::THREADS)
+template <bool GR, int STREAMS>
+__global__ void __launch_bounds__(DagGradGeomT<STREAMS>::THREADS)
     k_dag_grad(const DagDevRec *__restrict__ recs, const int *__restrict__ phase_row0, int n_fwd,
                int n_rev, int one_row, int zero_row, int one_adj_row, int nrows, int nslot,
                int natoms, int npad, const double *__restrict__ basic,
@@ -673,7 +676,7 @@ __global__ void __launch_bounds__(DagGradGeom::THREADS)
                int n_energy, double *__restrict__ adjoint2, double *__restrict__ energy_partials,
                double *__restrict__ gscratch, int *__restrict__ err_flag)
 {
-    using G = DagGradGeom;
+    using G = DagGradGeomT<STREAMS>;
     extern __shared__ __align__(128) unsigned char dsm[];
     __shared__ unsigned long long bar[G::WARPS][2];
     __shared__ int ph0[DAG_MAX_PHASES + 1];
@@ -704,7 +707,7 @@ __global__ void __launch_bounds__(DagGradGeom::THREADS)
     const unsigned ring_u32 = smem_u32(ring) + g * sizeof(DagDevRec);
     auto phase_src = [&](int ph) {
         const int rows_p = ph0[ph + 1] - ph0[ph];
-        return recs + (size_t)ph0[ph] * DAG_STREAMS + (size_t)warp * rows_p * G::SPW;
+        return recs + (size_t)ph0[ph] * STREAMS + (size_t)warp * rows_p * G::SPW;
     };
     auto nchunks = [&](int ph) { return (ph0[ph + 1] - ph0[ph] + G::CH - 1) / G::CH; };
     int iph = 0, ic = 0, nissued = 0, kw = 0;
@@ -776,10 +779,10 @@ __global__ void __launch_bounds__(DagGradGeom::THREADS)
                 const int n = min(G::CH, rows_p - c * G::CH);
                 const unsigned rec_addr = ring_u32 + slot * G::SLOT_BYTES;
                 if (fwd)
-                    dag_grad_segment<true, GR>(rec_addr, rowA, n, acc, accd, dlde, valid, gmask, q,
+                    dag_grad_segment<true, GR, STREAMS>(rec_addr, rowA, n, acc, accd, dlde, valid, gmask, q,
                                            gsm, adjoint2, npad, atom);
                 else
-                    dag_grad_segment<false, GR>(rec_addr, rowA, n, acc, accd, dlde, valid, gmask, q,
+                    dag_grad_segment<false, GR, STREAMS>(rec_addr, rowA, n, acc, accd, dlde, valid, gmask, q,
                                             gsm, adjoint2, npad, atom);
                 __syncwarp();
                 if (lane == 0) {
@@ -810,10 +813,10 @@ std::vector<DagDevRec> dag_grad_records(const DagPlan &plan)
     for (size_t ph = 0; ph < plan.phase_rows.size(); ++ph) {
         const int rows_p = plan.phase_rows[ph];
         const bool rev = (int)ph >= plan.n_fwd;
-        for (int w = 0; w < G::WARPS; ++w)
+        for (int w = 0; w < plan.streams / G::SPW; ++w)
             for (int r = 0; r < rows_p; ++r)
                 for (int s = 0; s < G::SPW; ++s) {
-                    const size_t idx = (row0 + r) * DAG_STREAMS + w * G::SPW + s;
+                    const size_t idx = (row0 + r) * plan.streams + w * G::SPW + s;
                     const DagRec &in = plan.recs[idx];
                     DagDevRec d{};
                     int s1 = (int)(in.s12 & 0xffffu), s2 = (int)(in.s12 >> 16);
@@ -865,9 +868,12 @@ int dag_grad_grid(const DagPlan &plan, int natoms)
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const size_t smem = dag_grad_smem_bytes(plan, false);
-    if (cudaFuncSetAttribute(k_dag_grad<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) == cudaSuccess)
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_dag_grad<false>, G::THREADS, smem);
+    const bool large = plan.streams == DAG_STREAMS_LARGE;
+    auto kern = large ? k_dag_grad<false, DAG_STREAMS_LARGE> : k_dag_grad<false, DAG_STREAMS>;
+    const int threads = large ? DagGradGeomT<DAG_STREAMS_LARGE>::THREADS : G::THREADS;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
+        cudaSuccess)
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, threads, smem);
     per = per < 1 ? 1 : per;
     return std::max(1, std::min(ngroups, sms * per));
 }
@@ -887,14 +893,20 @@ cudaError_t launch_dag_grad(const DagPlan &plan, const DagDevRec *recs, const in
     if (gr && (!gscratch || grid > plan.grad_grid))
         return cudaErrorInvalidValue;
     const size_t smem = dag_grad_smem_bytes(plan, gr);
-    auto kern = gr ? k_dag_grad<true> : k_dag_grad<false>;
+    const bool large = plan.streams == DAG_STREAMS_LARGE;
+    if (plan.streams != DAG_STREAMS && !large)
+        return cudaErrorInvalidValue;
+    auto kern = gr ? (large ? k_dag_grad<true, DAG_STREAMS_LARGE> : k_dag_grad<true, DAG_STREAMS>)
+                   : (large ? k_dag_grad<false, DAG_STREAMS_LARGE>
+                            : k_dag_grad<false, DAG_STREAMS>);
+    const int threads = large ? DagGradGeomT<DAG_STREAMS_LARGE>::THREADS : G::THREADS;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)smem);
     if (err == cudaSuccess && gr)   // leave the rest of the SM's memory to L1
         err = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 25);
     if (err != cudaSuccess)
         return err;
-    kern<<<grid, G::THREADS, smem, s>>>(recs, phase_row0, plan.n_fwd, plan.n_rev, plan.one_row,
+    kern<<<grid, threads, smem, s>>>(recs, phase_row0, plan.n_fwd, plan.n_rev, plan.one_row,
                                         plan.zero_row, plan.nrows, plan.nrows + 1, nslot, natoms,
                                         npad, basic, tangent, dlde_atom,
                                         (int)plan.energy_moments.size(), adjoint2,

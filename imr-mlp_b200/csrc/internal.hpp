@@ -59,13 +59,13 @@ inline DagRec make_rec(int s1, int s2, int out, unsigned flags, double c)
     return r;
 }
 
-#ifndef MTPB_DAG_STREAMS
-#define MTPB_DAG_STREAMS 32
-#endif
-#ifndef MTPB_DAG_CHUNK_ROWS
-#define MTPB_DAG_CHUNK_ROWS 32
-#endif
-constexpr int DAG_STREAMS = MTPB_DAG_STREAMS;         // record streams per block
+// Record streams per graph block: 32, or 64 for graphs whose rows do not fit
+// in shared memory (those run from L2 and gain from the extra warps).
+constexpr int DAG_STREAMS = 32;
+constexpr int DAG_STREAMS_LARGE = 64;
+constexpr int DAG_STREAMS_MAX = 64;
+// record rows per ring slot (the ring stays 32 KB for both stream counts)
+constexpr int dag_chunk_rows(int streams) { return streams > 32 ? 16 : 32; }
 
 // Device form of a record (16 bytes): the two operand row indices (16 bits
 // each), a word that is zero for plain product records and otherwise holds
@@ -75,7 +75,6 @@ struct alignas(16) DagDevRec {
     unsigned outf;
     double c;
 };
-constexpr int DAG_CHUNK_ROWS = MTPB_DAG_CHUNK_ROWS;   // record rows per shared chunk
 
 struct DagPlan {
     int nrows = 0;           // rows (one double per atom each)
@@ -84,7 +83,8 @@ struct DagPlan {
     int scratch_row = 0;     // row receiving stores that nothing reads
     std::vector<int> phase_rows;   // record rows per phase (fwd phases, then reverse)
     int n_fwd = 0, n_rev = 0;
-    std::vector<DagRec> recs;      // [sum rows][DAG_STREAMS]
+    int streams = DAG_STREAMS;     // record streams (DAG_STREAMS or DAG_STREAMS_LARGE)
+    std::vector<DagRec> recs;      // [sum rows][streams]
     // training: index into energy_moments of the scalar moment an ENERGY
     // record closes (-1 for every other record), parallel to recs
     std::vector<int> rec_energy;

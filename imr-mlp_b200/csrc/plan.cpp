@@ -145,9 +145,10 @@ void emit_phase(std::vector<Item> &items, DagPlan &plan)
     std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
         return items[a].recs.size() > items[b].recs.size();
     });
-    std::vector<std::vector<DagRec>> streams(DAG_STREAMS);
-    std::vector<std::vector<int>> energy(DAG_STREAMS);
-    std::vector<size_t> load(DAG_STREAMS, 0);
+    const int S = plan.streams;
+    std::vector<std::vector<DagRec>> streams(S);
+    std::vector<std::vector<int>> energy(S);
+    std::vector<size_t> load(S, 0);
     for (int idx : order) {
         int s = (int)(std::min_element(load.begin(), load.end()) - load.begin());
         for (const DagRec &r : items[idx].recs) {
@@ -159,7 +160,7 @@ void emit_phase(std::vector<Item> &items, DagPlan &plan)
     size_t len = *std::max_element(load.begin(), load.end());
     const DagRec pad = make_rec(plan.zero_row, plan.zero_row, 0, 0, 0.0);
     for (size_t r = 0; r < len; ++r)
-        for (int s = 0; s < DAG_STREAMS; ++s) {
+        for (int s = 0; s < S; ++s) {
             const bool real = r < streams[s].size();
             plan.recs.push_back(real ? streams[s][r] : pad);
             plan.rec_energy.push_back(real ? energy[s][r] : -1);
@@ -221,6 +222,10 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
     plan.scratch_row = next++;
     plan.nrows = next;
     plan.energy_moments = energy_moments;
+    // graphs beyond shared memory at 8 atoms per block run from L2 with 64
+    // streams (twice the warps); the others keep 32 (less padding)
+    plan.streams = (size_t)plan.nrows * 8 * sizeof(double) > 200 * 1024 ? DAG_STREAMS_LARGE
+                                                                          : DAG_STREAMS;
     if (plan.nrows >= 65535) {   // the dual graph adds one row
         if (err)
             *err = "moment graph too large for 16-bit row indices (" +

@@ -31,13 +31,14 @@ def program(model):
                                 None, None, recs.ctypes.data_as(C.POINTER(C.c_uint)))
     assert rc == 0
     nslot, nrows, one, zero, nf, nr = (v.value for v in ints)
+    streams = nrec.value // int(phases[:nf + nr].sum())
     return dict(nslot=nslot, sob=sob, nrows=nrows, one=one, zero=zero, n_fwd=nf, n_rev=nr,
-                phase_rows=phases[:nf + nr], recs=recs)
+                phase_rows=phases[:nf + nr], recs=recs, streams=streams)
 
 
 def interpret(prog, basic_slots, species_part):
     """Executes the record streams (efs.cu k_dag semantics) for all atoms."""
-    S = 32
+    S = prog["streams"]
     natoms = basic_slots.shape[1]
     rows = np.zeros((prog["nrows"], natoms))
     rows[:prog["nslot"]] = basic_slots
@@ -98,7 +99,27 @@ def test_program_stream_balance_level20():
     """Padding stays small: LPT assignment over 32 streams."""
     m = load_model("l20_k2.mtp")
     prog = program(m)
+    assert prog["streams"] == 32
     recs = prog["recs"].reshape(-1, 32, 4)
     pad = np.sum((recs[:, :, 2] == 0) & (recs[:, :, 3] == 0) & (recs[:, :, 1] >> 16 == 0))
     assert pad / recs.shape[0] / 32 < 0.1
     assert prog["nrows"] * 16 * 8 <= 190 * 1024
+
+
+def test_level24_program_64_streams_matches_oracle(oracle):
+    """The generated level-24 graph (beyond shared memory) is planned on 64
+    streams; its program still reproduces the oracle's site energies and
+    basic-moment adjoints."""
+    m = configs.level24_model()
+    prog = program(m)
+    assert prog["streams"] == 64
+    st = configs.config4_structures(1, seed=72)[0]
+    nl = oracle.neighbors(st["cell"], st["pbc"], st["positions"], m.cutoff)
+    se, _ = oracle.site_derivatives(m, st["types"], nl)
+    b, a = oracle.site_moments(m, st["types"], nl)
+    n = 4
+    slots = np.zeros((prog["nslot"], n))
+    slots[prog["sob"]] = b[:n].T
+    e, adj = interpret(prog, slots, m.species_coeffs[st["types"][:n]])
+    assert np.max(np.abs(e - se[:n])) < 1e-12 * max(1, np.max(np.abs(se)))
+    assert np.max(np.abs(adj[prog["sob"]].T - a[:n])) < 1e-11 * max(1, np.max(np.abs(a)))
