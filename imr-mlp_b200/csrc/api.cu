@@ -345,6 +345,11 @@ int mtpb_create(int device, const mtpb_model_view *view, mtpb_context **out)
             }
         if (rc != MTPB_OK)
             break;
+        if ((e = cudaEventCreateWithFlags(&c->stage_ev, cudaEventDisableTiming)) !=
+            cudaSuccess) {
+            rc = cuda_fail(e, "cudaEventCreate");
+            break;
+        }
         rc = upload_model(c);
     } while (false);
     if (rc != MTPB_OK) {
@@ -370,6 +375,10 @@ int mtpb_destroy(mtpb_context *c)
     for (auto &ev : c->train.ev)
         if (ev)
             cudaEventDestroy(ev);
+    if (c->stage_ev)
+        cudaEventDestroy(c->stage_ev);
+    if (c->h_stage)
+        cudaFreeHost(c->h_stage);
     if (c->own_stream)
         cudaStreamDestroy(c->own_stream);
     delete c;
@@ -532,19 +541,6 @@ int mtpb_build_neighbors(mtpb_context *c, const mtpb_structures *in, int memory)
                  "copy types");
         d_types = t;
     }
-    // host-side type check (small cost relative to the build)
-    {
-        std::vector<int> ht(N);
-        if (N > 0)
-            CUDA_TRY(cudaMemcpyAsync(ht.data(), d_types, sizeof(int) * N, cudaMemcpyDeviceToHost,
-                                     c->stream),
-                     "read types");
-        CUDA_TRY(cudaStreamSynchronize(c->stream), "sync");
-        for (int i = 0; i < N; ++i)
-            if (ht[i] < 0 || ht[i] >= c->model.K)
-                return fail(MTPB_ERR_ARGUMENT, "atom " + std::to_string(i) +
-                                                   " has a species index outside 0..K-1");
-    }
     const int NC = c->center_count_req > 0 ? c->center_count_req : N;
     if (NC > N)
         return fail(MTPB_ERR_ARGUMENT, "center count " + std::to_string(NC) +
@@ -558,11 +554,16 @@ int mtpb_build_neighbors(mtpb_context *c, const mtpb_structures *in, int memory)
     bi.atom_offsets = d_aoff;
     bi.structs = d_ns;
     bi.positions = d_pos;
+    bi.types = d_types;   // species range checked on the device, read with the edge count
+    bi.K = c->model.K;
     CUDA_TRY(cudaEventRecord(c->ev[0], c->stream), "event");
     NbResult res;
     cudaError_t e = build_neighbors(bi, c->arena, res, c->stream);
     if (e != cudaSuccess)
         return cuda_fail(e, "neighbour build");
+    if (res.bad_type >= 0)
+        return fail(MTPB_ERR_ARGUMENT, "atom " + std::to_string(res.bad_type) +
+                                           " has a species index outside 0..K-1");
     {   // species pair of every edge, read by the moment kernels' prefetch
         int *pair = c->arena.get<int>("edge_pair", (size_t)res.nedges + 1);
         if (!pair)
@@ -604,28 +605,42 @@ int mtpb_build_neighbors(mtpb_context *c, const mtpb_structures *in, int memory)
     }
     s0[S] = (int)sb.size();
     c->nseg = (int)sb.size();
-    c->d_seg_begin = c->arena.get<int>("seg_begin", sb.size() + 1);
-    c->d_seg_end = c->arena.get<int>("seg_end", se.size() + 1);
-    c->d_struct_seg0 = c->arena.get<int>("struct_seg0", S + 1);
-    if (!c->d_seg_begin || !c->d_seg_end || !c->d_struct_seg0)
+    // one upload of the three tables through pinned staging (no stream sync:
+    // the staging buffer is rewritten only after its last copy has finished)
+    const size_t nseg_tab = sb.size(), ntab = 2 * nseg_tab + (size_t)S + 1;
+    int *d_tab = c->arena.get<int>("seg_tables", ntab + 1);
+    if (!d_tab)
         return fail(MTPB_ERR_MEMORY, "device allocation failed");
-    if (!sb.empty()) {
-        CUDA_TRY(cudaMemcpyAsync(c->d_seg_begin, sb.data(), sizeof(int) * sb.size(),
-                                 cudaMemcpyHostToDevice, c->stream),
-                 "upload segments");
-        CUDA_TRY(cudaMemcpyAsync(c->d_seg_end, se.data(), sizeof(int) * se.size(),
-                                 cudaMemcpyHostToDevice, c->stream),
-                 "upload segments");
+    if (c->stage_pending)
+        CUDA_TRY(cudaEventSynchronize(c->stage_ev), "staging buffer");
+    c->stage_pending = false;
+    if (c->h_stage_cap < ntab) {
+        if (c->h_stage)
+            cudaFreeHost(c->h_stage);
+        c->h_stage = nullptr;
+        c->h_stage_cap = 0;
+        CUDA_TRY(cudaHostAlloc(reinterpret_cast<void **>(&c->h_stage), sizeof(int) * (ntab + 1024),
+                               cudaHostAllocDefault),
+                 "pinned staging");
+        c->h_stage_cap = ntab + 1024;
     }
-    CUDA_TRY(cudaMemcpyAsync(c->d_struct_seg0, s0.data(), sizeof(int) * (S + 1),
-                             cudaMemcpyHostToDevice, c->stream),
+    std::copy(sb.begin(), sb.end(), c->h_stage);
+    std::copy(se.begin(), se.end(), c->h_stage + nseg_tab);
+    std::copy(s0.begin(), s0.end(), c->h_stage + 2 * nseg_tab);
+    CUDA_TRY(cudaMemcpyAsync(d_tab, c->h_stage, sizeof(int) * ntab, cudaMemcpyHostToDevice,
+                             c->stream),
              "upload segments");
-    CUDA_TRY(cudaStreamSynchronize(c->stream), "neighbour build");
+    CUDA_TRY(cudaEventRecord(c->stage_ev, c->stream), "event");
+    c->stage_pending = true;
+    c->d_seg_begin = d_tab;
+    c->d_seg_end = d_tab + nseg_tab;
+    c->d_struct_seg0 = d_tab + 2 * nseg_tab;
     c->have_list = true;
     c->edge_epoch++;
     c->nb_built_this_call = true;
-    // struct ids, wrap/bin, 3 scans (2 kernels each), cell fill and sort,
-    // count, fill, in-edge count, fill and sort, edge species pairs
+    // struct ids, wrap/bin, 3 scans (2 kernels each), cell fill, sort and
+    // position gather, count, fill, in-edge count, fill and sort, edge species
+    // pairs
     c->pending_launches = 18;
     return MTPB_OK;
 }
@@ -647,6 +662,7 @@ int mtpb_get_neighbors(const mtpb_context *c, int *offsets, int *nbr, double *ri
     if (!c->have_list)
         return fail(MTPB_ERR_STATE, "no neighbour list has been built");
     CUDA_TRY(cudaSetDevice(c->device), "cudaSetDevice");
+    CUDA_TRY(cudaStreamSynchronize(c->stream), "sync");   // the build is stream-ordered
     const long E = c->nedges;
     if (offsets)
         CUDA_TRY(cudaMemcpy(offsets, c->nb.offsets, sizeof(int) * (c->natoms + 1),
@@ -855,6 +871,7 @@ int mtpb_get_site_moments(const mtpb_context *c, double *basic, double *adjoint)
     if (!c->have_efs)
         return fail(MTPB_ERR_STATE, "no EFS result available");
     CUDA_TRY(cudaSetDevice(c->device), "cudaSetDevice");
+    CUDA_TRY(cudaStreamSynchronize(c->stream), "sync");
     const int nb = c->model.nb();
     const int N = c->natoms;
     auto fetch = [&](const char *name, double *dst) -> int {
@@ -882,6 +899,7 @@ int mtpb_get_edge_derivatives(const mtpb_context *c, double *dedr)
     if (!c->have_efs || !c->have_dedr)
         return fail(MTPB_ERR_STATE, "no EFS result available");
     CUDA_TRY(cudaSetDevice(c->device), "cudaSetDevice");
+    CUDA_TRY(cudaStreamSynchronize(c->stream), "sync");
     const long E = c->nedges;
     DeviceArena &ar = const_cast<DeviceArena &>(c->arena);
     std::vector<double> x(E), y(E), z(E);

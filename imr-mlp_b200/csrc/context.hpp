@@ -85,9 +85,15 @@ struct mtpb_context {
     int pending_launches = 0;   // neighbour build / refresh launches of this call
     bool have_efs = false;
     bool have_dedr = false;   // the last EFS call ran the reverse pass
-    long edge_epoch = 0;
+    long edge_epoch = 0;     // advanced whenever the edge list or its vectors change
     int dag_atoms_env = 0;   // MTPB_DAG_ATOMS override of the graph block width
-    bool force_global_rows = false;   // MTPB_DAG_GLOBAL_ROWS=1   // advanced whenever the edge list or its vectors change
+    bool force_global_rows = false;   // MTPB_DAG_GLOBAL_ROWS=1
+    // pinned staging of the per-build segment tables; stage_ev marks the end of
+    // its last upload
+    int *h_stage = nullptr;
+    size_t h_stage_cap = 0;
+    cudaEvent_t stage_ev = nullptr;
+    bool stage_pending = false;
     mtpb::TrainingState train;
 };
 

@@ -139,16 +139,118 @@ __global__ void k_sort_segments(int nseg, const int *__restrict__ start, int *__
     }
 }
 
-// Traverses the candidate set of centre i; FILL selects counting or writing.
+// Bitonic sort of n = 32 V keys held by one warp, key k = v * 32 + lane in
+// register v of that lane; ascending.
+template <int V> __device__ __forceinline__ void warp_bitonic(int (&a)[V], int lane)
+{
+#pragma unroll
+    for (int size = 2; size <= 32 * V; size <<= 1) {
+#pragma unroll
+        for (int j = size >> 1; j > 0; j >>= 1) {
+            if (j >= 32) {   // partner in register v ^ (j / 32) of the same lane
+#pragma unroll
+                for (int v = 0; v < V; ++v) {
+                    const int w = v ^ (j >> 5);
+                    if (w > v) {
+                        const bool up = (((v << 5) | lane) & size) == 0;
+                        const int lo = min(a[v], a[w]), hi = max(a[v], a[w]);
+                        a[v] = up ? lo : hi;
+                        a[w] = up ? hi : lo;
+                    }
+                }
+            } else {   // partner in lane ^ j, same register
+#pragma unroll
+                for (int v = 0; v < V; ++v) {
+                    const int other = __shfl_xor_sync(0xffffffffu, a[v], j);
+                    const bool up = (((v << 5) | lane) & size) == 0;
+                    const bool lower = (lane & j) == 0;
+                    a[v] = (up == lower) ? min(a[v], other) : max(a[v], other);
+                }
+            }
+        }
+    }
+}
+
+template <int V>
+__device__ __forceinline__ void warp_sort_segment(int *__restrict__ data, int b, int n, int lane)
+{
+    int a[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+        const int k = v * 32 + lane;
+        a[v] = k < n ? data[b + k] : 0x7fffffff;
+    }
+    warp_bitonic<V>(a, lane);
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+        const int k = v * 32 + lane;
+        if (k < n)
+            data[b + k] = a[v];
+    }
+}
+
+// In-edge lists: one warp sorts the segment of one atom into increasing edge
+// order (bitonic in registers up to 256 entries; a single lane's insertion
+// sort beyond), so that force sums run in a fixed order.
+__global__ void k_sort_in_edges(int nseg, const int *__restrict__ start, int *__restrict__ data)
+{
+    const long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int sgm = (int)(t >> 5);
+    const int lane = threadIdx.x & 31;
+    if (sgm >= nseg)
+        return;
+    const int b = start[sgm], n = start[sgm + 1] - b;
+    if (n <= 1)
+        return;
+    if (n <= 64)
+        warp_sort_segment<2>(data, b, n, lane);
+    else if (n <= 128)
+        warp_sort_segment<4>(data, b, n, lane);
+    else if (n <= 256)
+        warp_sort_segment<8>(data, b, n, lane);
+    else if (lane == 0)
+        for (int i = b + 1; i < b + n; ++i) {
+            const int v = data[i];
+            int j = i - 1;
+            while (j >= b && data[j] > v) {
+                data[j + 1] = data[j];
+                --j;
+            }
+            data[j + 1] = v;
+        }
+}
+
+// Cell-ordered copy of the wrapped positions: entry q holds the position of
+// cell_atoms[q], so that the candidates of one cell are read contiguously.
+__global__ void k_cell_positions(int natoms, const int *__restrict__ cell_atoms,
+                                 const double *__restrict__ wx, const double *__restrict__ wy,
+                                 const double *__restrict__ wz, double *__restrict__ xs,
+                                 double *__restrict__ ys, double *__restrict__ zs)
+{
+    const int q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= natoms)
+        return;
+    const int o = cell_atoms[q];
+    xs[q] = wx[o];
+    ys[q] = wy[o];
+    zs[q] = wz[o];
+}
+
+// Traverses the candidate set of centre i (one thread per centre): stencil
+// cells in (d0, d1, d2) order, atoms of a cell in increasing index, their
+// positions read from the cell-ordered copy.  FILL selects counting or
+// writing (neighbour, image code, displacement, centre).
 template <bool FILL>
 __global__ void k_neighbors(int natoms, const NbStruct *__restrict__ structs,
                             const int *__restrict__ struct_of, const double *__restrict__ wx,
                             const double *__restrict__ wy, const double *__restrict__ wz,
-                            const int *__restrict__ cell_of, const int *__restrict__ cell_start,
-                            const int *__restrict__ cell_atoms, int *__restrict__ counts,
-                            const int *__restrict__ offsets, int *__restrict__ nbr,
-                            int *__restrict__ shift_code, double *__restrict__ rx,
-                            double *__restrict__ ry, double *__restrict__ rz)
+                            const double *__restrict__ xs, const double *__restrict__ ys,
+                            const double *__restrict__ zs, const int *__restrict__ cell_of,
+                            const int *__restrict__ cell_start, const int *__restrict__ cell_atoms,
+                            int *__restrict__ counts, const int *__restrict__ offsets,
+                            int *__restrict__ nbr, int *__restrict__ shift_code,
+                            double *__restrict__ rx, double *__restrict__ ry,
+                            double *__restrict__ rz, int *__restrict__ center)
 {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= natoms)
@@ -183,7 +285,7 @@ __global__ void k_neighbors(int natoms, const NbStruct *__restrict__ structs,
                     const int o = cell_atoms[q];
                     if (zero && o == i)
                         continue;
-                    const double xo = wx[o], yo = wy[o], zo = wz[o];
+                    const double xo = xs[q], yo = ys[q], zo = zs[q];
                     double r0, r1, r2;
                     if (i <= o) {
                         const double px = zero ? xo : dadd(xo, t[0]);
@@ -208,6 +310,7 @@ __global__ void k_neighbors(int natoms, const NbStruct *__restrict__ structs,
                             rx[out] = r0;
                             ry[out] = r1;
                             rz[out] = r2;
+                            center[out] = i;
                             ++out;
                         } else {
                             ++count;
@@ -219,6 +322,15 @@ __global__ void k_neighbors(int natoms, const NbStruct *__restrict__ structs,
     }
     if (!FILL)
         counts[i] = count;
+}
+
+// lowest index of an atom whose species lies outside 0..K-1 (INT_MAX: none)
+__global__ void k_check_types(int natoms, const int *__restrict__ types, int K,
+                              int *__restrict__ bad)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < natoms && (types[i] < 0 || types[i] >= K))
+        atomicMin(bad, i);
 }
 
 __global__ void k_in_count(long nedges, const int *__restrict__ nbr, int *__restrict__ in_count)
@@ -301,16 +413,6 @@ __global__ void k_refresh_edges(long nedges, const NbStruct *__restrict__ struct
     }
 }
 
-// centre index of every edge (used by edge-parallel kernels)
-__global__ void k_edge_centers(int natoms, const int *__restrict__ offsets, int *__restrict__ center)
-{
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= natoms)
-        return;
-    for (int e = offsets[i]; e < offsets[i + 1]; ++e)
-        center[e] = i;
-}
-
 static inline int nblk(long n, int t) { return (int)((n + t - 1) / t); }
 
 cudaError_t exclusive_scan(const int *in, int *out, int n, DeviceArena &arena, cudaStream_t s)
@@ -352,10 +454,12 @@ cudaError_t build_neighbors(const NbBuildInput &in, DeviceArena &arena, NbResult
     int *cell_start = arena.get<int>("nb_cell_start", in.total_cells + 1);
     int *cell_cursor = arena.get<int>("nb_cell_cursor", in.total_cells + 1);
     int *cell_atoms = arena.get<int>("nb_cell_atoms", N);
+    double *xs = arena.get<double>("nb_xs", N), *ys = arena.get<double>("nb_ys", N),
+           *zs = arena.get<double>("nb_zs", N);
     int *counts = arena.get<int>("nb_counts", NC + 1);
     int *offsets = arena.get<int>("offsets", NC + 1);
     if (!struct_of || !wx || !wy || !wz || !cell_of || !cell_count || !cell_start ||
-        !cell_cursor || !cell_atoms || !counts || !offsets)
+        !cell_cursor || !cell_atoms || !xs || !ys || !zs || !counts || !offsets)
         return cudaErrorMemoryAllocation;
     res.wx = wx;
     res.wy = wy;
@@ -368,6 +472,12 @@ cudaError_t build_neighbors(const NbBuildInput &in, DeviceArena &arena, NbResult
         if (N == 0)
             return cudaSuccess;
     }
+    int *bad_type = arena.get<int>("nb_bad_type", 1);
+    if (!bad_type)
+        return cudaErrorMemoryAllocation;
+    CK(cudaMemsetAsync(bad_type, 0x7f, sizeof(int), s));   // 0x7f7f7f7f: above any index
+    if (in.types)
+        k_check_types<<<nblk(N, T), T, 0, s>>>(N, in.types, in.K, bad_type);
     CK(cudaMemsetAsync(cell_count, 0, sizeof(int) * (in.total_cells + 1), s));
     CK(cudaMemsetAsync(cell_cursor, 0, sizeof(int) * (in.total_cells + 1), s));
     k_struct_ids<<<nblk(N, T), T, 0, s>>>(in.nstruct, in.atom_offsets, N, struct_of);
@@ -378,33 +488,33 @@ cudaError_t build_neighbors(const NbBuildInput &in, DeviceArena &arena, NbResult
     k_fill_cells<<<nblk(N, T), T, 0, s>>>(N, cell_of, cell_start, cell_cursor, cell_atoms);
     k_sort_segments<<<nblk(in.total_cells, T), T, 0, s>>>(in.total_cells, cell_start,
                                                           cell_atoms);
+    k_cell_positions<<<nblk(N, T), T, 0, s>>>(N, cell_atoms, wx, wy, wz, xs, ys, zs);
+    CK(cudaGetLastError());
     if (NC > 0)
         k_neighbors<false><<<nblk(NC, 128), 128, 0, s>>>(
-            NC, in.structs, struct_of, wx, wy, wz, cell_of, cell_start, cell_atoms, counts,
-            nullptr, nullptr, nullptr, nullptr, nullptr, nullptr);
+            NC, in.structs, struct_of, wx, wy, wz, xs, ys, zs, cell_of, cell_start, cell_atoms,
+            counts, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr);
     CK(cudaGetLastError());
     CK(exclusive_scan(counts, offsets, NC, arena, s));
-    int E = 0;
+    int E = 0, bad = 0;
     CK(cudaMemcpyAsync(&E, offsets + NC, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(&bad, bad_type, sizeof(int), cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
     res.nedges = E;
+    res.bad_type = bad < N ? bad : -1;
     int *nbr = arena.get<int>("nbr", (size_t)E + 1);
     int *shift = arena.get<int>("shift", (size_t)E + 1);
     double *rx = arena.get<double>("rx", (size_t)E + 1);
     double *ry = arena.get<double>("ry", (size_t)E + 1);
     double *rz = arena.get<double>("rz", (size_t)E + 1);
-    if (!nbr || !shift || !rx || !ry || !rz)
-        return cudaErrorMemoryAllocation;
-    if (NC > 0)
-        k_neighbors<true><<<nblk(NC, 128), 128, 0, s>>>(NC, in.structs, struct_of, wx, wy, wz,
-                                                        cell_of, cell_start, cell_atoms, nullptr,
-                                                        offsets, nbr, shift, rx, ry, rz);
-    CK(cudaGetLastError());
     int *center = arena.get<int>("edge_center", (size_t)E + 1);
-    if (!center)
+    if (!nbr || !shift || !rx || !ry || !rz || !center)
         return cudaErrorMemoryAllocation;
     if (NC > 0)
-        k_edge_centers<<<nblk(NC, 128), 128, 0, s>>>(NC, offsets, center);
+        k_neighbors<true><<<nblk(NC, 128), 128, 0, s>>>(
+            NC, in.structs, struct_of, wx, wy, wz, xs, ys, zs, cell_of, cell_start, cell_atoms,
+            nullptr, offsets, nbr, shift, rx, ry, rz, center);
+    CK(cudaGetLastError());
     res.center = center;
     res.nbr = nbr;
     res.shift = shift;
@@ -436,7 +546,8 @@ cudaError_t build_in_edges(int ntotal, long E, const int *nbr, DeviceArena &aren
         return err;
     if (E > 0)
         k_in_fill<<<nblk(E, 256), 256, 0, s>>>(E, nbr, in_offsets, cursor, in_edges);
-    k_sort_segments<<<nblk(ntotal, 128), 128, 0, s>>>(ntotal, in_offsets, in_edges);
+    if (ntotal > 0)
+        k_sort_in_edges<<<nblk((long)ntotal * 32, 128), 128, 0, s>>>(ntotal, in_offsets, in_edges);
     res.in_offsets = in_offsets;
     res.in_edges = in_edges;
     return cudaGetLastError();

@@ -80,10 +80,13 @@ struct NbBuildInput {
     const int *atom_offsets = nullptr;  // device [nstruct+1]
     const NbStruct *structs = nullptr;  // device [nstruct]
     const double *positions = nullptr;  // device [natoms*3]
+    const int *types = nullptr;         // device [natoms]; checked against 0..K-1 when set
+    int K = 0;
 };
 
 struct NbResult {
     long nedges = 0;
+    int bad_type = -1;   // first atom whose species is outside 0..K-1, or -1
     const double *wx = nullptr, *wy = nullptr, *wz = nullptr;
     const int *offsets = nullptr;
     const int *nbr = nullptr;

@@ -10,7 +10,13 @@
  *
  * Array pointers carry host memory unless a call takes a `memory` argument
  * equal to MTPB_MEMORY_DEVICE, in which case every array of that call is
- * device memory on the context's device.
+ * device memory on the context's device.  Host-memory calls have finished
+ * with every array when they return.  Device-memory calls are ordered on the
+ * context's stream (mtpb_set_stream): their device arrays are read and
+ * written by work queued on that stream and must stay valid until it has
+ * run; the per-structure tables of mtpb_build_neighbors (atom_offsets, cells,
+ * pbc) are read back to the host at the start of the call and must already
+ * hold their values.
  *
  * Each declaration names the reference interface it replaces (paths relative
  * to the reference project root).
