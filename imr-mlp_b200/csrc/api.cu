@@ -90,7 +90,9 @@ static int dag_configure(mtpb_context *c)
              "device attribute");
     CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->device),
              "device attribute");
-    const size_t limit = (size_t)optin - 8 * 1024;   // static shared arrays of the kernels
+    // static shared arrays of the graph kernels: at most 64 x 16 energy
+    // partials (8 KB), the mbarriers and the phase table
+    const size_t limit = (size_t)optin - 10 * 1024;
     auto fits = [&](int atoms) {
         return dag_ring_bytes(atoms) + (size_t)p.nrows * atoms * sizeof(double) <= limit;
     };

@@ -41,7 +41,6 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long *bar, unsigned 
     return ok != 0;
 }
 
-constexpr int DAG_MAX_PHASES = 64;
 constexpr long DAG_WAIT_LIMIT = 1L << 22;   // bounded wait: sets the error flag
 
 // Geometry: ATOMS atoms per block, two atoms per lane; a record stream is

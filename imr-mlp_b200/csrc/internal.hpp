@@ -64,6 +64,7 @@ inline DagRec make_rec(int s1, int s2, int out, unsigned flags, double c)
 constexpr int DAG_STREAMS = 32;
 constexpr int DAG_STREAMS_LARGE = 64;
 constexpr int DAG_STREAMS_MAX = 64;
+constexpr int DAG_MAX_PHASES = 64;   // phase table size of the graph kernels
 // record rows per ring slot (the ring stays 32 KB for both stream counts)
 constexpr int dag_chunk_rows(int streams) { return streams > 32 ? 16 : 32; }
 

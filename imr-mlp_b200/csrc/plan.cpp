@@ -136,9 +136,9 @@ struct Item {
     int energy = -1;   // energy_moments index of the item's ENERGY record
 };
 
-// Longest-processing-time assignment of items to DAG_STREAMS streams, then
+// Longest-processing-time assignment of items to the plan's streams, then
 // padding to equal length.  Appends the phase to plan.recs.
-void emit_phase(std::vector<Item> &items, DagPlan &plan)
+void emit_packed(const std::vector<Item> &items, DagPlan &plan)
 {
     std::vector<int> order(items.size());
     std::iota(order.begin(), order.end(), 0);
@@ -168,6 +168,72 @@ void emit_phase(std::vector<Item> &items, DagPlan &plan)
     plan.phase_rows.push_back((int)len);
 }
 
+// Emits one phase of independent items.  An item much longer than the even
+// share ceil(records / streams) would set the phase length alone, so it is
+// split into parts of about that share, each summed into a partial row, and a
+// following combine phase adds the partial rows (times the constant one row,
+// as operand two so that the dual graph keeps it (1, 0)) and ends with the
+// item's original flags.  Partial rows come from `pool` and are reused by later
+// phases.  Returns the number of phases emitted (1 or 2).
+int emit_phase(std::vector<Item> &items, DagPlan &plan, std::vector<int> &pool)
+{
+    size_t total = 0, longest = 0;
+    for (const Item &it : items) {
+        total += it.recs.size();
+        longest = std::max(longest, it.recs.size());
+    }
+    const size_t S = (size_t)plan.streams;
+    const size_t share = std::max<size_t>(4, (total + S - 1) / S);
+    // splitting saves about len - share rows of this phase and costs the
+    // combine phase (one row per part) plus a barrier
+    auto split = [&](size_t len) { return len > share + (len + share - 1) / share + 1; };
+    if (!split(longest)) {
+        emit_packed(items, plan);
+        return 1;
+    }
+    std::vector<Item> parts, combine;
+    size_t used = 0;
+    for (Item &it : items) {
+        if (!split(it.recs.size())) {
+            parts.push_back(std::move(it));
+            continue;
+        }
+        // the item's closing record keeps its flags in the combine item; a
+        // pure flag record (zero x zero, e.g. the energy term) moves there
+        DagRec last = it.recs.back();
+        std::vector<DagRec> body(it.recs.begin(), it.recs.end() - 1);
+        const bool flag_only = last.s12 == ((unsigned)plan.zero_row | ((unsigned)plan.zero_row << 16));
+        if (!flag_only) {
+            DagRec plain = last;
+            plain.outf = 0;
+            body.push_back(plain);
+        }
+        const size_t k = (body.size() + share - 1) / share;
+        const size_t per = (body.size() + k - 1) / k;
+        Item comb;
+        comb.energy = it.energy;
+        for (size_t j = 0; j * per < body.size(); ++j) {
+            if (used == pool.size())
+                pool.push_back(plan.nrows++);
+            const int prow = pool[used++];
+            Item part;
+            const size_t e = std::min(body.size(), (j + 1) * per);
+            part.recs.assign(body.begin() + j * per, body.begin() + e);
+            part.recs.back().outf = (unsigned)prow | ((unsigned)DAG_END << 16);
+            parts.push_back(std::move(part));
+            comb.recs.push_back(make_rec(prow, plan.one_row, 0, 0, 1.0));
+        }
+        if (flag_only)
+            comb.recs.push_back(last);
+        else
+            comb.recs.back().outf = last.outf;
+        combine.push_back(std::move(comb));
+    }
+    emit_packed(parts, plan);
+    emit_packed(combine, plan);
+    return 2;
+}
+
 } // namespace
 
 // Builds the record program executed by k_dag (efs.cu).  Forward phases follow
@@ -177,8 +243,9 @@ void emit_phase(std::vector<Item> &items, DagPlan &plan)
 // rule operand, by decreasing level, as a sum over its uses (the gather form
 // of backpropagate_moments, :3292-3305), and finally the adjoints of the basic
 // moments, written to the kernel slots.
-bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_of_basic,
-                    DagPlan &plan, std::string *err)
+static bool build_dag_plan_streams(const ModelHost &m, int shape,
+                                   const std::vector<int> &slot_of_basic, int streams,
+                                   DagPlan &plan, std::string *err)
 {
     const int nb = m.nb(), M = m.M, T = m.T();
     const int nslot = shape_desc(shape).nslot;
@@ -222,10 +289,7 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
     plan.scratch_row = next++;
     plan.nrows = next;
     plan.energy_moments = energy_moments;
-    // graphs beyond shared memory at 8 atoms per block run from L2 with 64
-    // streams (twice the warps); the others keep 32 (less padding)
-    plan.streams = (size_t)plan.nrows * 8 * sizeof(double) > 200 * 1024 ? DAG_STREAMS_LARGE
-                                                                          : DAG_STREAMS;
+    plan.streams = streams;
     if (plan.nrows >= 65535) {   // the dual graph adds one row
         if (err)
             *err = "moment graph too large for 16-bit row indices (" +
@@ -239,6 +303,8 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
 
     // ---- forward phases ----------------------------------------------------
     const int nfwd = std::max(1, maxlevel);
+    std::vector<int> pool;   // partial rows of split items
+    int nfwd_phases = 0;
     for (int L = 1; L <= nfwd; ++L) {
         std::vector<Item> items;
         if (L == 1) {   // scalar basic moments contribute directly
@@ -275,9 +341,9 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
                 it.recs.back().outf = (unsigned)out | ((unsigned)DAG_END << 16);
             items.push_back(std::move(it));
         }
-        emit_phase(items, plan);
+        nfwd_phases += emit_phase(items, plan, pool);
     }
-    plan.n_fwd = nfwd;
+    plan.n_fwd = nfwd_phases;
 
     // ---- reverse phases ----------------------------------------------------
     // uses of each operand: (target, other operand, coefficient)
@@ -313,8 +379,7 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
         for (int x = nb; x < M; ++x)
             if (adjrow[x] >= 0 && level[x] == L)
                 items.push_back(make_item(x, adjrow[x], 0));
-        emit_phase(items, plan);
-        ++nrev;
+        nrev += emit_phase(items, plan, pool);
     }
     {
         std::vector<Item> items;
@@ -330,10 +395,32 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
                                            DAG_END | DAG_GLOBAL, 0.0));
                 items.push_back(std::move(it));
             }
-        emit_phase(items, plan);
-        ++nrev;
+        nrev += emit_phase(items, plan, pool);
     }
     plan.n_rev = nrev;
+    if (plan.nrows >= 65535 || (int)plan.phase_rows.size() > DAG_MAX_PHASES) {
+        if (err)
+            *err = "moment graph too large (" + std::to_string(plan.nrows) + " rows, " +
+                   std::to_string(plan.phase_rows.size()) + " phases)";
+        return false;
+    }
+    return true;
+}
+
+// The record program on 32 and on 64 streams; 64 streams (16 warps per block)
+// run a padded record slot about 10% faster (level-20 graph: 14.6 ms for 15.1k
+// slots against 15.7 ms for 14.6k on 32), so they are kept unless their padding
+// costs more than that.
+bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_of_basic,
+                    DagPlan &plan, std::string *err)
+{
+    DagPlan p32, p64;
+    if (!build_dag_plan_streams(m, shape, slot_of_basic, DAG_STREAMS, p32, err))
+        return false;
+    if (!build_dag_plan_streams(m, shape, slot_of_basic, DAG_STREAMS_LARGE, p64, err))
+        return false;
+    plan = 0.9 * (double)p64.recs.size() < (double)p32.recs.size() ? std::move(p64)
+                                                                     : std::move(p32);
     return true;
 }
 
