@@ -173,3 +173,14 @@ def test_gradient_central_differences(model_l16):
             fd = (lp - lm) / (2 * h)
             an = float(g @ v)
             assert abs(fd - an) <= 3e-5 + 3e-6 * abs(an), (lo, fd, an)
+
+
+def test_level24_gradient_matches_oracle(oracle):
+    """The config-4 workload's path: the generated level-24 graph (beyond
+    shared memory: L2-resident dual-graph rows, 64 streams, split items), the
+    two-pass edge kernel and the three-part launches, on three config-4
+    structures, against the restated trainer."""
+    m = configs.level24_model()
+    sts = configs.config4_structures(3, seed=64)
+    te, tf, ts = _labels(sts, 8)
+    _close(_gpu_grad(m, sts, te, tf, ts), _oracle_grad(oracle, m, sts, te, tf, ts))
