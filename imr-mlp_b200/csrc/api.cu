@@ -814,14 +814,17 @@ int mtpb_efs_structures(mtpb_context *c, const mtpb_structures *in, int memory,
                      "upload positions");
             x = p;
         }
+        double *unwrapped = c->arena.get<double>("refresh_unwrapped", 4 * (size_t)N + 4);
+        if (!unwrapped)
+            return fail(MTPB_ERR_MEMORY, "device allocation failed");
         CUDA_TRY(cudaEventRecord(c->ev[0], c->stream), "event");
-        CUDA_TRY(refresh_edges(N, c->d_ns, c->nb.struct_of, c->nb, c->d_x_build, x,
+        CUDA_TRY(refresh_edges(N, c->d_ns, c->nb.struct_of, c->nb, c->d_x_build, x, unwrapped,
                                const_cast<double *>(c->nb.rx), const_cast<double *>(c->nb.ry),
                                const_cast<double *>(c->nb.rz), c->stream),
                  "refresh edge vectors");
         c->edge_epoch++;
         c->nb_built_this_call = true;   // ev[0] marks the refresh
-        c->pending_launches = 1;
+        c->pending_launches = c->nedges ? 2 : 0;
     }
     return mtpb_efs_compute(c, memory, out);
 }

@@ -373,13 +373,28 @@ __global__ void k_edge_vectors(int ncenter, const int *__restrict__ offsets,
 // last build (MD steps between rebuilds, MTPGpuComputeRequest::reuse_topology):
 // w' = w_build + (x - x_build) keeps atoms unwrapped relative to the build, and
 // r follows the build's i <= o rule so that unchanged positions reproduce the
-// build's displacements bit for bit.
+// build's displacements bit for bit.  w' is formed once per atom (k_unwrapped,
+// [atom][4] so that an edge gathers one 32-byte sector per atom).
+__global__ void k_unwrapped(int natoms, const double *__restrict__ wx,
+                            const double *__restrict__ wy, const double *__restrict__ wz,
+                            const double *__restrict__ x_build, const double *__restrict__ x,
+                            double *__restrict__ p)
+{
+    const int a = blockIdx.x * blockDim.x + threadIdx.x;
+    if (a >= natoms)
+        return;
+    const double v0 = dadd(wx[a], __dsub_rn(x[3 * a], x_build[3 * a]));
+    const double v1 = dadd(wy[a], __dsub_rn(x[3 * a + 1], x_build[3 * a + 1]));
+    const double v2 = dadd(wz[a], __dsub_rn(x[3 * a + 2], x_build[3 * a + 2]));
+    double2 *q = reinterpret_cast<double2 *>(p + 4 * (size_t)a);
+    q[0] = make_double2(v0, v1);
+    q[1] = make_double2(v2, 0.0);
+}
+
 __global__ void k_refresh_edges(long nedges, const NbStruct *__restrict__ structs,
                                 const int *__restrict__ struct_of, const int *__restrict__ center,
                                 const int *__restrict__ nbr, const int *__restrict__ shift,
-                                const double *__restrict__ wx, const double *__restrict__ wy,
-                                const double *__restrict__ wz, const double *__restrict__ x_build,
-                                const double *__restrict__ x, double *__restrict__ rx,
+                                const double *__restrict__ p, double *__restrict__ rx,
                                 double *__restrict__ ry, double *__restrict__ rz)
 {
     const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -387,21 +402,17 @@ __global__ void k_refresh_edges(long nedges, const NbStruct *__restrict__ struct
         return;
     const int i = center[e];
     const int o = nbr[e];
-    const NbStruct &st = structs[struct_of[i]];
-    auto wpos = [&](int a, double p[3]) {
-        p[0] = dadd(wx[a], __dsub_rn(x[3 * a], x_build[3 * a]));
-        p[1] = dadd(wy[a], __dsub_rn(x[3 * a + 1], x_build[3 * a + 1]));
-        p[2] = dadd(wz[a], __dsub_rn(x[3 * a + 2], x_build[3 * a + 2]));
-    };
-    double pi[3], po[3];
-    wpos(i, pi);
-    wpos(o, po);
+    const double2 *P = reinterpret_cast<const double2 *>(p);
+    const double2 i01 = P[2 * (size_t)i], i2 = P[2 * (size_t)i + 1];
+    const double2 o01 = P[2 * (size_t)o], o2 = P[2 * (size_t)o + 1];
+    const double pi[3] = {i01.x, i01.y, i2.x}, po[3] = {o01.x, o01.y, o2.x};
     const int code = shift[e];
     const int s0 = (code & 0xff) - 128, s1 = ((code >> 8) & 0xff) - 128,
               s2 = ((code >> 16) & 0xff) - 128;
     const bool zero = (s0 == 0 && s1 == 0 && s2 == 0);
-    double t[3];
-    image_translation(st, s0, s1, s2, t);
+    double t[3] = {0.0, 0.0, 0.0};
+    if (!zero)
+        image_translation(structs[struct_of[i]], s0, s1, s2, t);
     if (i <= o) {
         rx[e] = __dsub_rn(zero ? po[0] : dadd(po[0], t[0]), pi[0]);
         ry[e] = __dsub_rn(zero ? po[1] : dadd(po[1], t[1]), pi[1]);
@@ -554,14 +565,16 @@ cudaError_t build_in_edges(int ntotal, long E, const int *nbr, DeviceArena &aren
 }
 
 cudaError_t refresh_edges(int natoms, const NbStruct *structs, const int *struct_of,
-                          const NbResult &nb, const double *x_build, const double *x, double *rx,
-                          double *ry, double *rz, cudaStream_t s)
+                          const NbResult &nb, const double *x_build, const double *x,
+                          double *unwrapped, double *rx, double *ry, double *rz, cudaStream_t s)
 {
     if (nb.nedges == 0)
         return cudaSuccess;
+    k_unwrapped<<<nblk(natoms, 256), 256, 0, s>>>(natoms, nb.wx, nb.wy, nb.wz, x_build, x,
+                                                  unwrapped);
     k_refresh_edges<<<nblk(nb.nedges, 256), 256, 0, s>>>(nb.nedges, structs, struct_of,
-                                                         nb.center, nb.nbr, nb.shift, nb.wx,
-                                                         nb.wy, nb.wz, x_build, x, rx, ry, rz);
+                                                         nb.center, nb.nbr, nb.shift, unwrapped,
+                                                         rx, ry, rz);
     return cudaGetLastError();
 }
 

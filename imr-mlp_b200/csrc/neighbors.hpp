@@ -103,9 +103,11 @@ cudaError_t build_neighbors(const NbBuildInput &in, DeviceArena &arena, NbResult
                             cudaStream_t s);
 cudaError_t build_in_edges(int ntotal, long nedges, const int *nbr, DeviceArena &arena,
                            NbResult &res, cudaStream_t s);
+// unwrapped: scratch of 4 * natoms doubles (per-atom positions relative to the
+// build's images)
 cudaError_t refresh_edges(int natoms, const NbStruct *structs, const int *struct_of,
-                          const NbResult &nb, const double *x_build, const double *x, double *rx,
-                          double *ry, double *rz, cudaStream_t s);
+                          const NbResult &nb, const double *x_build, const double *x,
+                          double *unwrapped, double *rx, double *ry, double *rz, cudaStream_t s);
 cudaError_t edge_vectors(int ncenter, const int *offsets, const int *nbr, const double *x,
                          double *rx, double *ry, double *rz, cudaStream_t s);
 cudaError_t edge_pairs(long nedges, const int *center, const int *nbr, const int *types, int K,
