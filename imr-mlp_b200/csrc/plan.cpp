@@ -324,11 +324,23 @@ static bool build_dag_plan_streams(const ModelHost &m, int shape,
             if (!is_operand[x] && !is_scalar[x])
                 continue;   // contributes nothing
             Item it;
+            // rules of x with the same operand pair are one record with the
+            // summed coefficient (first occurrence keeps its place)
             const auto &rl = rules_of[x];
+            std::vector<std::pair<long, double>> terms;
             for (size_t k = 0; k < rl.size(); ++k) {
                 const int *r = &m.times[4 * rl[k]];
-                it.recs.push_back(make_rec(row[r[0]], row[r[1]], 0, 0, (double)r[2]));
+                const long key = (long)std::min(r[0], r[1]) * M + std::max(r[0], r[1]);
+                auto hit = std::find_if(terms.begin(), terms.end(),
+                                        [&](const auto &t) { return t.first == key; });
+                if (hit == terms.end())
+                    terms.push_back({key, (double)r[2]});
+                else
+                    hit->second += (double)r[2];
             }
+            for (const auto &t : terms)
+                it.recs.push_back(make_rec(row[(int)(t.first / M)], row[(int)(t.first % M)], 0, 0,
+                                           t.second));
             // the item ends with its energy term (scalars) and the store of
             // the product moment (operands; otherwise a scratch row)
             const int out = is_operand[x] ? row[x] : plan.scratch_row;
@@ -351,11 +363,22 @@ static bool build_dag_plan_streams(const ModelHost &m, int shape,
         int target, other;
         double c;
     };
+    // Uses with the same (target, other operand) are one term with the summed
+    // coefficient: the two adjoint terms c adj_t m_a of a square m_a m_a, and
+    // repeated rules of one target and pair.
     std::vector<std::vector<Use>> uses(M);
+    auto add_use = [&](int x, int target, int other, double c) {
+        for (Use &u : uses[x])
+            if (u.target == target && u.other == other) {
+                u.c += c;
+                return;
+            }
+        uses[x].push_back({target, other, c});
+    };
     for (int t = 0; t < T; ++t) {
         const int *r = &m.times[4 * t];
-        uses[r[0]].push_back({r[3], r[1], (double)r[2]});
-        uses[r[1]].push_back({r[3], r[0], (double)r[2]});
+        add_use(r[0], r[3], r[1], (double)r[2]);
+        add_use(r[1], r[3], r[0], (double)r[2]);
     }
     auto make_item = [&](int x, int out, unsigned flags) {
         Item it;
