@@ -75,6 +75,24 @@ static bool copy_model(const mtpb_model_view *v, ModelHost &m, std::string *err)
     m.radial.assign(v->radial_coeffs, v->radial_coeffs + m.K * m.K * m.mu * m.R);
     m.species.assign(v->species_coeffs, v->species_coeffs + m.K);
     m.moment.assign(v->moment_coeffs, v->moment_coeffs + v->alpha_scalar_moments);
+    m.family.clear();
+    if (v->radial_family) {
+        const int nf = m.split ? m.K * m.K : 1;
+        for (int p = 0; p < nf; ++p) {
+            const mtpb_radial_family &f = v->radial_family[p];
+            RadialFamily h;
+            h.type = f.type;
+            h.cutoff = f.cutoff_type;
+            h.shift = f.shift_type;
+            h.flipped = f.one_minus_chebyshev ? 1 : 0;
+            h.b = f.b;
+            h.r1 = f.r1;
+            h.r2 = f.r2;
+            h.lambda = f.lambda;
+            h.scale_lambda = f.scale_lambda;
+            m.family.push_back(h);
+        }
+    }
     return true;
 }
 
@@ -126,7 +144,31 @@ static int upload_model(mtpb_context *c)
     std::vector<PairParams> pp(KK);
     for (int p = 0; p < KK; ++p) {
         const double rmin = m.pair_min(p), rmax = m.pair_max(p);
-        pp[p] = {rmax + rmin, rmax - rmin, 2.0 / (rmax - rmin), rmax};
+        const RadialFamily f = m.pair_family(p);
+        PairParams &q = pp[p];
+        q = PairParams{};
+        // the constants the reference bases compute once (basis.cpp setup(),
+        // cutoff.cpp / xtrans.cpp constructors)
+        q.pu = rmax + rmin;
+        q.su = rmax - rmin;
+        q.mult = 2.0 / (rmax - rmin);
+        q.rmax = rmax;
+        q.rmin = rmin;
+        q.inv_range = 1.0 / (rmax - rmin);
+        q.irpi = M_PI / rmax;
+        q.cfreq = M_PI / (rmax - rmin);
+        q.slope = 2.0 / (rmax - rmin);
+        q.b = f.b;
+        q.r1 = f.r1;
+        q.r2 = f.r2;
+        q.lambda = f.lambda;
+        q.scale_lambda = f.scale_lambda;
+        q.den = f.lambda != 0.0 ? std::expm1(f.lambda) : 0.0;
+        q.sden = f.scale_lambda != 0.0 ? std::tanh(f.scale_lambda) : 0.0;
+        q.type = f.type;
+        q.cutoff = f.cutoff;
+        q.shift = f.shift;
+        q.flipped = f.flipped;
     }
     c->d_radial = c->arena.get<double>("model_radial", m.radial.size());
     c->d_species = c->arena.get<double>("model_species", m.K);

@@ -18,6 +18,7 @@
 // each polynomial evaluated along x-chains with Horner's rule.  This replaces
 // the reference's per-edge Jacobian (nb x n_e x 3 doubles per site) by
 // registers.
+#include "radial.cuh"
 #include "internal.hpp"
 #include "moments.cuh"
 #include "dag.cuh"
@@ -39,7 +40,7 @@ template <class S, bool REV> constexpr int smem_doubles(int K, int R)
     int n = stage_rows<S, REV>() * KS * STR;
     if (REV)
         n += NW * 3 * KS * 32;
-    n += 4 * K * K;             // pair parameters
+    n += PAIR_PARAM_DOUBLES * K * K;   // pair parameters
     n += K * K * S::NMU * R;    // radial coefficients of the used channels
     return n;
 }
@@ -105,40 +106,16 @@ __device__ __forceinline__ void stage_chunk(const EdgeArgs &p, const StageView &
                     xh = x * rinv;
                     yh = y * rinv;
                     zh = z * rinv;
-                    // Chebyshev recurrence (basis.cpp:148-164) folded into
-                    // the channel sums f_mu = sum_xi c[pair,mu,xi] Q_xi(r)
-                    const double ksi = (2.0 * r - pp.pu) / pp.su;
-                    const double ru = r - pp.rmax;
-                    const double s = p.scaling;
+                    // radial basis of the pair's family (radial.cuh) folded
+                    // into the channel sums f_mu = sum_xi c[pair,mu,xi] Q_xi(r)
                     const double *c = v.radial + pair * NMU * p.R;
-                    double q0 = s * (ru * ru), d0 = s * (2.0 * ru);
-#pragma unroll
-                    for (int m = 0; m < NMU; ++m) {
-                        f[m] = c[m * p.R] * q0;
-                        fp[m] = c[m * p.R] * d0;
-                    }
-                    if (p.R > 1) {
-                        double q1 = s * (ksi * ru * ru);
-                        double d1 = s * (pp.mult * ru * ru + 2.0 * ksi * ru);
+                    radial_basis(pp, p.scaling, p.R, r, [&](int xi, double q, double d) {
 #pragma unroll
                         for (int m = 0; m < NMU; ++m) {
-                            f[m] = fma(c[m * p.R + 1], q1, f[m]);
-                            fp[m] = fma(c[m * p.R + 1], d1, fp[m]);
+                            f[m] = fma(c[m * p.R + xi], q, f[m]);
+                            fp[m] = fma(c[m * p.R + xi], d, fp[m]);
                         }
-                        for (int xi = 2; xi < p.R; ++xi) {
-                            const double q2 = 2.0 * ksi * q1 - q0;
-                            const double d2 = 2.0 * (pp.mult * q1 + ksi * d1) - d0;
-#pragma unroll
-                            for (int m = 0; m < NMU; ++m) {
-                                f[m] = fma(c[m * p.R + xi], q2, f[m]);
-                                fp[m] = fma(c[m * p.R + xi], d2, fp[m]);
-                            }
-                            q0 = q1;
-                            q1 = q2;
-                            d0 = d1;
-                            d1 = d2;
-                        }
-                    }
+                    });
                 }
             }
         }
@@ -407,7 +384,7 @@ __global__ void __launch_bounds__(ShapeCfg<S>::NW * 32, KCfg<S, REV>::BLOCKS)
     if (REV)
         cur += NW * 3 * KS * 32;
     PairParams *pairs = reinterpret_cast<PairParams *>(cur);
-    cur += 4 * p.K * p.K;
+    cur += PAIR_PARAM_DOUBLES * p.K * p.K;
     double *radial = cur;
     const int KK = p.K * p.K;
     for (int i = threadIdx.x; i < KK; i += blockDim.x)

@@ -24,6 +24,7 @@
 //     basics k of channel mu -- the contraction of the reference's
 //     moment_jacobian_coeffs / _coord workspaces (:3424-3452, 3520-3535)
 //     without materialising them.
+#include "radial.cuh"
 #include "internal.hpp"
 #include "moments.cuh"
 #include "dag.cuh"
@@ -62,7 +63,7 @@ template <class S, bool TAN> constexpr size_t grad_smem_doubles(int K, int R)
     size_t n = (size_t)grad_stage_rows<S, TAN>() * KSG * STR;
     if (!TAN)
         n += (size_t)NW * 2 * S::NMU * KSG * 32;   // per-warp partial sums
-    n += 4 * K * K + (size_t)K * K * S::NMU * R;
+    n += PAIR_PARAM_DOUBLES * K * K + (size_t)K * K * S::NMU * R;
     return n;
 }
 
@@ -117,39 +118,20 @@ __device__ __forceinline__ void grad_stage(const EdgeArgs &p, const double *__re
                     for (int a = 0; a < 3; ++a)
                         hd[a] = (w[a] - h[a] * sw) * rinv;
                     if constexpr (TAN) {
-                        const double ksi = (2.0 * r - pp.pu) / pp.su;
-                        const double ru = r - pp.rmax;
-                        const double sc = p.scaling;
                         const double *c = v.radial + pair * NMU * p.R;
-                        double q0 = sc * (ru * ru), d0 = sc * (2.0 * ru);
                         double fp[NMU];
 #pragma unroll
                         for (int m = 0; m < NMU; ++m) {
-                            f[m] = c[m * p.R] * q0;
-                            fp[m] = c[m * p.R] * d0;
+                            f[m] = 0.0;
+                            fp[m] = 0.0;
                         }
-                        if (p.R > 1) {
-                            double q1 = sc * (ksi * ru * ru);
-                            double d1 = sc * (pp.mult * ru * ru + 2.0 * ksi * ru);
+                        radial_basis(pp, p.scaling, p.R, r, [&](int xi, double q, double d) {
 #pragma unroll
                             for (int m = 0; m < NMU; ++m) {
-                                f[m] = fma(c[m * p.R + 1], q1, f[m]);
-                                fp[m] = fma(c[m * p.R + 1], d1, fp[m]);
+                                f[m] = fma(c[m * p.R + xi], q, f[m]);
+                                fp[m] = fma(c[m * p.R + xi], d, fp[m]);
                             }
-                            for (int xi = 2; xi < p.R; ++xi) {
-                                const double q2 = 2.0 * ksi * q1 - q0;
-                                const double d2 = 2.0 * (pp.mult * q1 + ksi * d1) - d0;
-#pragma unroll
-                                for (int m = 0; m < NMU; ++m) {
-                                    f[m] = fma(c[m * p.R + xi], q2, f[m]);
-                                    fp[m] = fma(c[m * p.R + xi], d2, fp[m]);
-                                }
-                                q0 = q1;
-                                q1 = q2;
-                                d0 = d1;
-                                d1 = d2;
-                            }
-                        }
+                        });
 #pragma unroll
                         for (int m = 0; m < NMU; ++m)
                             fd[m] = fp[m] * sw;
@@ -436,7 +418,7 @@ __global__ void __launch_bounds__(GradCfg<S>::NW * 32, GradCfg<S>::BLOCKS)
     if (!TAN)
         cur += NW * 2 * NMU * KSG * 32;
     PairParams *pairs = reinterpret_cast<PairParams *>(cur);
-    cur += 4 * p.K * p.K;
+    cur += PAIR_PARAM_DOUBLES * p.K * p.K;
     double *radial = cur;
     const int KK = p.K * p.K;
     for (int i = threadIdx.x; i < KK; i += blockDim.x)

@@ -34,9 +34,32 @@ int shape_slot(int id, int mu, int a, int b, int c);
 // Radial parameters of one ordered species pair (RBasis_Chebyshev::setup,
 // basis/basis.cpp:119-126): pu = rmax + rmin, su = rmax - rmin,
 // mult = 2 / (rmax - rmin), rmax is also the pair cutoff.
+// Radial family of a pair (mtpb_radial_family of include/mtpb200.h).
+enum RadialType { RB_CHEBYSHEV = 0, RB_CHEBY_COS = 1, RB_CHEBY_POLY5 = 2, RB_CONFIGURABLE = 3,
+                  RB_CHEBY_POLY4 = 4 };
+enum RadialCutoffType { CUT_QUADRATIC = 0, CUT_COSINE = 1, CUT_POLY5 = 2,
+                        CUT_NORMALIZED_QUADRATIC = 3, CUT_COSINE_LEFT = 4,
+                        CUT_COSINE_UNSCALED = 5, CUT_COSINE_SQUARED = 6, CUT_SINE_SQUARED = 7,
+                        CUT_POLY3 = 8, CUT_POLY4 = 9, CUT_SMOOTHSTEP5 = 10, CUT_SMOOTHSTEP7 = 11 };
+enum RadialShiftType { SHIFT_LINEAR = 0, SHIFT_EXPONENTIAL = 1, SHIFT_EXPONENTIAL_LEFT = 2,
+                       SHIFT_I2 = 3, SHIFT_EXPONENTIAL_TANH = 4 };
+struct RadialFamily {
+    int type = RB_CHEBYSHEV, cutoff = CUT_QUADRATIC, shift = SHIFT_LINEAR, flipped = 0;
+    double b = 0.0, r1 = 0.0, r2 = 0.0, lambda = 0.0, scale_lambda = 0.0;
+};
+
+// Device parameters of a pair's radial basis (filled by upload_model, api.cu):
+// the Chebyshev coordinate ksi = (2r - pu) / su with dksi/dr = mult, the
+// interval, and the family's envelope / shift parameters with the constants the
+// reference computes once per basis (expm1(lambda), tanh(scale_lambda)).
 struct PairParams {
     double pu, su, mult, rmax;
+    double rmin, inv_range, irpi, b;
+    double r1, r2, lambda, scale_lambda;
+    double den, sden, slope, cfreq;   // cfreq: pi / (max - min) of the cosine cutoff
+    int type, cutoff, shift, flipped;
 };
+constexpr int PAIR_PARAM_DOUBLES = (int)(sizeof(PairParams) / sizeof(double));
 
 // Record of the moment-graph program (see k_dag in efs.cu): 16 bytes,
 // {s1 | s2 << 16, out | flags << 16, c (double)}.

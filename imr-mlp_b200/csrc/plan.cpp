@@ -33,6 +33,35 @@ bool validate_model(const ModelHost &m, std::string *err)
             return fail("invalid radial interval");
     if (!std::isfinite(m.scaling))
         return fail("scaling must be finite");
+    // radial families: the checks of the reference's loaders and constructors
+    // (runtime/mtp/radial_basis.h:46-200, basis/cutoff.cpp, basis/xtrans.cpp)
+    if (!m.family.empty() && (int)m.family.size() != pairs)
+        return fail("radial family count does not match the split flag");
+    for (int p = 0; p < (int)m.family.size(); ++p) {
+        const RadialFamily &f = m.family[p];
+        const double lo = m.min_dist[p], hi = m.max_dist[p];
+        if (f.type < RB_CHEBYSHEV || f.type > RB_CHEBY_POLY4)
+            return fail("unsupported radial basis type " + std::to_string(f.type) +
+                        " (RBChebyshev, RBChebyCos, RBChebyshevPoly4/5 and "
+                        "RBChebyshevConfigurable are implemented)");
+        if (!std::isfinite(f.b) || !std::isfinite(f.r1) || !std::isfinite(f.r2) ||
+            !std::isfinite(f.lambda) || !std::isfinite(f.scale_lambda))
+            return fail("non-finite radial parameter");
+        if (f.type != RB_CONFIGURABLE)
+            continue;
+        if (f.cutoff < CUT_QUADRATIC || f.cutoff > CUT_SMOOTHSTEP7 || f.shift < SHIFT_LINEAR ||
+            f.shift > SHIFT_EXPONENTIAL_TANH)
+            return fail("unknown configurable cutoff_type or shift_type");
+        if (f.cutoff == CUT_SMOOTHSTEP7 && !(lo < f.r1 && f.r1 <= f.r2 && f.r2 < hi))
+            return fail("smoothstep7 cutoff requires min_dist < cutoff_r1 <= cutoff_r2 < max_dist");
+        if ((f.shift == SHIFT_EXPONENTIAL || f.shift == SHIFT_EXPONENTIAL_LEFT ||
+             f.shift == SHIFT_EXPONENTIAL_TANH) &&
+            f.lambda != 0.0 && !(std::isfinite(std::expm1(f.lambda)) && std::expm1(f.lambda) != 0.0))
+            return fail("shift_lambda produces a non-finite exponential normalization");
+        if (f.shift == SHIFT_EXPONENTIAL_TANH && f.scale_lambda != 0.0 &&
+            std::tanh(f.scale_lambda) == 0.0)
+            return fail("shift_scale_lambda produces an invalid normalization");
+    }
     const int nb = m.nb(), M = m.M;
     if (nb <= 0 || nb > M)
         return fail("basic moment count exceeds total moment slots");

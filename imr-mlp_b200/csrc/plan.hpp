@@ -18,12 +18,17 @@ struct ModelHost {
     std::vector<int> times;    // [T*4]
     std::vector<int> mapping;  // [S]
     std::vector<double> radial, species, moment;
+    std::vector<RadialFamily> family;   // empty: RBChebyshev; else 1 or K*K (split)
     int nb() const { return (int)basic.size() / 4; }
     int T() const { return (int)times.size() / 4; }
     int S() const { return (int)mapping.size(); }
     int pairs() const { return K * K; }
     double pair_min(int p) const { return split ? min_dist[p] : min_dist[0]; }
     double pair_max(int p) const { return split ? max_dist[p] : max_dist[0]; }
+    RadialFamily pair_family(int p) const
+    {
+        return family.empty() ? RadialFamily{} : family[split && family.size() > 1 ? p : 0];
+    }
     double cutoff() const
     {
         double c = 0;

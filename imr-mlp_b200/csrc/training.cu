@@ -13,6 +13,7 @@
 //   -> dual graph -> per-edge channel records -> k_radial_grad over edges
 //   bucketed by species pair -> column sums -> k_assemble.
 // Every reduction runs in a fixed order, so results are reproducible.
+#include "radial.cuh"
 #include "context.hpp"
 
 #include <cub/cub.cuh>
@@ -242,27 +243,14 @@ __global__ void __launch_bounds__(RG_THREADS)
                 const double x = rx[e], y = ry[e], z = rz[e];
                 const double r = sqrt(__dadd_rn(__dadd_rn(__dmul_rn(x, x), __dmul_rn(y, y)),
                                                 __dmul_rn(z, z)));
-                const double ksi = (2.0 * r - pp.pu) / pp.su;
-                const double ru = r - pp.rmax;
-                double q0 = scaling * (ru * ru), d0 = scaling * (2.0 * ru);
-                Q[tid * R] = q0;
-                Qd[tid * R] = d0;
-                if (R > 1) {
-                    double q1 = scaling * (ksi * ru * ru);
-                    double d1 = scaling * (pp.mult * ru * ru + 2.0 * ksi * ru);
-                    Q[tid * R + 1] = q1;
-                    Qd[tid * R + 1] = d1;
-                    for (int xi = 2; xi < R; ++xi) {
-                        const double q2 = 2.0 * ksi * q1 - q0;
-                        const double d2 = 2.0 * (pp.mult * q1 + ksi * d1) - d0;
-                        Q[tid * R + xi] = q2;
-                        Qd[tid * R + xi] = d2;
-                        q0 = q1;
-                        q1 = q2;
-                        d0 = d1;
-                        d1 = d2;
-                    }
+                for (int xi = 0; xi < R; ++xi) {   // zero where the family vanishes
+                    Q[tid * R + xi] = 0.0;
+                    Qd[tid * R + xi] = 0.0;
                 }
+                radial_basis(pp, scaling, R, r, [&](int xi, double q, double d) {
+                    Q[tid * R + xi] = q;
+                    Qd[tid * R + xi] = d;
+                });
                 const double *u = uv + (size_t)e * 2 * nmu;
                 for (int m = 0; m < nmu; ++m) {
                     U[tid * nmu + m] = u[m];

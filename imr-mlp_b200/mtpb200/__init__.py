@@ -89,12 +89,14 @@ class _ModelKeep:
         self.radial = _f64(m.radial_coeffs)
         self.species = _f64(m.species_coeffs)
         self.moment = _f64(m.moment_coeffs)
+        self.families = _lib.radial_family_array(m)
         self.view = _lib.ModelView(
             m.species_count, m.radial_func_count, m.rb_size, int(m.radial_basis_split),
             _dp(self.mins), _dp(self.maxs), float(m.scaling), m.alpha_moments_count,
             m.alpha_index_basic_count, m.alpha_index_times_count, m.alpha_scalar_moments,
             _ip(self.basic), _ip(self.times), _ip(self.mapping), _dp(self.radial),
-            _dp(self.species), _dp(self.moment))
+            _dp(self.species), _dp(self.moment),
+            C.cast(self.families, C.POINTER(_lib.RadialFamilyView)) if self.families else None)
 
 
 class StructureBatch:

@@ -25,6 +25,13 @@ MEMORY_HOST = 0
 MEMORY_DEVICE = 1
 
 
+class RadialFamilyView(C.Structure):
+    _fields_ = [("type", C.c_int), ("cutoff_type", C.c_int), ("shift_type", C.c_int),
+                ("one_minus_chebyshev", C.c_int), ("b", C.c_double), ("r1", C.c_double),
+                ("r2", C.c_double), ("shift_lambda", C.c_double),
+                ("shift_scale_lambda", C.c_double)]
+
+
 class ModelView(C.Structure):
     _fields_ = [
         ("species_count", C.c_int), ("radial_func_count", C.c_int), ("rb_size", C.c_int),
@@ -34,7 +41,23 @@ class ModelView(C.Structure):
         ("alpha_scalar_moments", C.c_int), ("alpha_index_basic", _ip),
         ("alpha_index_times", _ip), ("alpha_moment_mapping", _ip), ("radial_coeffs", _dp),
         ("species_coeffs", _dp), ("moment_coeffs", _dp),
+        ("radial_family", C.POINTER(RadialFamilyView)),
     ]
+
+
+def radial_family_array(model):
+    """ctypes array of the model's radial families (None for RBChebyshev)."""
+    from .mtpfile import CUTOFF_TYPES, SHIFT_TYPES
+    fams = model.radial_family
+    if not fams:
+        return None
+    arr = (RadialFamilyView * len(fams))()
+    for i, f in enumerate(fams):
+        arr[i] = RadialFamilyView(f.type_id, CUTOFF_TYPES[f.cutoff_type],
+                                  SHIFT_TYPES[f.shift_type], int(f.one_minus_chebyshev),
+                                  float(f.b), float(f.r1), float(f.r2), float(f.shift_lambda),
+                                  float(f.shift_scale_lambda))
+    return arr
 
 
 class Structures(C.Structure):

@@ -8,16 +8,21 @@ The layout follows the reference reader ``PotMTP::Load``
   ``scaling`` (absent means 0.01 in ``PotMTP::Load`` but 1.0 in MLIPCore, so
   :func:`write_mtp` always writes it), ``species_count``, optional
   ``potential_tag``;
-* one ``RBChebyshev`` radial basis, or ``radial_basis_split = 1`` followed by
-  one ``pair i j`` block per ordered species pair;
+* one radial basis, or ``radial_basis_split = 1`` followed by one ``pair i j``
+  block per ordered species pair; a basis is ``RBChebyshev``, ``RBChebyCos``,
+  ``RBChebyshevPoly4`` / ``RBChebyshevPoly5`` (with ``rb_b``) or
+  ``RBChebyshevConfigurable`` (``basis_function_type``, ``cutoff_type`` with
+  ``cutoff_b`` / ``cutoff_r1``, ``cutoff_r2``, ``shift_type`` with
+  ``shift_lambda`` / ``shift_scale_lambda``), as read by the basis loaders of
+  basis/basis.cpp, basis/cutoff.cpp:450-460 and basis/xtrans.cpp:361-371;
 * ``radial_funcs_count`` and optional ``radial_coeffs`` as ``i-j`` blocks of
   ``radial_funcs_count`` rows of ``radial_basis_size`` values;
 * the moment graph: ``alpha_index_basic`` {mu, a, b, c}, ``alpha_index_times``
   {l1, l2, c, id}, ``alpha_moment_mapping``;
 * optional ``species_coeffs`` and ``moment_coeffs``.
 
-Only the Chebyshev radial family is accepted, which is what the B200 kernels
-implement; other families are rejected with a clear error.
+The polynomial families RBPolyB and RBPolyBCos are rejected with a clear
+error (the B200 kernels implement the Chebyshev families above).
 """
 from __future__ import annotations
 
@@ -27,7 +32,57 @@ from typing import List, Optional
 
 import numpy as np
 
-__all__ = ["MTPModel", "parse_mtp", "read_mtp", "write_mtp", "format_mtp"]
+__all__ = ["MTPModel", "RadialFamily", "parse_mtp", "read_mtp", "write_mtp", "format_mtp"]
+
+# numbering of mtpb_radial_type / mtpb_radial_cutoff / mtpb_radial_shift
+# (include/mtpb200.h; RadialBasis, RadialCutoff, RadialTransform of
+# runtime/mtp/gpu-direct/mtp_gpu_direct.h:152-186)
+RADIAL_TYPES = {"RBChebyshev": 0, "RBChebyCos": 1, "RBChebyshevPoly5": 2,
+                "RBChebyshevConfigurable": 3, "RBChebyshevPoly4": 4}
+CUTOFF_TYPES = {"quadratic": 0, "cosine": 1, "poly5": 2, "normalized_quadratic": 3,
+                "cosine_left": 4, "cosine_unscaled": 5, "cosine_squared": 6,
+                "sine_squared": 7, "poly3": 8, "poly4": 9, "smoothstep5": 10,
+                "smoothstep7": 11}
+SHIFT_TYPES = {"linear": 0, "exponential": 1, "exponential_left": 2, "i2": 3,
+               "exponential_tanh": 4}
+
+
+@dataclasses.dataclass
+class RadialFamily:
+    """One radial basis family with its parameters (mtpb_radial_family)."""
+    name: str = "RBChebyshev"
+    cutoff_type: str = "quadratic"         # configurable only
+    shift_type: str = "linear"             # configurable only
+    one_minus_chebyshev: bool = False      # configurable only
+    b: float = 0.0                         # rb_b (Poly4/Poly5) or cutoff_b
+    r1: float = 0.0                        # cutoff_r1 (smoothstep7)
+    r2: float = 0.0                        # cutoff_r2
+    shift_lambda: float = 0.0
+    shift_scale_lambda: float = 0.0
+
+    @property
+    def type_id(self) -> int:
+        return RADIAL_TYPES[self.name]
+
+    def lines(self) -> List[str]:
+        """The family-specific lines written after radial_basis_size."""
+        if self.name in ("RBChebyshevPoly4", "RBChebyshevPoly5"):
+            return [f"\trb_b = {_fmt(self.b)}"]
+        if self.name != "RBChebyshevConfigurable":
+            return []
+        out = ["\tbasis_function_type = " +
+               ("one_minus_chebyshev" if self.one_minus_chebyshev else "chebyshev"),
+               f"\tcutoff_type = {self.cutoff_type}"]
+        if self.cutoff_type in ("poly3", "poly4", "poly5"):
+            out.append(f"\tcutoff_b = {_fmt(self.b)}")
+        if self.cutoff_type == "smoothstep7":
+            out += [f"\tcutoff_r1 = {_fmt(self.r1)}", f"\tcutoff_r2 = {_fmt(self.r2)}"]
+        out.append(f"\tshift_type = {self.shift_type}")
+        if self.shift_type in ("exponential", "exponential_left", "exponential_tanh"):
+            out.append(f"\tshift_lambda = {_fmt(self.shift_lambda)}")
+        if self.shift_type == "exponential_tanh":
+            out.append(f"\tshift_scale_lambda = {_fmt(self.shift_scale_lambda)}")
+        return out
 
 
 @dataclasses.dataclass
@@ -47,6 +102,12 @@ class MTPModel:
     scaling: float = 0.01
     radial_basis_split: bool = False
     potential_name: str = "MTP1m"
+    radial_family: Optional[List[RadialFamily]] = None   # None: RBChebyshev; [1] or [K*K]
+
+    def family(self, pair: int) -> RadialFamily:
+        if not self.radial_family:
+            return RadialFamily()
+        return self.radial_family[pair if len(self.radial_family) > 1 else 0]
 
     @property
     def alpha_index_basic_count(self) -> int:
@@ -180,34 +241,67 @@ def parse_mtp(text: str) -> MTPModel:
 
     def read_basis():
         btype = tk.assignment("radial_basis_type")
-        if btype != "RBChebyshev":
-            raise ValueError(f"radial basis '{btype}' is not supported (RBChebyshev only)")
+        if btype not in RADIAL_TYPES:
+            raise ValueError(f"radial basis '{btype}' is not supported (implemented: "
+                             + ", ".join(RADIAL_TYPES) + ")")
         rmin = float(tk.assignment("min_dist"))
         rmax = float(tk.assignment("max_dist"))
         size = int(tk.assignment("radial_basis_size"))
         if size <= 0 or not rmax > rmin:
             raise ValueError("invalid radial basis interval or size")
-        return rmin, rmax, size
+        fam = RadialFamily(name=btype)
+        if btype in ("RBChebyshevPoly4", "RBChebyshevPoly5"):
+            fam.b = float(tk.assignment("rb_b"))
+        elif btype == "RBChebyshevConfigurable":
+            if tk.peek() == "basis_function_type":
+                kind = tk.assignment("basis_function_type")
+                if kind not in ("chebyshev", "one_minus_chebyshev"):
+                    raise ValueError(f"unknown basis_function_type '{kind}'")
+                fam.one_minus_chebyshev = kind == "one_minus_chebyshev"
+            fam.cutoff_type = tk.assignment("cutoff_type")
+            if fam.cutoff_type not in CUTOFF_TYPES:
+                raise ValueError(f"unknown cutoff_type '{fam.cutoff_type}'")
+            if fam.cutoff_type in ("poly3", "poly4", "poly5"):
+                fam.b = float(tk.assignment("cutoff_b"))
+            if fam.cutoff_type == "smoothstep7":
+                fam.r1 = float(tk.assignment("cutoff_r1"))
+                fam.r2 = float(tk.assignment("cutoff_r2"))
+                if not (rmin < fam.r1 <= fam.r2 < rmax):
+                    raise ValueError("smoothstep7 requires min_dist < cutoff_r1 <= cutoff_r2 "
+                                     "< max_dist")
+            fam.shift_type = tk.assignment("shift_type")
+            if fam.shift_type not in SHIFT_TYPES:
+                raise ValueError(f"unknown shift_type '{fam.shift_type}'")
+            if fam.shift_type in ("exponential", "exponential_left", "exponential_tanh"):
+                fam.shift_lambda = float(tk.assignment("shift_lambda"))
+            if fam.shift_type == "exponential_tanh":
+                fam.shift_scale_lambda = float(tk.assignment("shift_scale_lambda"))
+        return rmin, rmax, size, fam
 
     if split:
         mins = np.zeros(K * K)
         maxs = np.zeros(K * K)
         seen = set()
         R = None
+        families = [None] * (K * K)
         for _ in range(K * K):
             tk.expect("pair")
             ci, cj = int(tk.next()), int(tk.next())
             if not (0 <= ci < K and 0 <= cj < K) or (ci, cj) in seen:
                 raise ValueError("invalid or duplicate radial basis pair")
             seen.add((ci, cj))
-            rmin, rmax, size = read_basis()
+            rmin, rmax, size, fam = read_basis()
             if R is not None and size != R:
                 raise ValueError("split radial bases must share radial_basis_size")
             R = size
             mins[ci * K + cj], maxs[ci * K + cj] = rmin, rmax
+            families[ci * K + cj] = fam
     else:
-        rmin, rmax, R = read_basis()
+        rmin, rmax, R, fam = read_basis()
         mins, maxs = np.array([rmin]), np.array([rmax])
+        families = [fam]
+    if all(f.name == "RBChebyshev" for f in families):
+        families = None
     mu = int(tk.assignment("radial_funcs_count"))
     radial = np.zeros(K * K * mu * R)
     if tk.peek() == "radial_coeffs":
@@ -274,7 +368,8 @@ def parse_mtp(text: str) -> MTPModel:
                      max_dist=maxs, alpha_moments_count=M, alpha_index_basic=basic,
                      alpha_index_times=times, alpha_moment_mapping=mapping,
                      radial_coeffs=radial, species_coeffs=species, moment_coeffs=moment,
-                     scaling=scaling, radial_basis_split=split, potential_name=name)
+                     scaling=scaling, radial_basis_split=split, potential_name=name,
+                     radial_family=families)
     validate(model)
     return model
 
@@ -318,15 +413,17 @@ def format_mtp(m: MTPModel) -> str:
         out.append("radial_basis_split = 1")
         for i in range(K):
             for j in range(K):
-                out += [f"pair {i} {j}", "radial_basis_type = RBChebyshev",
+                fam = m.family(i * K + j)
+                out += [f"pair {i} {j}", f"radial_basis_type = {fam.name}",
                         f"\tmin_dist = {_fmt(m.min_dist[i * K + j])}",
                         f"\tmax_dist = {_fmt(m.max_dist[i * K + j])}",
-                        f"\tradial_basis_size = {R}"]
+                        f"\tradial_basis_size = {R}"] + fam.lines()
         out.append(f"\tradial_funcs_count = {mu}")
     else:
-        out += ["radial_basis_type = RBChebyshev", f"\tmin_dist = {_fmt(m.min_dist[0])}",
-                f"\tmax_dist = {_fmt(m.max_dist[0])}", f"\tradial_basis_size = {R}",
-                f"\tradial_funcs_count = {mu}"]
+        fam = m.family(0)
+        out += [f"radial_basis_type = {fam.name}", f"\tmin_dist = {_fmt(m.min_dist[0])}",
+                f"\tmax_dist = {_fmt(m.max_dist[0])}", f"\tradial_basis_size = {R}"]
+        out += fam.lines() + [f"\tradial_funcs_count = {mu}"]
     out.append("\tradial_coeffs")
     for i in range(K):
         for j in range(K):

@@ -34,7 +34,7 @@ extern "C" {
 #pragma GCC visibility push(default)
 #endif
 
-#define MTPB_ABI_VERSION 1
+#define MTPB_ABI_VERSION 2
 
 enum mtpb_status {
     MTPB_OK = 0,
@@ -49,9 +49,49 @@ enum mtpb_memory { MTPB_MEMORY_HOST = 0, MTPB_MEMORY_DEVICE = 1 };
 
 typedef struct mtpb_context mtpb_context;
 
-/* Linear MTP with Chebyshev radial bases.  Field meaning follows
- * MTPGpuPotentialView (runtime/mtp/gpu-direct/mtp_gpu_direct.h:270-325) and the
- * .mtp layout read by PotMTP::Load (potentials/potential_mtp.cpp:119-576):
+/* Radial basis families (basis/basis.cpp; numbering of RadialBasis,
+ * RadialCutoff and RadialTransform in runtime/mtp/gpu-direct/mtp_gpu_direct.h:
+ * 152-186).  Every family is a Chebyshev series in a coordinate x(r) times an
+ * envelope fc(r), scaled by the model's scaling:
+ *   RBChebyshev        x = (2r - min - max)/(max - min), fc = (r - max)^2
+ *   RBChebyCos         same x, fc = (1 + cos(pi r / max)) / 2
+ *   RBChebyshevPoly4   same x, fc = (1-t)^3 (1 + (3+b) t), t = (r-min)/(max-min)
+ *   RBChebyshevPoly5   same x, fc = (1-t)^4 (1 + (4+b) t)
+ *   RBChebyshevConfigurable  x from shift_type, fc from cutoff_type, optionally
+ *                      the 1 - T_(i+1) polynomials (basis.cpp:937-1013,
+ *                      cutoff.cpp, xtrans.cpp)
+ * Poly4, Poly5 and the configurable family are zero below min_dist. */
+enum mtpb_radial_type {
+    MTPB_RB_CHEBYSHEV = 0,
+    MTPB_RB_CHEBY_COS = 1,
+    MTPB_RB_CHEBY_POLY5 = 2,
+    MTPB_RB_CHEBY_CONFIGURABLE = 3,
+    MTPB_RB_CHEBY_POLY4 = 4
+};
+enum mtpb_radial_cutoff {   /* cutoff_type of RBChebyshevConfigurable */
+    MTPB_CUT_QUADRATIC = 0, MTPB_CUT_COSINE = 1, MTPB_CUT_POLY5 = 2,
+    MTPB_CUT_NORMALIZED_QUADRATIC = 3, MTPB_CUT_COSINE_LEFT = 4, MTPB_CUT_COSINE_UNSCALED = 5,
+    MTPB_CUT_COSINE_SQUARED = 6, MTPB_CUT_SINE_SQUARED = 7, MTPB_CUT_POLY3 = 8,
+    MTPB_CUT_POLY4 = 9, MTPB_CUT_SMOOTHSTEP5 = 10, MTPB_CUT_SMOOTHSTEP7 = 11
+};
+enum mtpb_radial_shift {   /* shift_type of RBChebyshevConfigurable */
+    MTPB_SHIFT_LINEAR = 0, MTPB_SHIFT_EXPONENTIAL = 1, MTPB_SHIFT_EXPONENTIAL_LEFT = 2,
+    MTPB_SHIFT_I2 = 3, MTPB_SHIFT_EXPONENTIAL_TANH = 4
+};
+typedef struct mtpb_radial_family {
+    int type;                  /* mtpb_radial_type */
+    int cutoff_type;           /* configurable only */
+    int shift_type;            /* configurable only */
+    int one_minus_chebyshev;   /* configurable only: basis_function_type */
+    double b;                  /* rb_b (Poly4, Poly5) or cutoff_b (poly3/4/5 cutoffs) */
+    double r1, r2;             /* cutoff_r1, cutoff_r2 (smoothstep7) */
+    double lambda;             /* shift_lambda */
+    double scale_lambda;       /* shift_scale_lambda */
+} mtpb_radial_family;
+
+/* Linear MTP.  Field meaning follows MTPGpuPotentialView
+ * (runtime/mtp/gpu-direct/mtp_gpu_direct.h:270-325) and the .mtp layout read
+ * by PotMTP::Load (potentials/potential_mtp.cpp:119-576):
  * radial_coeffs[(ti*K + tj)*mu*R + m*R + xi], alpha_index_basic[i] =
  * {mu, a, b, c}, alpha_index_times[t] = {l1, l2, coefficient, target}. */
 typedef struct mtpb_model_view {
@@ -72,6 +112,7 @@ typedef struct mtpb_model_view {
     const double *radial_coeffs;      /* [K*K*mu*R] */
     const double *species_coeffs;     /* [K] */
     const double *moment_coeffs;      /* [S] */
+    const mtpb_radial_family *radial_family;  /* NULL: RBChebyshev; else [1] or [K*K] */
 } mtpb_model_view;
 
 /* A batch of periodic structures (the Atoms + Neighborhoods inputs of

@@ -419,6 +419,244 @@ static void cheb_calc_der(double rmin, double rmax, double scaling, int R, doubl
     }
 }
 
+/* ---- other radial families ---------------------------------------------
+ * Value / derivative jets of basis/cutoff.cpp FormulaCutoff and
+ * basis/xtrans.cpp FormulaShift (their Jet2 arithmetic, first order). */
+typedef struct {
+    double v, d;
+} jet;
+static jet j_add(jet a, jet b) { jet r = {a.v + b.v, a.d + b.d}; return r; }
+static jet j_sub(jet a, jet b) { jet r = {a.v - b.v, a.d - b.d}; return r; }
+static jet j_mul(jet a, jet b) { jet r = {a.v * b.v, a.d * b.v + a.v * b.d}; return r; }
+static jet j_sc(double s, jet a) { jet r = {s * a.v, s * a.d}; return r; }
+static jet j_div(jet a, double s) { return j_sc(1.0 / s, a); }
+static jet j_cos(jet a) { jet r = {cos(a.v), -sin(a.v) * a.d}; return r; }
+static jet j_sin(jet a) { jet r = {sin(a.v), cos(a.v) * a.d}; return r; }
+static jet j_exp(jet a) { double e = exp(a.v); jet r = {e, e * a.d}; return r; }
+static jet j_tanh(jet a)
+{
+    double t = tanh(a.v);
+    jet r = {t, (1.0 - t * t) * a.d};
+    return r;
+}
+static jet j_pow2(jet a) { return j_mul(a, a); }
+static jet j_pow3(jet a) { return j_mul(j_mul(a, a), a); }
+static jet j_pow4(jet a) { return j_pow2(j_pow2(a)); }
+static jet j_pow5(jet a) { return j_mul(j_pow4(a), a); }
+static jet j_pow6(jet a) { return j_mul(j_pow3(a), j_pow3(a)); }
+static jet j_pow7(jet a) { return j_mul(j_pow6(a), a); }
+static const double ORACLE_PI = 3.141592653589793238462643383279502884;
+
+/* AnyCutoff::compute_der of basis/cutoff.cpp (QuadraticCutoff, CosineCutoff,
+ * Poly5Cutoff, FormulaCutoff::evaluate). */
+static void cutoff_der(const oracle_radial_family *f, double lo, double hi, double r, double *val,
+                       double *der)
+{
+    const double inv_range = 1.0 / (hi - lo);
+    if (f->cutoff_type == 0) { /* quadratic */
+        double delta = r - hi;
+        *val = delta * delta;
+        *der = 2.0 * delta;
+        return;
+    }
+    if (f->cutoff_type == 1) { /* cosine */
+        double freq = ORACLE_PI / (hi - lo);
+        double phase = (r - lo) * freq;
+        *val = 0.5 * (1.0 + cos(phase));
+        *der = -0.5 * freq * sin(phase);
+        return;
+    }
+    if (f->cutoff_type == 2) { /* poly5 */
+        double x = (r - lo) * inv_range;
+        double omx = 1.0 - x;
+        double square = omx * omx;
+        double cube = square * omx;
+        *val = square * square * (1.0 + (4.0 + f->b) * x);
+        *der = -cube * (20.0 * x + f->b * (5.0 * x - 1.0)) * inv_range;
+        return;
+    }
+    jet radius = {r, 1.0}, one = {1.0, 0.0}, lo_j = {lo, 0.0}, ir = {inv_range, 0.0};
+    jet t = j_mul(j_sub(radius, lo_j), ir);
+    jet q = j_sub(one, t);
+    jet out = {0.0, 0.0};
+    switch (f->cutoff_type) {
+    case 3: out = j_pow2(q); break;
+    case 4: out = j_sc(0.5, j_add(one, j_cos(j_sc(ORACLE_PI / hi, radius)))); break;
+    case 5: out = j_add(one, j_cos(j_sc(ORACLE_PI, t))); break;
+    case 6: out = j_pow2(j_add(one, j_cos(j_sc(ORACLE_PI, t)))); break;
+    case 7: out = j_pow2(j_sin(j_sc(ORACLE_PI, t))); break;
+    case 8: out = j_mul(j_pow2(q), j_add(one, j_sc(f->b + 2.0, t))); break;
+    case 9: out = j_mul(j_pow3(q), j_add(one, j_sc(f->b + 3.0, t))); break;
+    case 10:
+        out = j_add(j_sub(j_sc(6.0, j_pow5(q)), j_sc(15.0, j_pow4(q))), j_sc(10.0, j_pow3(q)));
+        break;
+    case 11:
+        if (r <= f->r1) {
+            jet p = j_div(j_sub(radius, lo_j), f->r1 - lo);
+            out = j_sub(j_add(j_sub(j_sc(35.0, j_pow4(p)), j_sc(84.0, j_pow5(p))),
+                              j_sc(70.0, j_pow6(p))),
+                        j_sc(20.0, j_pow7(p)));
+        } else if (r >= f->r2) {
+            jet r2 = {f->r2, 0.0};
+            jet p = j_div(j_sub(radius, r2), hi - f->r2);
+            out = j_add(j_sub(j_add(j_sub(one, j_sc(35.0, j_pow4(p))), j_sc(84.0, j_pow5(p))),
+                              j_sc(70.0, j_pow6(p))),
+                        j_sc(20.0, j_pow7(p)));
+        } else {
+            out = one;
+        }
+        break;
+    default: break;
+    }
+    *val = out.v;
+    *der = out.d;
+}
+
+/* AnyTrans::compute_der of basis/xtrans.cpp (LinearShift, ExponentialShift,
+ * FormulaShift::evaluate). */
+static void shift_der(const oracle_radial_family *f, double lo, double hi, double r, double *val,
+                      double *der)
+{
+    const double inv_range = 1.0 / (hi - lo);
+    const double lambda = f->lambda;
+    if (f->shift_type == 0) { /* linear */
+        double slope = 2.0 / (hi - lo);
+        *val = -1.0 + slope * (r - lo);
+        *der = slope;
+        return;
+    }
+    if (f->shift_type == 1) { /* exponential */
+        if (lambda == 0.0) {
+            *val = -1.0 + 2.0 * (r - lo) * inv_range;
+            *der = 2.0 * inv_range;
+            return;
+        }
+        double denominator = expm1(lambda);
+        double exponent = lambda * (hi - r) * inv_range;
+        double exponential = exp(exponent);
+        *val = 1.0 - 2.0 * expm1(exponent) / denominator;
+        *der = 2.0 * lambda * inv_range * exponential / denominator;
+        return;
+    }
+    jet radius = {r, 1.0}, one = {1.0, 0.0}, lo_j = {lo, 0.0}, ir = {inv_range, 0.0};
+    jet t = j_mul(j_sub(radius, lo_j), ir);
+    jet out = {0.0, 0.0};
+    if (f->shift_type == 3) { /* i2 */
+        jet hi_j = {hi, 0.0};
+        jet k = j_mul(j_sub(radius, hi_j), ir);
+        out = j_sub(j_sc(2.0, j_mul(k, k)), one);
+    } else if (f->shift_type == 2) { /* exponential_left */
+        if (lambda == 0.0) {
+            out = j_sub(j_div(j_sc(2.0, radius), hi), one);
+        } else {
+            double denominator = expm1(lambda);
+            jet exponent = j_sc(lambda, j_sub(one, j_div(radius, hi)));
+            out = j_sub(one, j_sc(2.0 / denominator, j_sub(j_exp(exponent), one)));
+        }
+    } else if (f->shift_type == 4) { /* exponential_tanh */
+        jet shifted;
+        if (lambda == 0.0) {
+            shifted = j_sub(j_sc(2.0, t), one);
+        } else {
+            double denominator = expm1(lambda);
+            shifted =
+                j_sub(one, j_sc(2.0 / denominator, j_sub(j_exp(j_sc(lambda, j_sub(one, t))), one)));
+        }
+        if (f->scale_lambda == 0.0)
+            out = shifted;
+        else
+            out = j_div(j_tanh(j_sc(f->scale_lambda, shifted)), tanh(f->scale_lambda));
+    }
+    *val = out.v;
+    *der = out.d;
+}
+
+/* Radial basis values and derivatives of a pair's family. */
+static void rb_calc_der(const oracle_model *m, int pair, int R, double r, double *val,
+                        double *der)
+{
+    const double lo = pair_min(m, pair), hi = pair_max(m, pair), s = m->scaling;
+    const oracle_radial_family *f = NULL;
+    if (m->radial_family)
+        f = &m->radial_family[m->radial_basis_split ? pair : 0];
+    if (!f || f->type == 0) {
+        cheb_calc_der(lo, hi, s, R, r, val, der);
+        return;
+    }
+    const double mult = 2.0 / (hi - lo), su = hi - lo, pu = hi + lo;
+    if (f->type == 3) { /* RBasis_ChebyshevConfigurable::calculate, order 1 */
+        if (r < lo || r > hi) {
+            for (int i = 0; i < R; ++i)
+                val[i] = der[i] = 0.0;
+            return;
+        }
+        double x, dx, fc, dfc;
+        shift_der(f, lo, hi, r, &x, &dx);
+        cutoff_der(f, lo, hi, r, &fc, &dfc);
+        const int flipped = f->one_minus_chebyshev != 0;
+        const int n = R + (flipped ? 1 : 0);
+        double *tv = (double *)calloc((size_t)n, sizeof(double));
+        double *td = (double *)calloc((size_t)n, sizeof(double));
+        tv[0] = 1.0;
+        if (n > 1) {
+            tv[1] = x;
+            td[1] = dx;
+        }
+        for (int i = 2; i < n; ++i) {
+            tv[i] = 2.0 * x * tv[i - 1] - tv[i - 2];
+            td[i] = 2.0 * (dx * tv[i - 1] + x * td[i - 1]) - td[i - 2];
+        }
+        for (int i = 0; i < R; ++i) {
+            const int k = i + (flipped ? 1 : 0);
+            const double raw = flipped ? 1.0 - tv[k] : tv[k];
+            const double raw_der = flipped ? -td[k] : td[k];
+            val[i] = s * raw * fc;
+            der[i] = s * (raw_der * fc + raw * dfc);
+        }
+        free(tv);
+        free(td);
+        return;
+    }
+    double ksi = (2 * r - pu) / su;
+    double rc, drc;
+    if (f->type == 1) { /* RBasis_ChebyCos::calc_der */
+        double irpi = ORACLE_PI / hi;   /* M_PI of basis.cpp */
+        rc = 0.5 * (1.0 + cos(r * irpi));
+        drc = -0.5 * irpi * sin(r * irpi);
+        val[0] = s * (1 * rc);
+        der[0] = s * (0 * rc + drc);
+    } else { /* RBasis_ChebyshevPoly4 / Poly5::calc_der */
+        if (r < lo || r > hi) {
+            for (int i = 0; i < R; ++i)
+                val[i] = der[i] = 0.0;
+            return;
+        }
+        double x = (r - lo) / su;
+        double dxdr = 1.0 / su;
+        double vx = 1.0 - x;
+        double vxx = vx * vx;
+        double vxxx = vxx * vx;
+        if (f->type == 2) {
+            double vxxxx = vxx * vxx;
+            rc = vxxxx * (1 + (4 + f->b) * x);
+            drc = -vxxx * (20 * x + f->b * (5 * x - 1)) * dxdr;
+        } else {
+            rc = vxxx * (1 + (3 + f->b) * x);
+            drc = vxx * (f->b * (1. - 4.0 * x) - 12.0 * x) * dxdr;
+        }
+        val[0] = s * rc;
+        der[0] = s * drc;
+    }
+    if (R == 1)
+        return;
+    val[1] = s * (ksi * rc);
+    der[1] = s * (mult * rc + ksi * drc);
+    for (int i = 2; i < R; i++) {
+        val[i] = 2 * ksi * val[i - 1] - val[i - 2];
+        der[i] = 2 * (mult * val[i - 1] + ksi * der[i - 1]) - der[i - 2];
+    }
+}
+
 #define CP(ws, k, a) ((ws)->cp[(k)*3 + (a)])
 #define MJ(ws, n, i, j, a) ((ws)->mj[((size_t)(i) * (n) + (j)) * 3 + (a)])
 
@@ -440,7 +678,7 @@ static void site_descriptors(const oracle_model *m, site_ws *ws, int itype, int 
         if (r > pair_max(m, pair))
             continue;
         const double rinv = 1.0 / r;
-        cheb_calc_der(pair_min(m, pair), pair_max(m, pair), m->scaling, R, r, ws->rv, ws->rd);
+        rb_calc_der(m, pair, R, r, ws->rv, ws->rd);
         ws->dp[0] = 1;
         for (int k = 1; k < ws->maxnu; ++k) {
             ws->dp[k] = ws->dp[k - 1] * rinv;
@@ -702,7 +940,7 @@ static void site_parameter_gradient(const oracle_model *m, site_ws *ws, int ityp
         if (r > pair_max(m, pair))
             continue;
         const double rinv = 1.0 / r;
-        cheb_calc_der(pair_min(m, pair), pair_max(m, pair), m->scaling, R, r, ws->rv, ws->rd);
+        rb_calc_der(m, pair, R, r, ws->rv, ws->rd);
         ws->dp[0] = 1;
         for (int k = 1; k < ws->maxnu; ++k) {
             ws->dp[k] = ws->dp[k - 1] * rinv;

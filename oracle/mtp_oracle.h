@@ -12,7 +12,11 @@
  *   - neighbour lists:  base/neighborhoods_base.h:31-126 (images, wrapping),
  *                       base/neighborhood.cpp:77-140 (pair filter and the
  *                       two-direction emission)
- *   - radial basis:     basis/basis.cpp:148-164 (RBasis_Chebyshev::calc_der)
+ *   - radial basis:     basis/basis.cpp:148-164 (RBasis_Chebyshev::calc_der),
+ *                       :265-280 (RBChebyCos), :644-673 (RBChebyshevPoly4),
+ *                       :776-806 (RBChebyshevPoly5), :937-1013
+ *                       (RBChebyshevConfigurable with basis/cutoff.cpp and
+ *                       basis/xtrans.cpp)
  *   - site EFS:         potentials/potential_mtp.cpp:2813-2925, 2959-2984,
  *                       3292-3305, 2938-2957 and the scatter in 1899-1933
  *   - parameter grad:   potentials/potential_mtp.cpp:3348-3550, 3312-3318,
@@ -30,6 +34,14 @@
 #ifdef __cplusplus
 extern "C" {
 #endif
+
+/* Radial basis family of a pair (same layout and numbering as
+ * mtpb_radial_family in include/mtpb200.h): type 0 RBChebyshev, 1 RBChebyCos,
+ * 2 RBChebyshevPoly5, 3 RBChebyshevConfigurable, 4 RBChebyshevPoly4. */
+typedef struct oracle_radial_family {
+    int type, cutoff_type, shift_type, one_minus_chebyshev;
+    double b, r1, r2, lambda, scale_lambda;
+} oracle_radial_family;
 
 /* Flat model description.  Same field order as mtpb_model_view in
  * include/mtpb200.h so one Python-side builder can fill both. */
@@ -51,6 +63,7 @@ typedef struct oracle_model {
     const double *radial_coeffs;     /* [K*K][mu][R] */
     const double *species_coeffs;    /* [K] */
     const double *moment_coeffs;     /* [S] */
+    const oracle_radial_family *radial_family; /* NULL: RBChebyshev; [1] or [K*K] */
 } oracle_model;
 
 /* Neighbour lists of one structure with the reference's default builder

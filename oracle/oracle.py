@@ -31,6 +31,23 @@ def _i(a):
     return a.ctypes.data_as(_ip) if a is not None else None
 
 
+class OracleRadialFamily(C.Structure):
+    """oracle_radial_family (same layout as mtpb_radial_family)."""
+    _fields_ = [("type", C.c_int), ("cutoff_type", C.c_int), ("shift_type", C.c_int),
+                ("one_minus_chebyshev", C.c_int), ("b", C.c_double), ("r1", C.c_double),
+                ("r2", C.c_double), ("shift_lambda", C.c_double),
+                ("shift_scale_lambda", C.c_double)]
+
+
+_RB_TYPES = {"RBChebyshev": 0, "RBChebyCos": 1, "RBChebyshevPoly5": 2,
+             "RBChebyshevConfigurable": 3, "RBChebyshevPoly4": 4}
+_CUTOFFS = {"quadratic": 0, "cosine": 1, "poly5": 2, "normalized_quadratic": 3,
+            "cosine_left": 4, "cosine_unscaled": 5, "cosine_squared": 6, "sine_squared": 7,
+            "poly3": 8, "poly4": 9, "smoothstep5": 10, "smoothstep7": 11}
+_SHIFTS = {"linear": 0, "exponential": 1, "exponential_left": 2, "i2": 3,
+           "exponential_tanh": 4}
+
+
 class OracleModel(C.Structure):
     _fields_ = [
         ("species_count", C.c_int), ("radial_func_count", C.c_int), ("rb_size", C.c_int),
@@ -40,6 +57,7 @@ class OracleModel(C.Structure):
         ("alpha_scalar_moments", C.c_int), ("alpha_index_basic", _ip),
         ("alpha_index_times", _ip), ("alpha_moment_mapping", _ip), ("radial_coeffs", _dp),
         ("species_coeffs", _dp), ("moment_coeffs", _dp),
+        ("radial_family", C.POINTER(OracleRadialFamily)),
     ]
 
 
@@ -61,13 +79,23 @@ def model_struct(model):
         species=np.ascontiguousarray(model.species_coeffs, dtype=np.float64),
         moment=np.ascontiguousarray(model.moment_coeffs, dtype=np.float64),
     )
+    fams = getattr(model, "radial_family", None)
+    fam_ptr = None
+    if fams:
+        arr = (OracleRadialFamily * len(fams))()
+        for i, f in enumerate(fams):
+            arr[i] = OracleRadialFamily(_RB_TYPES[f.name], _CUTOFFS[f.cutoff_type],
+                                        _SHIFTS[f.shift_type], int(f.one_minus_chebyshev),
+                                        f.b, f.r1, f.r2, f.shift_lambda, f.shift_scale_lambda)
+        keep["families"] = arr
+        fam_ptr = C.cast(arr, C.POINTER(OracleRadialFamily))
     s = OracleModel(model.species_count, model.radial_func_count, model.rb_size,
                     int(model.radial_basis_split), _d(keep["mins"]), _d(keep["maxs"]),
                     float(model.scaling), model.alpha_moments_count,
                     model.alpha_index_basic_count, model.alpha_index_times_count,
                     model.alpha_scalar_moments, _i(keep["basic"]), _i(keep["times"]),
                     _i(keep["mapping"]), _d(keep["radial"]), _d(keep["species"]),
-                    _d(keep["moment"]))
+                    _d(keep["moment"]), fam_ptr)
     return s, keep
 
 

@@ -33,3 +33,55 @@ def same_lists(off_a, nbr_a, rij_a, off_b, nbr_b, rij_b) -> bool:
     na, ra, _ = canonical(off_a, nbr_a, rij_a)
     nb, rb, _ = canonical(off_b, nbr_b, rij_b)
     return np.array_equal(na, nb) and np.array_equal(bits(ra), bits(rb))
+
+
+# Radial families exercised by the parity tests: every family, every
+# configurable cutoff and shift, the one-minus-Chebyshev polynomials, lambda = 0
+# branches, and a lower bound that excludes the first neighbour shell.
+RADIAL_CASES = {
+    "chebycos": dict(name="RBChebyCos"),
+    "poly4": dict(name="RBChebyshevPoly4", b=-0.5),
+    "poly5": dict(name="RBChebyshevPoly5", b=-1.0 / 3.0),
+    "poly5_min26": dict(name="RBChebyshevPoly5", b=0.25, min_dist=2.6),
+    "cfg_cosine_linear": dict(name="RBChebyshevConfigurable", cutoff_type="cosine"),
+    "cfg_poly5_exp": dict(name="RBChebyshevConfigurable", cutoff_type="poly5", b=0.2,
+                          shift_type="exponential", shift_lambda=1.5),
+    "cfg_smooth7_tanh_flip": dict(name="RBChebyshevConfigurable", cutoff_type="smoothstep7",
+                                  r1=3.0, r2=4.0, shift_type="exponential_tanh",
+                                  shift_lambda=1.2, shift_scale_lambda=0.7,
+                                  one_minus_chebyshev=True),
+    "cfg_nquad_i2": dict(name="RBChebyshevConfigurable", cutoff_type="normalized_quadratic",
+                         shift_type="i2"),
+    "cfg_cosleft_expleft": dict(name="RBChebyshevConfigurable", cutoff_type="cosine_left",
+                                shift_type="exponential_left", shift_lambda=0.8),
+    "cfg_cosunscaled_exp0": dict(name="RBChebyshevConfigurable", cutoff_type="cosine_unscaled",
+                                 shift_type="exponential", shift_lambda=0.0),
+    "cfg_cossq_flip": dict(name="RBChebyshevConfigurable", cutoff_type="cosine_squared",
+                           one_minus_chebyshev=True),
+    "cfg_sinsq_tanh0": dict(name="RBChebyshevConfigurable", cutoff_type="sine_squared",
+                            shift_type="exponential_tanh", shift_lambda=0.0,
+                            shift_scale_lambda=0.5),
+    "cfg_poly3": dict(name="RBChebyshevConfigurable", cutoff_type="poly3", b=0.1),
+    "cfg_poly4_expleft0": dict(name="RBChebyshevConfigurable", cutoff_type="poly4", b=-0.2,
+                               shift_type="exponential_left", shift_lambda=0.0),
+    "cfg_smooth5_i2": dict(name="RBChebyshevConfigurable", cutoff_type="smoothstep5",
+                           shift_type="i2"),
+    "cfg_quad_tanh_noscale": dict(name="RBChebyshevConfigurable", cutoff_type="quadratic",
+                                  shift_type="exponential_tanh", shift_lambda=0.9,
+                                  shift_scale_lambda=0.0),
+}
+
+
+def with_radial_family(model, case):
+    """The model with every pair's radial basis replaced by RADIAL_CASES[case]
+    (an optional min_dist in the case moves the lower bound)."""
+    import dataclasses
+    from mtpb200.mtpfile import RadialFamily
+    spec = dict(RADIAL_CASES[case])
+    lo = spec.pop("min_dist", None)
+    fam = RadialFamily(**spec)
+    n = model.species_count ** 2 if model.radial_basis_split else 1
+    mins = np.array(model.min_dist, dtype=np.float64)
+    if lo is not None:
+        mins[:] = lo
+    return dataclasses.replace(model, radial_family=[fam] * n, min_dist=mins)

@@ -35,7 +35,7 @@ def test_python_signatures_cover_header():
 def test_abi_version_and_error_without_device():
     import mtpb200
     lib = mtpb200.library()
-    assert lib.mtpb_abi_version() == 1
+    assert lib.mtpb_abi_version() == 2
     if mtpb200.device_count() > 0:
         pytest.skip("a device is present")
     m = load_model("pair_k1.mtp")
@@ -85,3 +85,25 @@ def test_mtp_parser_reads_reference_templates():
             m.alpha_moments_count) == (295, 4665, 288, 1035)
     assert m.scaling == 0.01
     assert m.basis_shape() == [8, 6, 4, 2, 0]
+
+
+@pytest.mark.parametrize("field,value,message", [
+    ("type", 5, b"unsupported radial basis type 5"),          # RBPolyB
+    ("cutoff_type", 12, b"unknown configurable cutoff_type"),
+    ("r2", 6.0, b"smoothstep7 cutoff requires"),
+    ("shift_lambda", float("nan"), b"non-finite radial parameter"),
+])
+def test_radial_family_validation(field, value, message):
+    """Model validation of the radial families runs before any device call:
+    unsupported families and invalid parameters are refused by mtpb_create."""
+    import ctypes as C
+    import mtpb200
+    from helpers import with_radial_family
+    m = with_radial_family(load_model("l16_k2.mtp"), "cfg_smooth7_tanh_flip")
+    keep = mtpb200._ModelKeep(m)
+    setattr(keep.families[0], field, value)
+    lib = mtpb200.library()
+    ctx = C.c_void_p()
+    rc = lib.mtpb_create(0, C.byref(keep.view), C.byref(ctx))
+    assert rc == 1 and message in lib.mtpb_last_error(), lib.mtpb_last_error()
+    assert not ctx.value

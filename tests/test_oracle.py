@@ -6,6 +6,7 @@ import numpy as np
 import pytest
 
 from conftest import GOLDEN, load_model
+from helpers import RADIAL_CASES, with_radial_family
 from mtpb200 import configs, format_mtp
 from oracle import concat_lists
 
@@ -188,3 +189,29 @@ def test_oracle_efs_matches_mlipcore_generated_level24(oracle, reference, case):
                                         oracle.wrap(st["cell"], st["pbc"], st["positions"]))
     assert abs(e - e2) < 1e-12 * max(1, abs(e))
     assert np.max(np.abs(f - f2)) < 1e-11 * max(1.0, np.max(np.abs(f)))
+
+
+@pytest.mark.parametrize("case", sorted(RADIAL_CASES))
+def test_oracle_radial_families_match_mlipcore(oracle, reference, model_l16, case):
+    """Every radial family (and configurable cutoff / shift) of the C
+    restatement, which follows basis/basis.cpp, cutoff.cpp and xtrans.cpp,
+    against the compiled reference MLIPCore reading the same .mtp text
+    (runtime/mtp/radial_basis.h)."""
+    m = with_radial_family(model_l16, case)
+    st = configs.config1()
+    nl = oracle.neighbors(st["cell"], st["pbc"], st["positions"], m.cutoff)
+    e, se, f, s = oracle.efs(m, st["types"], nl)
+    e2, se2, f2, _ = reference.mlip_efs(format_mtp(m), st["types"], nl,
+                                        oracle.wrap(st["cell"], st["pbc"], st["positions"]))
+    assert abs(e - e2) < 1e-11 * max(1, abs(e)), (e, e2)
+    assert np.max(np.abs(f - f2)) < 1e-10 * max(1.0, np.max(np.abs(f)))
+    assert np.max(np.abs(se - se2)) < 1e-11 * max(1.0, np.max(np.abs(se)))
+
+
+@pytest.mark.parametrize("case", sorted(RADIAL_CASES))
+def test_mtp_radial_family_round_trip(case, model_l16):
+    from mtpb200 import parse_mtp
+    m = with_radial_family(model_l16, case)
+    m2 = parse_mtp(format_mtp(m))
+    assert m2.radial_family == m.radial_family
+    assert np.array_equal(m2.min_dist, m.min_dist)
