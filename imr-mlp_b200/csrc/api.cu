@@ -230,6 +230,9 @@ EdgeArgs edge_args(const mtpb_context *c, int ncenter, const int *types, const i
     a.scaling = c->model.scaling;
     a.radial = c->d_radial;
     a.pairs = c->d_pairs;
+    a.rb_generic = 0;
+    for (const RadialFamily &f : c->model.family)
+        a.rb_generic |= f.type != RB_CHEBYSHEV;
     return a;
 }
 

@@ -54,7 +54,9 @@ struct StageView {
 
 // Computes the per-edge quantities of one chunk of edge slots for the 32
 // atoms of this block.  Every thread of the block takes part.
-template <class S, int NW, bool REV>
+// RG: the model has radial families other than RBChebyshev (radial.cuh);
+// the RBChebyshev-only kernels carry none of their code.
+template <class S, int NW, bool REV, bool RG>
 __device__ __forceinline__ void stage_chunk(const EdgeArgs &p, const StageView &v, int atom0,
                                             int chunk)
 {
@@ -99,7 +101,7 @@ __device__ __forceinline__ void stage_chunk(const EdgeArgs &p, const StageView &
                                             __dmul_rn(z, z));
                 const double r = sqrt(r2);
                 // atoms of type -1 are skipped (runtime/mtp/mlip.cpp:944, 952)
-                const PairParams pp = v.pairs[pair >= 0 ? pair : 0];
+                const PairParams &pp = v.pairs[pair >= 0 ? pair : 0];
                 // potential_mtp.cpp:2842 skips r > cutoff; mlip.cpp:966 r > 0
                 if (pair >= 0 && r > 0.0 && r <= pp.rmax) {
                     rinv = 1.0 / r;
@@ -109,13 +111,17 @@ __device__ __forceinline__ void stage_chunk(const EdgeArgs &p, const StageView &
                     // radial basis of the pair's family (radial.cuh) folded
                     // into the channel sums f_mu = sum_xi c[pair,mu,xi] Q_xi(r)
                     const double *c = v.radial + pair * NMU * p.R;
-                    radial_basis(pp, p.scaling, p.R, r, [&](int xi, double q, double d) {
+                    auto emit = [&](int xi, double q, double d) {
 #pragma unroll
                         for (int m = 0; m < NMU; ++m) {
                             f[m] = fma(c[m * p.R + xi], q, f[m]);
                             fp[m] = fma(c[m * p.R + xi], d, fp[m]);
                         }
-                    });
+                    };
+                    if constexpr (RG)
+                        radial_basis(pp, p.scaling, p.R, r, emit);
+                    else
+                        radial_chebyshev(pp, p.scaling, p.R, r, emit);
                 }
             }
         }
@@ -137,7 +143,7 @@ __device__ __forceinline__ void stage_chunk(const EdgeArgs &p, const StageView &
 // ----------------------------------------------------------------------------
 // Forward: basic moments of 32 atoms; warp W owns the chains of Partition.
 // ----------------------------------------------------------------------------
-template <class S, int NW, int W>
+template <class S, int NW, int W, bool RG>
 __device__ __forceinline__ void fwd_warp(const EdgeArgs &p, const StageView &v, int atom0,
                                          int maxdeg, double *basic)
 {
@@ -154,7 +160,7 @@ __device__ __forceinline__ void fwd_warp(const EdgeArgs &p, const StageView &v, 
         acc[i] = 0.0;
     const int nchunks = (maxdeg + KS - 1) / KS;
     for (int ch = 0; ch < nchunks; ++ch) {
-        stage_chunk<S, NW, false>(p, v, atom0, ch);
+        stage_chunk<S, NW, false, RG>(p, v, atom0, ch);
         __syncthreads();
         const int kend = min(KS, maxdeg - ch * KS);
         for (int k = 0; k < kend; ++k) {
@@ -224,7 +230,7 @@ __device__ __forceinline__ void fwd_warp(const EdgeArgs &p, const StageView &v, 
 // the size of the chain partition, W the warp's index in it and NWB the warps
 // of this block; the first part stores the sums, later parts add to them.
 // ----------------------------------------------------------------------------
-template <class S, int NW, int W, int NWB, bool FIRST>
+template <class S, int NW, int W, int NWB, bool FIRST, bool RG>
 __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, int atom0,
                                          int maxdeg, const double *adjoint, double *dx,
                                          double *dy, double *dz)
@@ -255,7 +261,7 @@ __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, 
     }
     const int nchunks = (maxdeg + KS - 1) / KS;
     for (int ch = 0; ch < nchunks; ++ch) {
-        stage_chunk<S, NW, true>(p, v, atom0, ch);
+        stage_chunk<S, NW, true, RG>(p, v, atom0, ch);
         __syncthreads();
         const int kend = min(KS, maxdeg - ch * KS);
         for (int k = 0; k < kend; ++k) {
@@ -369,7 +375,7 @@ __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, 
 
 // PART: which block of NW warps of the NW * NPART chain partition this launch
 // runs
-template <class S, bool REV, int PART>
+template <class S, bool REV, int PART, bool RG>
 __global__ void __launch_bounds__(ShapeCfg<S>::NW * 32, KCfg<S, REV>::BLOCKS)
     k_moments(EdgeArgs p, double *basic, const double *adjoint, double *dx, double *dy,
               double *dz)
@@ -407,9 +413,9 @@ __global__ void __launch_bounds__(ShapeCfg<S>::NW * 32, KCfg<S, REV>::BLOCKS)
         constexpr int W = PART * NW + WL;
         if (warp == WL) {
             if constexpr (REV)
-                rev_warp<S, NWT, W, NW, PART == 0>(p, v, atom0, maxdeg, adjoint, dx, dy, dz);
+                rev_warp<S, NWT, W, NW, PART == 0, RG>(p, v, atom0, maxdeg, adjoint, dx, dy, dz);
             else
-                fwd_warp<S, NWT, W>(p, v, atom0, maxdeg, basic);
+                fwd_warp<S, NWT, W, RG>(p, v, atom0, maxdeg, basic);
         }
     });
 }
@@ -429,7 +435,7 @@ template <class S, bool REV> static cudaError_t launch_shape(const EdgeArgs &a, 
         constexpr int P = decltype(ip)::value;
         if (err != cudaSuccess)
             return;
-        auto kern = k_moments<S, REV, P>;
+        auto kern = a.rb_generic ? k_moments<S, REV, P, true> : k_moments<S, REV, P, false>;
         err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (err == cudaSuccess) {
             kern<<<groups, NW * 32, smem, s>>>(a, basic, adjoint, dx, dy, dz);

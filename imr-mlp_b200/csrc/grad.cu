@@ -77,7 +77,7 @@ struct GradView {
 // Per-edge dual geometry (and for TAN the radial functions with their
 // directional derivatives) of one chunk of edge slots of 32 atoms.  Edges the
 // reference skips (r > cutoff, r = 0, type -1) stage zeros.
-template <class S, int NW, bool TAN>
+template <class S, int NW, bool TAN, bool RG>
 __device__ __forceinline__ void grad_stage(const EdgeArgs &p, const double *__restrict__ wx,
                                            const double *__restrict__ wy,
                                            const double *__restrict__ wz, const GradView &v,
@@ -106,7 +106,7 @@ __device__ __forceinline__ void grad_stage(const EdgeArgs &p, const double *__re
                 const int it = __ldg(p.types + atom);
                 const int jt = __ldg(p.types + __ldg(p.nbr + e));
                 const int pair = (it >= 0 && jt >= 0) ? it * p.K + jt : 0;
-                const PairParams pp = v.pairs[pair];
+                const PairParams &pp = v.pairs[pair];
                 if (it >= 0 && jt >= 0 && r > 0.0 && r <= pp.rmax) {
                     const double rinv = 1.0 / r;
                     const double w[3] = {__ldg(wx + e), __ldg(wy + e), __ldg(wz + e)};
@@ -125,13 +125,17 @@ __device__ __forceinline__ void grad_stage(const EdgeArgs &p, const double *__re
                             f[m] = 0.0;
                             fp[m] = 0.0;
                         }
-                        radial_basis(pp, p.scaling, p.R, r, [&](int xi, double q, double d) {
+                        auto emit = [&](int xi, double q, double d) {
 #pragma unroll
                             for (int m = 0; m < NMU; ++m) {
                                 f[m] = fma(c[m * p.R + xi], q, f[m]);
                                 fp[m] = fma(c[m * p.R + xi], d, fp[m]);
                             }
-                        });
+                        };
+                        if constexpr (RG)
+                            radial_basis(pp, p.scaling, p.R, r, emit);
+                        else
+                            radial_chebyshev(pp, p.scaling, p.R, r, emit);
 #pragma unroll
                         for (int m = 0; m < NMU; ++m)
                             fd[m] = fp[m] * sw;
@@ -189,7 +193,7 @@ __device__ __forceinline__ void chain_base(const double *yp, const double *zp, d
 // Tangent basic moments of 32 atoms: Db = sum_j (D_w f) u + f D_w u.  Warp W
 // owns the chains of Partition, as in the forward kernel.
 // ----------------------------------------------------------------------------
-template <class S, int NW, int W>
+template <class S, int NW, int W, bool RG>
 __device__ __forceinline__ void tan_warp(const EdgeArgs &p, const double *wx, const double *wy,
                                          const double *wz, const GradView &v, int atom0,
                                          int maxdeg, double *tangent)
@@ -208,7 +212,7 @@ __device__ __forceinline__ void tan_warp(const EdgeArgs &p, const double *wx, co
         acc[i] = 0.0;
     const int nchunks = (maxdeg + KSG - 1) / KSG;
     for (int ch = 0; ch < nchunks; ++ch) {
-        grad_stage<S, NW, true>(p, wx, wy, wz, v, atom0, ch);
+        grad_stage<S, NW, true, RG>(p, wx, wy, wz, v, atom0, ch);
         __syncthreads();
         const int kend = min(KSG, maxdeg - ch * KSG);
         for (int k = 0; k < kend; ++k) {
@@ -317,7 +321,7 @@ __device__ __forceinline__ void edge_grad_warp(const EdgeArgs &p, const double *
     const int nchunks = (maxdeg + KSG - 1) / KSG;
     double *part = v.part + (size_t)(W % NWB) * 2 * NMU * KSG * 32;
     for (int ch = 0; ch < nchunks; ++ch) {
-        grad_stage<S, NW, false>(p, wx, wy, wz, v, atom0, ch);
+        grad_stage<S, NW, false, false>(p, wx, wy, wz, v, atom0, ch);
         __syncthreads();
         const int kend = min(KSG, maxdeg - ch * KSG);
         for (int k = 0; k < kend; ++k) {
@@ -400,7 +404,7 @@ __device__ __forceinline__ void edge_grad_warp(const EdgeArgs &p, const double *
 
 // MODE 0: tangent basics; 1-3: edge records with PASS = MODE - 1; PART: which
 // block of NW warps of the chain partition this launch runs
-template <class S, int MODE, int PART>
+template <class S, int MODE, int PART, bool RG>
 __global__ void __launch_bounds__(GradCfg<S>::NW * 32, GradCfg<S>::BLOCKS)
     k_grad_moments(EdgeArgs p, const double *__restrict__ wx, const double *__restrict__ wy,
                    const double *__restrict__ wz, const double *__restrict__ adjoint,
@@ -441,7 +445,7 @@ __global__ void __launch_bounds__(GradCfg<S>::NW * 32, GradCfg<S>::BLOCKS)
         constexpr int W = PART * NW + WL;
         if (warp == WL) {
             if constexpr (TAN)
-                tan_warp<S, NWT, W>(p, wx, wy, wz, v, atom0, maxdeg, out);
+                tan_warp<S, NWT, W, RG>(p, wx, wy, wz, v, atom0, maxdeg, out);
             else
                 edge_grad_warp<S, NWT, W, MODE - 1, NW, PART == 0>(p, wx, wy, wz, v, atom0,
                                                                    maxdeg, adjoint, adjoint2,
@@ -465,7 +469,9 @@ static cudaError_t launch_grad_shape(const EdgeArgs &a, const double *wx, const 
         constexpr int P = decltype(ip)::value;
         if (err != cudaSuccess)
             return;
-        auto kern = k_grad_moments<S, MODE, P>;
+        // the edge records take no radial values: one instantiation
+        auto kern = (MODE == 0 && a.rb_generic) ? k_grad_moments<S, MODE, P, MODE == 0>
+                                                : k_grad_moments<S, MODE, P, false>;
         err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (err == cudaSuccess) {
             kern<<<groups, NW * 32, smem, s>>>(a, wx, wy, wz, adjoint, adjoint2, out);

@@ -135,6 +135,7 @@ struct EdgeArgs {
     double scaling;
     const double *radial;          // [K*K][mu_total][R]
     const PairParams *pairs;       // [K*K]
+    int rb_generic;                // some pair's radial family is not RBChebyshev
 };
 
 // launchers (efs.cu); moment_kernel_parts = launches per call

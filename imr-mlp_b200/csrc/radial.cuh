@@ -177,85 +177,129 @@ static __device__ __noinline__ void radial_shift(const PairParams &pp, double r,
     dx = out.d;
 }
 
-// Q_xi(r) and dQ_xi/dr for xi = 0..R-1 of the pair's family, in order, passed
-// to emit(xi, q, dq); s is the model's scaling.  Returns false (and emits
-// nothing: every Q is zero) where the family vanishes: below min_dist for
-// Poly4, Poly5 and the configurable family.  Callers have already skipped
-// r > max_dist.
+// RBChebyshev alone (basis.cpp:148-164): the kernels of models without other
+// families use this.
 template <class Emit>
-__device__ __forceinline__ bool radial_basis(const PairParams &pp, double s, int R, double r,
-                                             Emit &&emit)
+__device__ __forceinline__ void radial_chebyshev(const PairParams &pp, double s, int R, double r,
+                                                 Emit &&emit)
 {
     const double ksi = (2.0 * r - pp.pu) / pp.su;
-    if (pp.type == RB_CHEBYSHEV) {
-        const double ru = r - pp.rmax;
-        double q0 = s * (ru * ru), d0 = s * (2.0 * ru);
-        emit(0, q0, d0);
-        if (R > 1) {
-            double q1 = s * (ksi * ru * ru);
-            double d1 = s * (pp.mult * ru * ru + 2.0 * ksi * ru);
-            emit(1, q1, d1);
-            for (int xi = 2; xi < R; ++xi) {
-                const double q2 = 2.0 * ksi * q1 - q0;
-                const double d2 = 2.0 * (pp.mult * q1 + ksi * d1) - d0;
-                emit(xi, q2, d2);
-                q0 = q1;
-                q1 = q2;
-                d0 = d1;
-                d1 = d2;
-            }
-        }
-        return true;
-    }
-    if (pp.type != RB_CHEBY_COS && r < pp.rmin)
-        return false;
-    if (pp.type == RB_CONFIGURABLE) {
-        double x, dx, fc, dfc;
-        radial_shift(pp, r, x, dx);
-        radial_cutoff(pp, r, fc, dfc);
-        // Chebyshev polynomials T_i(x) and their r-derivatives, then
-        // Q_i = s raw_i fc with raw_i = T_i, or 1 - T_(i+1) when flipped
-        double t0 = 1.0, g0 = 0.0, t1 = x, g1 = dx;
-        for (int i = 0; i < R; ++i) {
-            const double raw = pp.flipped ? 1.0 - t1 : t0;
-            const double rawd = pp.flipped ? -g1 : g0;
-            emit(i, s * raw * fc, s * (rawd * fc + raw * dfc));
-            const double t2 = 2.0 * x * t1 - t0;
-            const double g2 = 2.0 * (dx * t1 + x * g1) - g0;
-            t0 = t1;
-            t1 = t2;
-            g0 = g1;
-            g1 = g2;
-        }
-        return true;
-    }
-    double rc, drc;
-    if (pp.type == RB_CHEBY_COS) {
-        rc = 0.5 * (1.0 + cos(r * pp.irpi));
-        drc = -0.5 * pp.irpi * sin(r * pp.irpi);
-    } else {   // Poly4 / Poly5 envelopes in t = (r - min) / (max - min)
-        const double x = (r - pp.rmin) / pp.su;
-        const double dxdr = 1.0 / pp.su;
-        const double vx = 1.0 - x;
-        const double vxx = vx * vx;
-        const double vxxx = vxx * vx;
-        if (pp.type == RB_CHEBY_POLY5) {
-            rc = vxx * vxx * (1 + (4 + pp.b) * x);
-            drc = -vxxx * (20 * x + pp.b * (5 * x - 1)) * dxdr;
-        } else {
-            rc = vxxx * (1 + (3 + pp.b) * x);
-            drc = vxx * (pp.b * (1. - 4.0 * x) - 12.0 * x) * dxdr;
-        }
-    }
-    double q0 = s * rc, d0 = s * drc;
+    const double ru = r - pp.rmax;
+    double q0 = s * (ru * ru), d0 = s * (2.0 * ru);
     emit(0, q0, d0);
     if (R > 1) {
-        double q1 = s * (ksi * rc);
-        double d1 = s * (pp.mult * rc + ksi * drc);
+        double q1 = s * (ksi * ru * ru);
+        double d1 = s * (pp.mult * ru * ru + 2.0 * ksi * ru);
         emit(1, q1, d1);
         for (int xi = 2; xi < R; ++xi) {
             const double q2 = 2.0 * ksi * q1 - q0;
             const double d2 = 2.0 * (pp.mult * q1 + ksi * d1) - d0;
+            emit(xi, q2, d2);
+            q0 = q1;
+            q1 = q2;
+            d0 = d1;
+            d1 = d2;
+        }
+    }
+}
+
+// Coordinate and envelope of the families other than RBChebyshev, out of
+// line so that their transcendental functions stay out of the moment kernels'
+// instruction stream.  mode 0: the family vanishes at r (below min_dist for
+// Poly4, Poly5 and the configurable family); 1: Chebyshev series in x times
+// the envelope, carried through the recurrence (basis.cpp calc_der of
+// RBChebyCos, Poly4, Poly5); 2: configurable, polynomials first, then scaled
+// by the envelope (basis.cpp:937-1013).
+struct RadialStart {
+    int mode;
+    double x, dx, fc, dfc;
+};
+static __device__ __noinline__ RadialStart radial_start(const PairParams &pp, double r)
+{
+    RadialStart st{0, 0.0, 0.0, 0.0, 0.0};
+    if (pp.type != RB_CHEBY_COS && r < pp.rmin)
+        return st;
+    if (pp.type == RB_CONFIGURABLE) {
+        radial_shift(pp, r, st.x, st.dx);
+        radial_cutoff(pp, r, st.fc, st.dfc);
+        st.mode = 2;
+        return st;
+    }
+    st.mode = 1;
+    st.x = (2.0 * r - pp.pu) / pp.su;
+    st.dx = pp.mult;
+    if (pp.type == RB_CHEBY_COS) {
+        st.fc = 0.5 * (1.0 + cos(r * pp.irpi));
+        st.dfc = -0.5 * pp.irpi * sin(r * pp.irpi);
+        return st;
+    }
+    // Poly4 / Poly5 envelopes in t = (r - min) / (max - min)
+    const double t = (r - pp.rmin) / pp.su;
+    const double dtdr = 1.0 / pp.su;
+    const double vx = 1.0 - t;
+    const double vxx = vx * vx;
+    const double vxxx = vxx * vx;
+    if (pp.type == RB_CHEBY_POLY5) {
+        st.fc = vxx * vxx * (1 + (4 + pp.b) * t);
+        st.dfc = -vxxx * (20 * t + pp.b * (5 * t - 1)) * dtdr;
+    } else {
+        st.fc = vxxx * (1 + (3 + pp.b) * t);
+        st.dfc = vxx * (pp.b * (1. - 4.0 * t) - 12.0 * t) * dtdr;
+    }
+    return st;
+}
+
+// Q_xi(r) and dQ_xi/dr for xi = 0..R-1 of the pair's family, in order, passed
+// to emit(xi, q, dq); s is the model's scaling.  Returns false (and emits
+// nothing: every Q is zero) where the family vanishes.  Callers have already
+// skipped r > max_dist.
+template <class Emit>
+__device__ __forceinline__ bool radial_basis(const PairParams &pp, double s, int R, double r,
+                                             Emit &&emit)
+{
+    double x, dx, q0, d0, q1, d1;
+    if (pp.type == RB_CHEBYSHEV) {
+        x = (2.0 * r - pp.pu) / pp.su;
+        dx = pp.mult;
+        const double ru = r - pp.rmax;
+        q0 = s * (ru * ru);
+        d0 = s * (2.0 * ru);
+        q1 = s * (x * ru * ru);
+        d1 = s * (dx * ru * ru + 2.0 * x * ru);
+    } else {
+        const RadialStart st = radial_start(pp, r);
+        if (st.mode == 0)
+            return false;
+        x = st.x;
+        dx = st.dx;
+        if (st.mode == 2) {
+            // T_i(x) and their r-derivatives, then Q_i = s raw_i fc with
+            // raw_i = T_i, or 1 - T_(i+1) for the one-minus-Chebyshev type
+            double t0 = 1.0, g0 = 0.0, t1 = x, g1 = dx;
+            for (int i = 0; i < R; ++i) {
+                const double raw = pp.flipped ? 1.0 - t1 : t0;
+                const double rawd = pp.flipped ? -g1 : g0;
+                emit(i, s * raw * st.fc, s * (rawd * st.fc + raw * st.dfc));
+                const double t2 = 2.0 * x * t1 - t0;
+                const double g2 = 2.0 * (dx * t1 + x * g1) - g0;
+                t0 = t1;
+                t1 = t2;
+                g0 = g1;
+                g1 = g2;
+            }
+            return true;
+        }
+        q0 = s * st.fc;
+        d0 = s * st.dfc;
+        q1 = s * (x * st.fc);
+        d1 = s * (dx * st.fc + x * st.dfc);
+    }
+    emit(0, q0, d0);
+    if (R > 1) {
+        emit(1, q1, d1);
+        for (int xi = 2; xi < R; ++xi) {
+            const double q2 = 2.0 * x * q1 - q0;
+            const double d2 = 2.0 * (dx * q1 + x * d1) - d0;
             emit(xi, q2, d2);
             q0 = q1;
             q1 = q2;

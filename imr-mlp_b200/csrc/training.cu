@@ -214,6 +214,7 @@ __global__ void k_bucket_bounds(long E, int nb, const unsigned *__restrict__ sor
 // sums them.  partial[block][p][mu][xi].
 constexpr int RG_THREADS = 256;
 
+template <bool RG>   // RG: radial families other than RBChebyshev present
 __global__ void __launch_bounds__(RG_THREADS)
     k_radial_grad(int KK, int nmu, int R, double scaling, const long *__restrict__ bounds,
                   const int *__restrict__ perm, const double *__restrict__ rx,
@@ -234,7 +235,7 @@ __global__ void __launch_bounds__(RG_THREADS)
         const long per = (b1 - b0 + gridDim.x - 1) / gridDim.x;
         const long lo = b0 + per * blockIdx.x;
         const long hi = min(b1, lo + per);
-        const PairParams pp = pairs[p];
+        const PairParams &pp = pairs[p];
         double acc = 0.0;
         for (long base = lo; base < hi; base += RG_THREADS) {
             const long i = base + tid;
@@ -247,10 +248,14 @@ __global__ void __launch_bounds__(RG_THREADS)
                     Q[tid * R + xi] = 0.0;
                     Qd[tid * R + xi] = 0.0;
                 }
-                radial_basis(pp, scaling, R, r, [&](int xi, double q, double d) {
+                auto emit = [&](int xi, double q, double d) {
                     Q[tid * R + xi] = q;
                     Qd[tid * R + xi] = d;
-                });
+                };
+                if constexpr (RG)
+                    radial_basis(pp, scaling, R, r, emit);
+                else
+                    radial_chebyshev(pp, scaling, R, r, emit);
                 const double *u = uv + (size_t)e * 2 * nmu;
                 for (int m = 0; m < nmu; ++m) {
                     U[tid * nmu + m] = u[m];
@@ -555,10 +560,11 @@ int loss_grad_compute(mtpb_context *c, const mtpb_labels *labels, const mtpb_los
     c->launches += (energy_only ? 0 : grad_kernel_launches(c->shape, false)) + 1 +
                    grad_kernel_launches(c->shape, true);
     const size_t rg_smem = sizeof(double) * RG_THREADS * (2 * m.R + 2 * nmu);
-    CUDA_TRY(cudaFuncSetAttribute(k_radial_grad, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    auto rg_kern = a.rb_generic ? k_radial_grad<true> : k_radial_grad<false>;
+    CUDA_TRY(cudaFuncSetAttribute(rg_kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)rg_smem),
              "radial gradient attribute");
-    k_radial_grad<<<rg_grid, RG_THREADS, rg_smem, c->stream>>>(
+    rg_kern<<<rg_grid, RG_THREADS, rg_smem, c->stream>>>(
         KK, nmu, m.R, m.scaling, c->train.bounds, c->train.perm, c->nb.rx, c->nb.ry, c->nb.rz,
         c->d_pairs, uv, rpart);
     CUDA_TRY(cudaGetLastError(), "radial gradient");
