@@ -71,3 +71,27 @@ def test_csr_without_centres(model_l16):
                                 np.zeros(4, np.int32), np.zeros((4, 3)), center_count=0)
     assert out["energy"] == 0.0
     assert np.all(out["force"] == 0.0) and np.all(out["virial"] == 0.0)
+
+
+@pytest.mark.parametrize("cutoff", [8.0, 11.0])
+def test_high_degree_lists(oracle, model_l16, cutoff):
+    """Long cutoffs on the 256-atom box: about 200 and 530 neighbours per atom,
+    so the in-edge lists take the 256-entry register sort and the single-lane
+    fallback of the neighbour builder; lists, energies and forces still match
+    the oracle."""
+    import dataclasses
+    from helpers import same_lists
+    from mtpb200 import MTPGpuDirect, StructureBatch
+    m = dataclasses.replace(model_l16, max_dist=np.array([cutoff]))
+    st = configs.config1()
+    with MTPGpuDirect(m, 0) as gpu:
+        gpu.build_neighbors(StructureBatch.from_structures([st]))
+        off, nbr, rij, _ = gpu.get_neighbors()
+        e, f, s, _ = gpu.compute()
+    nl = oracle.neighbors(st["cell"], st["pbc"], st["positions"], cutoff)
+    assert same_lists(off, nbr, rij, nl.offsets, nl.nbr, nl.rij)
+    assert np.diff(off).max() > (256 if cutoff > 10 else 128)
+    re, _, rf, rs = oracle.efs(m, st["types"], nl)
+    assert abs(e[0] - re) < 1e-12 * max(1.0, abs(re))
+    assert np.max(np.abs(f - rf)) < 1e-9 * max(1.0, np.max(np.abs(rf)))
+    assert np.max(np.abs(s[0] - rs)) < 1e-9 * max(1.0, np.max(np.abs(rs)))
