@@ -82,8 +82,9 @@ inline DagRec make_rec(int s1, int s2, int out, unsigned flags, double c)
     return r;
 }
 
-// Record streams per graph block: 32, or 64 for graphs whose rows do not fit
-// in shared memory (those run from L2 and gain from the extra warps).
+// Record streams per graph block: 32 or 64 (16 warps, the planner's choice
+// unless the 64-stream program pads more than 10% extra record slots;
+// build_dag_plan in plan.cpp).
 constexpr int DAG_STREAMS = 32;
 constexpr int DAG_STREAMS_LARGE = 64;
 constexpr int DAG_STREAMS_MAX = 64;

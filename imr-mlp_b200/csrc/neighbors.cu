@@ -121,7 +121,7 @@ __global__ void k_fill_cells(int natoms, const int *__restrict__ cell_of,
     cell_atoms[cell_start[c] + atomicAdd(cell_cursor + c, 1)] = i;
 }
 
-// insertion sort of small segments (atoms of a cell, in-edges of an atom)
+// insertion sort of small segments (the atoms of a cell, about ten each)
 __global__ void k_sort_segments(int nseg, const int *__restrict__ start, int *__restrict__ data)
 {
     const int s = blockIdx.x * blockDim.x + threadIdx.x;
