@@ -474,6 +474,21 @@ def train_flops(model, edges_per_atom, records):
             "radial_per_atom": (4 * R + 4 * R * nmu) * edges_per_atom}
 
 
+def train_ref_flops(model, edges, atoms, configs_count):
+    """Reference-formulation FLOPs of one loss-and-gradient pass (the survey's
+    count: per atom n_e (64 + 4 mu R + 4 nu_max + 1 + 38 nb + 24) + 11 T + 2 S
+    + 1 for EFS and n_e (23 nb + 29 + 4 mu R) + 15 T + 3 S + 1 for the
+    gradient, 12 N + 40 per configuration for the loss), for this rank."""
+    R, mu = model.rb_size, model.radial_func_count
+    nb, T, S = (model.alpha_index_basic_count, model.alpha_index_times_count,
+                model.alpha_scalar_moments)
+    numax = max(v for v in model.basis_shape() if v >= 0)
+    ne = edges / max(atoms, 1)
+    per_atom = (ne * (16 + 8 * (R - 2) + 4 * mu * R + 4 * numax + 1 + 38 * nb + 24)
+                + 11 * T + 2 * S + 1 + ne * (23 * nb + 29 + 4 * mu * R) + 15 * T + 3 * S + 1)
+    return per_atom * atoms + 12 * atoms + 40 * configs_count
+
+
 def run_train(args, torch, dist, ws, rank, local, dev, stream):
     """Training leg on every rank; returns the JSON object on rank 0."""
     from mtpb200 import MTPGpuDirect, StructureBatch
@@ -571,7 +586,17 @@ def run_train(args, torch, dist, ws, rank, local, dev, stream):
                       "edge_records": float(tms[4]), "radial_reduce": float(tms[5])},
         "gpu_launches": int(launches),
         "roofline": {"bound": "fp64", "kernel": kname, "achieved": achieved, "unit": "TFLOP/s",
-                     "flops_per_atom": kflops},
+                     "flops_per_atom": kflops,
+                     # the dual graph reads two (value, tangent) operand pairs,
+                     # 32 B, per real record and atom from its L2-resident rows
+                     "dual_graph_operands": {
+                         "bytes_per_atom": 32.0 * recs,
+                         "achieved_tb_s": 32.0 * recs * N / (tms[3] / 1e3) / 1e12,
+                         "peak": None,
+                         "note": "L1/L2 operand read rate; no measured L2 figure"}},
+        # rank 0 GPU: its shard's reference-formulation FLOPs over the pass time
+        "step_tflops_ref_formulation": train_ref_flops(student, edges, N, len(mine))
+        / (ms / args.train_steps / 1e3) / 1e12,
         "e2e": e2e,
     }
     return res, (student, sts, (te, tf, ts))
