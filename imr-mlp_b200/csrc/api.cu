@@ -686,9 +686,9 @@ int mtpb_build_neighbors(mtpb_context *c, const mtpb_structures *in, int memory)
     c->edge_epoch++;
     c->nb_built_this_call = true;
     // struct ids, wrap/bin, 3 scans (2 kernels each), cell fill, sort and
-    // position gather, count, fill, in-edge count, fill and sort, edge species
-    // pairs
-    c->pending_launches = 18;
+    // position gather, count, fill, position packing and displacements,
+    // in-edge count, fill and sort, edge species pairs
+    c->pending_launches = 20;
     return MTPB_OK;
 }
 

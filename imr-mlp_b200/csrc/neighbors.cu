@@ -304,12 +304,9 @@ __global__ void k_neighbors(int natoms, const NbStruct *__restrict__ structs,
                     }
                     const double dsq = dadd(dadd(dmul(r0, r0), dmul(r1, r1)), dmul(r2, r2));
                     if (dsq < st.cutsq) {
-                        if (FILL) {
+                        if (FILL) {   // displacements: k_refresh_edges after this pass
                             nbr[out] = o;
                             shift_code[out] = (s0 + 128) | ((s1 + 128) << 8) | ((s2 + 128) << 16);
-                            rx[out] = r0;
-                            ry[out] = r1;
-                            rz[out] = r2;
                             center[out] = i;
                             ++out;
                         } else {
@@ -389,6 +386,20 @@ __global__ void k_unwrapped(int natoms, const double *__restrict__ wx,
     double2 *q = reinterpret_cast<double2 *>(p + 4 * (size_t)a);
     q[0] = make_double2(v0, v1);
     q[1] = make_double2(v2, 0.0);
+}
+
+// Wrapped positions as [atom][4] rows for k_refresh_edges, which then
+// reproduces the build's displacement arithmetic edge by edge.
+__global__ void k_pack_positions(int natoms, const double *__restrict__ wx,
+                                 const double *__restrict__ wy, const double *__restrict__ wz,
+                                 double *__restrict__ p)
+{
+    const int a = blockIdx.x * blockDim.x + threadIdx.x;
+    if (a >= natoms)
+        return;
+    double2 *q = reinterpret_cast<double2 *>(p + 4 * (size_t)a);
+    q[0] = make_double2(wx[a], wy[a]);
+    q[1] = make_double2(wz[a], 0.0);
 }
 
 __global__ void k_refresh_edges(long nedges, const NbStruct *__restrict__ structs,
@@ -526,6 +537,17 @@ cudaError_t build_neighbors(const NbBuildInput &in, DeviceArena &arena, NbResult
             NC, in.structs, struct_of, wx, wy, wz, xs, ys, zs, cell_of, cell_start, cell_atoms,
             nullptr, offsets, nbr, shift, rx, ry, rz, center);
     CK(cudaGetLastError());
+    // displacements edge-parallel from the wrapped positions (coalesced
+    // stores; the same operations as the candidate test of the fill pass)
+    double *packed = arena.get<double>("nb_packed", 4 * (size_t)N + 4);
+    if (!packed)
+        return cudaErrorMemoryAllocation;
+    if (E > 0) {
+        k_pack_positions<<<nblk(N, T), T, 0, s>>>(N, wx, wy, wz, packed);
+        k_refresh_edges<<<nblk(E, 256), 256, 0, s>>>(E, in.structs, struct_of, center, nbr, shift,
+                                                     packed, rx, ry, rz);
+        CK(cudaGetLastError());
+    }
     res.center = center;
     res.nbr = nbr;
     res.shift = shift;
