@@ -578,9 +578,9 @@ __device__ __forceinline__ void dag_segment(unsigned rec_addr, const Rows<GR> &r
             const unsigned out = outf & DEV_OUT_MASK;
             if (!FWD && (outf & DEV_GLOBAL)) {
                 if (atom_a < natoms)
-                    adjoint[(size_t)out * npad + atom_a] = acc[0];
+                    __stcs(adjoint + (size_t)out * npad + atom_a, acc[0]);   // streamed out
                 if (atom_a + 1 < natoms)
-                    adjoint[(size_t)out * npad + atom_a + 1] = acc[1];
+                    __stcs(adjoint + (size_t)out * npad + atom_a + 1, acc[1]);
             } else {
                 rowsA.st(out, acc[0], acc[1]);
             }
@@ -720,7 +720,7 @@ __global__ void __launch_bounds__(DagGeom<ATOMS, STREAMS>::THREADS)
             const double *src = basic + (size_t)sl * npad + atom0 + a;
             if constexpr (GR)
                 *reinterpret_cast<double2 *>(rows + (size_t)sl * ATOMS + a) =
-                    *reinterpret_cast<const double2 *>(src);
+                    __ldcs(reinterpret_cast<const double2 *>(src));   // read once
             else
                 cp_async16(rows_u32 + (unsigned)(sl * ATOMS + a) * 8, src);
         }

@@ -588,7 +588,7 @@ __device__ __forceinline__ void dag_grad_segment(unsigned rec_addr, const Rows<G
             const unsigned out = outf & DEV_OUT_MASK;
             if (!FWD && (outf & DEV_GLOBAL)) {
                 if (valid)
-                    adjoint2[(size_t)out * npad + atom] = accd;
+                    __stcs(adjoint2 + (size_t)out * npad + atom, accd);   // streamed out
             } else {
                 rowA.st(out, acc, accd);
             }
@@ -723,8 +723,8 @@ __global__ void __launch_bounds__(DagGradGeomT<STREAMS>::THREADS)
             const int atom = atom0 + a;
             double v = 0.0, t = 0.0;
             if (atom < natoms) {
-                v = basic[(size_t)sl * npad + atom];
-                t = tangent[(size_t)sl * npad + atom];
+                v = __ldcs(basic + (size_t)sl * npad + atom);   // read once: keep the
+                t = __ldcs(tangent + (size_t)sl * npad + atom);   // L2 for the row slices
             }
             rows[(size_t)(sl * G::ATOMS + a) * 2] = v;
             rows[(size_t)(sl * G::ATOMS + a) * 2 + 1] = t;
