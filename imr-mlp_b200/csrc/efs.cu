@@ -140,18 +140,30 @@ __device__ __forceinline__ void stage_chunk(const EdgeArgs &p, const StageView &
     }
 }
 
+// Partition members of warp W0 when NW members are shared by NW / SUB warps:
+// W0, W0 + NW / SUB, ... (strided, which balances the warps' register counts
+// better than consecutive members).  Accumulator base of the warp's s-th
+// member in its register array; s = SUB gives the array's size.
+template <class S, int NW, int W0, int SUB> constexpr int sub_base(int s)
+{
+    int b = 0;
+    for (int i = 0; i < s; ++i)
+        b += Partition<S, NW>::table.nacc[i * (NW / SUB) + W0];
+    return b;
+}
+
 // ----------------------------------------------------------------------------
-// Forward: basic moments of 32 atoms; warp W owns the chains of Partition.
+// Forward: basic moments of 32 atoms (lane = atom).  NW is the size of the
+// chain partition; the warp runs its SUB members (sub_base) one after the
+// other over each chunk's edges (one pass per member keeps the
+// unrolled per-edge code small).
 // ----------------------------------------------------------------------------
-template <class S, int NW, int W, bool RG>
+template <class S, int NW, int W0, int SUB, bool RG>
 __device__ __forceinline__ void fwd_warp(const EdgeArgs &p, const StageView &v, int atom0,
                                          int maxdeg, double *basic)
 {
     using P = Partition<S, NW>;
-    constexpr int NACC = P::table.nacc[W];
-    constexpr int NCHW = P::table.count[W];
-    constexpr int MAXB = P::table.maxb[W];
-    constexpr int MAXC = P::table.maxc[W];
+    constexpr int NACC = sub_base<S, NW, W0, SUB>(SUB);
     constexpr int NMU = S::NMU;
     const int lane = threadIdx.x & 31;
     double acc[NACC > 0 ? NACC : 1];
@@ -160,99 +172,200 @@ __device__ __forceinline__ void fwd_warp(const EdgeArgs &p, const StageView &v, 
         acc[i] = 0.0;
     const int nchunks = (maxdeg + KS - 1) / KS;
     for (int ch = 0; ch < nchunks; ++ch) {
-        stage_chunk<S, NW, false, RG>(p, v, atom0, ch);
+        stage_chunk<S, NW / SUB, false, RG>(p, v, atom0, ch);
         __syncthreads();
         const int kend = min(KS, maxdeg - ch * KS);
-        for (int k = 0; k < kend; ++k) {
-            const double xh = SV(v.st, 0, k, lane);
-            const double yh = SV(v.st, 1, k, lane);
-            const double zh = SV(v.st, 2, k, lane);
-            double f[NMU];
+        static_for<SUB>([&](auto is) {
+            constexpr int W = decltype(is)::value * (NW / SUB) + W0;
+            constexpr int BASE = sub_base<S, NW, W0, SUB>(decltype(is)::value);
+            constexpr int NCHW = P::table.count[W];
+            constexpr int MAXB = P::table.maxb[W];
+            constexpr int MAXC = P::table.maxc[W];
+            for (int k = 0; k < kend; ++k) {
+                const double xh = SV(v.st, 0, k, lane);
+                const double yh = SV(v.st, 1, k, lane);
+                const double zh = SV(v.st, 2, k, lane);
+                double f[NMU];
 #pragma unroll
-            for (int m = 0; m < NMU; ++m)
-                f[m] = SV(v.st, 4 + m, k, lane);
-            double yp[MAXB + 1], zp[MAXC + 1];
-            yp[0] = 1.0;
-            zp[0] = 1.0;
+                for (int m = 0; m < NMU; ++m)
+                    f[m] = SV(v.st, 4 + m, k, lane);
+                double yp[MAXB + 1], zp[MAXC + 1];
+                yp[0] = 1.0;
+                zp[0] = 1.0;
 #pragma unroll
-            for (int i = 1; i <= MAXB; ++i)
-                yp[i] = yp[i - 1] * yh;
+                for (int i = 1; i <= MAXB; ++i)
+                    yp[i] = yp[i - 1] * yh;
 #pragma unroll
-            for (int i = 1; i <= MAXC; ++i)
-                zp[i] = zp[i - 1] * zh;
-            static_for<NCHW>([&](auto ii) {
-                constexpr int ci = P::table.list[W * S::NCH + decltype(ii)::value];
-                constexpr int a0 = P::table.acc0[W * S::NCH + decltype(ii)::value];
-                constexpr int b = S::chains.b[ci];
-                constexpr int c = S::chains.c[ci];
-                constexpr int L = S::chains.len[ci];
-                double u;
-                if constexpr (b == 0 && c == 0)
-                    u = 1.0;
-                else if constexpr (b == 0)
-                    u = zp[c];
-                else if constexpr (c == 0)
-                    u = yp[b];
-                else
-                    u = yp[b] * zp[c];
-                static_for<L>([&](auto ia) {
-                    constexpr int a = decltype(ia)::value;
-                    constexpr int nu = a + b + c;
-                    constexpr int off = a0 + chain_acc_off<S>(b + c, a);
-                    static_for<S::cnt(nu)>([&](auto iq) {
-                        constexpr int q = decltype(iq)::value;
-                        acc[off + q] = fma(f[S::chan(nu, q)], u, acc[off + q]);
+                for (int i = 1; i <= MAXC; ++i)
+                    zp[i] = zp[i - 1] * zh;
+                static_for<NCHW>([&](auto ii) {
+                    constexpr int ci = P::table.list[W * S::NCH + decltype(ii)::value];
+                    constexpr int a0 = BASE + P::table.acc0[W * S::NCH + decltype(ii)::value];
+                    constexpr int b = S::chains.b[ci];
+                    constexpr int c = S::chains.c[ci];
+                    constexpr int L = S::chains.len[ci];
+                    double u;
+                    if constexpr (b == 0 && c == 0)
+                        u = 1.0;
+                    else if constexpr (b == 0)
+                        u = zp[c];
+                    else if constexpr (c == 0)
+                        u = yp[b];
+                    else
+                        u = yp[b] * zp[c];
+                    static_for<L>([&](auto ia) {
+                        constexpr int a = decltype(ia)::value;
+                        constexpr int nu = a + b + c;
+                        constexpr int off = a0 + chain_acc_off<S>(b + c, a);
+                        static_for<S::cnt(nu)>([&](auto iq) {
+                            constexpr int q = decltype(iq)::value;
+                            acc[off + q] = fma(f[S::chan(nu, q)], u, acc[off + q]);
+                        });
+                        if constexpr (a + 1 < L)
+                            u *= xh;
                     });
-                    if constexpr (a + 1 < L)
-                        u *= xh;
                 });
-            });
-        }
+            }
+        });
         __syncthreads();
     }
     const int atom = atom0 + lane;
     if (atom < p.natoms) {
-        static_for<NCHW>([&](auto ii) {
-            constexpr int ci = P::table.list[W * S::NCH + decltype(ii)::value];
-            constexpr int a0 = P::table.acc0[W * S::NCH + decltype(ii)::value];
-            constexpr int n = S::chains.nacc[ci];
-            constexpr int slot0 = S::chains.slot0[ci];
+        static_for<SUB>([&](auto is) {
+            constexpr int W = decltype(is)::value * (NW / SUB) + W0;
+            constexpr int BASE = sub_base<S, NW, W0, SUB>(decltype(is)::value);
+            static_for<P::table.count[W]>([&](auto ii) {
+                constexpr int ci = P::table.list[W * S::NCH + decltype(ii)::value];
+                constexpr int a0 = BASE + P::table.acc0[W * S::NCH + decltype(ii)::value];
+                constexpr int n = S::chains.nacc[ci];
+                constexpr int slot0 = S::chains.slot0[ci];
 #pragma unroll
-            for (int i = 0; i < n; ++i)
-                basic[(size_t)(slot0 + i) * p.npad + atom] = acc[a0 + i];
+                for (int i = 0; i < n; ++i)
+                    basic[(size_t)(slot0 + i) * p.npad + atom] = acc[a0 + i];
+            });
         });
     }
+}
+
+// One staged edge's share of the chains of partition member W (adjoints at
+// adj[BASE..]): the partial dE/dr_j of the file header's formula.
+template <class S, int NW, int W, int BASE, int NA>
+__device__ __forceinline__ void rev_edge(const StageView &v, int k, int lane,
+                                         const double (&adj)[NA], double &ox, double &oy,
+                                         double &oz)
+{
+    using P = Partition<S, NW>;
+    constexpr int NCHW = P::table.count[W];
+    constexpr int MAXB = P::table.maxb[W];
+    constexpr int MAXC = P::table.maxc[W];
+    constexpr int NMU = S::NMU;
+    const double xh = SV(v.st, 0, k, lane);
+    const double yh = SV(v.st, 1, k, lane);
+    const double zh = SV(v.st, 2, k, lane);
+    const double rinv = SV(v.st, 3, k, lane);
+    double f[NMU], fp[NMU];
+#pragma unroll
+    for (int m = 0; m < NMU; ++m) {
+        f[m] = SV(v.st, 4 + m, k, lane);
+        fp[m] = SV(v.st, 4 + NMU + m, k, lane);
+    }
+    double yp[MAXB + 1], zp[MAXC + 1];
+    yp[0] = 1.0;
+    zp[0] = 1.0;
+#pragma unroll
+    for (int i = 1; i <= MAXB; ++i)
+        yp[i] = yp[i - 1] * yh;
+#pragma unroll
+    for (int i = 1; i <= MAXC; ++i)
+        zp[i] = zp[i - 1] * zh;
+    double V = 0.0, H = 0.0, Gx = 0.0, Gy = 0.0, Gz = 0.0;
+    static_for<NCHW>([&](auto ii) {
+        constexpr int ci = P::table.list[W * S::NCH + decltype(ii)::value];
+        constexpr int a0 = BASE + P::table.acc0[W * S::NCH + decltype(ii)::value];
+        constexpr int b = S::chains.b[ci];
+        constexpr int c = S::chains.c[ci];
+        constexpr int L = S::chains.len[ci];
+        double h0 = 0.0, h1 = 0.0, g0 = 0.0;
+        static_for<L>([&](auto ia) {
+            constexpr int a = L - 1 - decltype(ia)::value;
+            constexpr int nu = a + b + c;
+            constexpr int off = a0 + chain_acc_off<S>(b + c, a);
+            double Pv = adj[off] * f[S::chan(nu, 0)];
+            double Pd = adj[off] * fp[S::chan(nu, 0)];
+            static_for<S::cnt(nu) - 1>([&](auto iq) {
+                constexpr int q = decltype(iq)::value + 1;
+                Pv = fma(adj[off + q], f[S::chan(nu, q)], Pv);
+                Pd = fma(adj[off + q], fp[S::chan(nu, q)], Pd);
+            });
+            if constexpr (a == L - 1) {
+                h0 = Pv;
+                g0 = Pd;
+            } else {
+                h1 = fma(h1, xh, h0);
+                h0 = fma(h0, xh, Pv);
+                g0 = fma(g0, xh, Pd);
+            }
+        });
+        double q;
+        if constexpr (b == 0 && c == 0)
+            q = 1.0;
+        else if constexpr (b == 0)
+            q = zp[c];
+        else if constexpr (c == 0)
+            q = yp[b];
+        else
+            q = yp[b] * zp[c];
+        V = fma(q, g0, V);
+        Gx = fma(q, h1, Gx);
+        if constexpr (b > 0) {
+            double qy = (c == 0) ? yp[b - 1] : yp[b - 1] * zp[c];
+            Gy = fma(double(b) * qy, h0, Gy);
+        }
+        if constexpr (c > 0) {
+            double qz = (b == 0) ? zp[c - 1] : yp[b] * zp[c - 1];
+            Gz = fma(double(c) * qz, h0, Gz);
+        }
+        H = fma(q, fma(xh, h1, double(b + c) * h0), H);
+    });
+    const double t = V - H * rinv;
+    ox = fma(xh, t, Gx * rinv);
+    oy = fma(yh, t, Gy * rinv);
+    oz = fma(zh, t, Gz * rinv);
 }
 
 // ----------------------------------------------------------------------------
 // Reverse: per-edge dE_i/dr_ij of 32 atoms.  Each warp adds its chains'
 // share; the shares are summed in fixed warp order (deterministic).  NW is
-// the size of the chain partition, W the warp's index in it and NWB the warps
-// of this block; the first part stores the sums, later parts add to them.
+// the size of the chain partition; the warp runs its SUB members (sub_base)
+// one after the other over each chunk's edges (one pass
+// per member, so that the unrolled code run per edge stays small: a long
+// per-edge body stalls on instruction fetch), adding their shares in member
+// order.  NWB is the warps of this block; the first part stores the sums,
+// later parts add to them.
 // ----------------------------------------------------------------------------
-template <class S, int NW, int W, int NWB, bool FIRST, bool RG>
+template <class S, int NW, int W0, int SUB, int NWB, bool FIRST, bool RG>
 __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, int atom0,
                                          int maxdeg, const double *adjoint, double *dx,
                                          double *dy, double *dz)
 {
     using P = Partition<S, NW>;
-    constexpr int NACC = P::table.nacc[W];
-    constexpr int NCHW = P::table.count[W];
-    constexpr int MAXB = P::table.maxb[W];
-    constexpr int MAXC = P::table.maxc[W];
-    constexpr int NMU = S::NMU;
+    constexpr int NACC = sub_base<S, NW, W0, SUB>(SUB);
     const int lane = threadIdx.x & 31;
     const int atom = atom0 + lane;
     double adj[NACC > 0 ? NACC : 1];
     if (atom < p.natoms) {
-        static_for<NCHW>([&](auto ii) {
-            constexpr int ci = P::table.list[W * S::NCH + decltype(ii)::value];
-            constexpr int a0 = P::table.acc0[W * S::NCH + decltype(ii)::value];
-            constexpr int n = S::chains.nacc[ci];
-            constexpr int slot0 = S::chains.slot0[ci];
+        static_for<SUB>([&](auto is) {
+            constexpr int W = decltype(is)::value * (NW / SUB) + W0;
+            constexpr int BASE = sub_base<S, NW, W0, SUB>(decltype(is)::value);
+            static_for<P::table.count[W]>([&](auto ii) {
+                constexpr int ci = P::table.list[W * S::NCH + decltype(ii)::value];
+                constexpr int a0 = BASE + P::table.acc0[W * S::NCH + decltype(ii)::value];
+                constexpr int n = S::chains.nacc[ci];
+                constexpr int slot0 = S::chains.slot0[ci];
 #pragma unroll
-            for (int i = 0; i < n; ++i)
-                adj[a0 + i] = __ldg(adjoint + (size_t)(slot0 + i) * p.npad + atom);
+                for (int i = 0; i < n; ++i)
+                    adj[a0 + i] = __ldg(adjoint + (size_t)(slot0 + i) * p.npad + atom);
+            });
         });
     } else {
 #pragma unroll
@@ -260,85 +373,32 @@ __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, 
             adj[i] = 0.0;
     }
     const int nchunks = (maxdeg + KS - 1) / KS;
+    double *part = v.part + (size_t)(W0 % NWB) * 3 * KS * 32;
     for (int ch = 0; ch < nchunks; ++ch) {
-        stage_chunk<S, NW, true, RG>(p, v, atom0, ch);
+        stage_chunk<S, NW / SUB, true, RG>(p, v, atom0, ch);
         __syncthreads();
         const int kend = min(KS, maxdeg - ch * KS);
-        for (int k = 0; k < kend; ++k) {
-            const double xh = SV(v.st, 0, k, lane);
-            const double yh = SV(v.st, 1, k, lane);
-            const double zh = SV(v.st, 2, k, lane);
-            const double rinv = SV(v.st, 3, k, lane);
-            double f[NMU], fp[NMU];
-#pragma unroll
-            for (int m = 0; m < NMU; ++m) {
-                f[m] = SV(v.st, 4 + m, k, lane);
-                fp[m] = SV(v.st, 4 + NMU + m, k, lane);
+        static_for<SUB>([&](auto is) {
+            constexpr int s = decltype(is)::value;
+            constexpr int W = s * (NW / SUB) + W0;
+            constexpr int BASE = sub_base<S, NW, W0, SUB>(s);
+            for (int k = 0; k < kend; ++k) {
+                double ox, oy, oz;
+                rev_edge<S, NW, W, BASE>(v, k, lane, adj, ox, oy, oz);
+                double *px = part + (0 * KS + k) * 32 + lane;
+                double *py = part + (1 * KS + k) * 32 + lane;
+                double *pz = part + (2 * KS + k) * 32 + lane;
+                if constexpr (s == 0) {
+                    *px = ox;
+                    *py = oy;
+                    *pz = oz;
+                } else {
+                    *px += ox;
+                    *py += oy;
+                    *pz += oz;
+                }
             }
-            double yp[MAXB + 1], zp[MAXC + 1];
-            yp[0] = 1.0;
-            zp[0] = 1.0;
-#pragma unroll
-            for (int i = 1; i <= MAXB; ++i)
-                yp[i] = yp[i - 1] * yh;
-#pragma unroll
-            for (int i = 1; i <= MAXC; ++i)
-                zp[i] = zp[i - 1] * zh;
-            double V = 0.0, H = 0.0, Gx = 0.0, Gy = 0.0, Gz = 0.0;
-            static_for<NCHW>([&](auto ii) {
-                constexpr int ci = P::table.list[W * S::NCH + decltype(ii)::value];
-                constexpr int a0 = P::table.acc0[W * S::NCH + decltype(ii)::value];
-                constexpr int b = S::chains.b[ci];
-                constexpr int c = S::chains.c[ci];
-                constexpr int L = S::chains.len[ci];
-                double h0 = 0.0, h1 = 0.0, g0 = 0.0;
-                static_for<L>([&](auto ia) {
-                    constexpr int a = L - 1 - decltype(ia)::value;
-                    constexpr int nu = a + b + c;
-                    constexpr int off = a0 + chain_acc_off<S>(b + c, a);
-                    double Pv = adj[off] * f[S::chan(nu, 0)];
-                    double Pd = adj[off] * fp[S::chan(nu, 0)];
-                    static_for<S::cnt(nu) - 1>([&](auto iq) {
-                        constexpr int q = decltype(iq)::value + 1;
-                        Pv = fma(adj[off + q], f[S::chan(nu, q)], Pv);
-                        Pd = fma(adj[off + q], fp[S::chan(nu, q)], Pd);
-                    });
-                    if constexpr (a == L - 1) {
-                        h0 = Pv;
-                        g0 = Pd;
-                    } else {
-                        h1 = fma(h1, xh, h0);
-                        h0 = fma(h0, xh, Pv);
-                        g0 = fma(g0, xh, Pd);
-                    }
-                });
-                double q;
-                if constexpr (b == 0 && c == 0)
-                    q = 1.0;
-                else if constexpr (b == 0)
-                    q = zp[c];
-                else if constexpr (c == 0)
-                    q = yp[b];
-                else
-                    q = yp[b] * zp[c];
-                V = fma(q, g0, V);
-                Gx = fma(q, h1, Gx);
-                if constexpr (b > 0) {
-                    double qy = (c == 0) ? yp[b - 1] : yp[b - 1] * zp[c];
-                    Gy = fma(double(b) * qy, h0, Gy);
-                }
-                if constexpr (c > 0) {
-                    double qz = (b == 0) ? zp[c - 1] : yp[b] * zp[c - 1];
-                    Gz = fma(double(c) * qz, h0, Gz);
-                }
-                H = fma(q, fma(xh, h1, double(b + c) * h0), H);
-            });
-            const double t = V - H * rinv;
-            double *part = v.part + (size_t)(W % NWB) * 3 * KS * 32;
-            part[(0 * KS + k) * 32 + lane] = fma(xh, t, Gx * rinv);
-            part[(1 * KS + k) * 32 + lane] = fma(yh, t, Gy * rinv);
-            part[(2 * KS + k) * 32 + lane] = fma(zh, t, Gz * rinv);
-        }
+        });
         __syncthreads();
         // sum the warps' shares in warp order and store per edge (thread ->
         // (slot, lane) so that the shared reads are lane-contiguous)
@@ -408,14 +468,16 @@ __global__ void __launch_bounds__(ShapeCfg<S>::NW * 32, KCfg<S, REV>::BLOCKS)
     const int maxdeg = __ldg(p.group_maxdeg + group);
     const int warp = threadIdx.x >> 5;
     constexpr int NWT = NW * KCfg<S, REV>::NPART;
+    constexpr int SUB = KCfg<S, REV>::SUB;
     static_for<NW>([&](auto iw) {
         constexpr int WL = decltype(iw)::value;
         constexpr int W = PART * NW + WL;
         if (warp == WL) {
             if constexpr (REV)
-                rev_warp<S, NWT, W, NW, PART == 0, RG>(p, v, atom0, maxdeg, adjoint, dx, dy, dz);
+                rev_warp<S, NWT * SUB, W, SUB, NW, PART == 0, RG>(p, v, atom0, maxdeg, adjoint,
+                                                                  dx, dy, dz);
             else
-                fwd_warp<S, NWT, W, RG>(p, v, atom0, maxdeg, basic);
+                fwd_warp<S, NWT * SUB, W, SUB, RG>(p, v, atom0, maxdeg, basic);
         }
     });
 }

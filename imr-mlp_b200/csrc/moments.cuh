@@ -16,23 +16,28 @@ constexpr int STR = 36;   // row stride of the staging arrays (doubles): conflic
 // same unrolled chain code (8 or 12 different bodies per SM thrashed the
 // instruction cache).
 template <class S> struct ShapeCfg;
-template <> struct ShapeCfg<ShapeS1> { static constexpr int NW = 2, NPART = 1, NPART_REV = 1; };
-template <> struct ShapeCfg<ShapeS2> { static constexpr int NW = 2, NPART = 1, NPART_REV = 1; };
-template <> struct ShapeCfg<ShapeL16> { static constexpr int NW = 4, NPART = 1, NPART_REV = 1; };
+template <> struct ShapeCfg<ShapeS1> { static constexpr int NW = 2, NPART = 1, NPART_REV = 1, SUB = 1, SUB_REV = 1; };
+template <> struct ShapeCfg<ShapeS2> { static constexpr int NW = 2, NPART = 1, NPART_REV = 1, SUB = 1, SUB_REV = 1; };
+template <> struct ShapeCfg<ShapeL16> { static constexpr int NW = 4, NPART = 1, NPART_REV = 1, SUB = 1, SUB_REV = 1; };
 // level 20: one launch each way (a reverse split over 8 warps in two launches
-// measured slower: 15.3 ms against 14.2 ms on the 1M-atom box)
-template <> struct ShapeCfg<ShapeL20> { static constexpr int NW = 4, NPART = 1, NPART_REV = 1; };
+// measured slower: 15.3 ms against 14.2 ms on the 1M-atom box); the reverse
+// chains are partitioned 16 ways and every warp runs four members in turn
+// (reverse 14.4 -> 10.2 ms; 2 / 6 / 8 members: 12.0 / 12.5 / 12.1 ms; more
+// than one member per warp in the forward kernel was slower)
+template <> struct ShapeCfg<ShapeL20> { static constexpr int NW = 4, NPART = 1, NPART_REV = 1, SUB = 1, SUB_REV = 4; };
 // level 24: the chains are partitioned over 12 warps (register budget) and
 // run as three launches ("parts") of 4 warps, three blocks per SM, so that
-// every scheduler still runs a single unrolled body
-template <> struct ShapeCfg<ShapeL24> { static constexpr int NW = 4, NPART = 3, NPART_REV = 3; };
-template <> struct ShapeCfg<ShapePS> { static constexpr int NW = 4, NPART = 1, NPART_REV = 1; };
+// every scheduler still runs a single unrolled body; the reverse partition
+// has 24 members, two per warp
+template <> struct ShapeCfg<ShapeL24> { static constexpr int NW = 4, NPART = 3, NPART_REV = 3, SUB = 1, SUB_REV = 2; };
+template <> struct ShapeCfg<ShapePS> { static constexpr int NW = 4, NPART = 1, NPART_REV = 1, SUB = 1, SUB_REV = 1; };
 
-// launches ("parts") and blocks per SM of the forward (REV false) and reverse
-// kernels
+// launches ("parts"), partition members per warp and blocks per SM of the
+// forward (REV false) and reverse kernels
 template <class S, bool REV> struct KCfg {
     static constexpr int NW = ShapeCfg<S>::NW;
     static constexpr int NPART = REV ? ShapeCfg<S>::NPART_REV : ShapeCfg<S>::NPART;
+    static constexpr int SUB = REV ? ShapeCfg<S>::SUB_REV : ShapeCfg<S>::SUB;   // members per warp
     static constexpr int BLOCKS = NW > 4 ? 1 : NPART > 1 ? 3 : 2;
 };
 
