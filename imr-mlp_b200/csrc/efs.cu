@@ -140,18 +140,6 @@ __device__ __forceinline__ void stage_chunk(const EdgeArgs &p, const StageView &
     }
 }
 
-// Partition members of warp W0 when NW members are shared by NW / SUB warps:
-// W0, W0 + NW / SUB, ... (strided, which balances the warps' register counts
-// better than consecutive members).  Accumulator base of the warp's s-th
-// member in its register array; s = SUB gives the array's size.
-template <class S, int NW, int W0, int SUB> constexpr int sub_base(int s)
-{
-    int b = 0;
-    for (int i = 0; i < s; ++i)
-        b += Partition<S, NW>::table.nacc[i * (NW / SUB) + W0];
-    return b;
-}
-
 // ----------------------------------------------------------------------------
 // Forward: basic moments of 32 atoms (lane = atom).  NW is the size of the
 // chain partition; the warp runs its SUB members (sub_base) one after the

@@ -46,6 +46,18 @@ __device__ __forceinline__ double &SV(double *st, int row, int k, int lane)
     return st[(row * KS + k) * STR + lane];
 }
 
+// Partition members of warp W0 when NW members are shared by NW / SUB warps:
+// W0, W0 + NW / SUB, ... (strided, which balances the warps' register counts
+// better than consecutive members).  Accumulator base of the warp's s-th
+// member in its register array; s = SUB gives the array's size.
+template <class S, int NW, int W0, int SUB> constexpr int sub_base(int s)
+{
+    int b = 0;
+    for (int i = 0; i < s; ++i)
+        b += Partition<S, NW>::table.nacc[i * (NW / SUB) + W0];
+    return b;
+}
+
 // accumulator offset of monomial a within a chain (sum of channel counts of
 // the lower powers)
 template <class S> constexpr int chain_acc_off(int s, int a)
