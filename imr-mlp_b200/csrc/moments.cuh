@@ -23,8 +23,8 @@ template <> struct ShapeCfg<ShapeL16> { static constexpr int NW = 4, NPART = 1, 
 // measured slower: 15.3 ms against 14.2 ms on the 1M-atom box); the reverse
 // chains are partitioned 16 ways and every warp runs four members in turn
 // (reverse 14.4 -> 10.2 ms; 2 / 3 / 5 / 6 / 8 members: 12.0 / 10.2 / 11.4 /
-// 12.5 / 12.1 ms; more
-// than one member per warp in the forward kernel was slower)
+// 12.5 / 12.1 ms; more than one member per warp in the forward kernel was
+// slower)
 template <> struct ShapeCfg<ShapeL20> { static constexpr int NW = 4, NPART = 1, NPART_REV = 1, SUB = 1, SUB_REV = 4; };
 // level 24: the chains are partitioned over 12 warps (register budget) and
 // run as three launches ("parts") of 4 warps, three blocks per SM, so that
