@@ -1026,4 +1026,11 @@ int mtpb_loss_grad(mtpb_context *c, const mtpb_labels *labels, const mtpb_loss_w
     return loss_grad_compute(c, labels, w, norm_count, memory, loss, metrics, grad);
 }
 
+int mtpb_check_training_values(mtpb_context *c, long *first_nonfinite)
+{
+    if (!c || !first_nonfinite)
+        return fail(MTPB_ERR_ARGUMENT, "NULL argument");
+    return training_values_status(c, first_nonfinite);
+}
+
 } // extern "C"

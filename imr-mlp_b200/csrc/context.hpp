@@ -28,8 +28,12 @@ struct TrainingState {
     long *bounds = nullptr;           // bucket start positions [K*K+2]
     cudaEvent_t ev[7] = {};           // timing events of the last call
     bool ev_valid = false;
+    int *nonfinite = nullptr;         // finite check of the last call's outputs
 };
 int upload_training_program(mtpb_context *c);
+// Reads the finite check of the last mtpb_loss_grad call (synchronises the
+// context stream); first_bad = -1 when every value was finite.
+int training_values_status(mtpb_context *c, long *first_bad);
 
 int fail(int status, const std::string &msg);
 int cuda_fail(cudaError_t e, const char *where);

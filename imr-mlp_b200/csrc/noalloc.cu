@@ -46,7 +46,8 @@ constexpr size_t NA_VROWS = NA_FORCE + al256(24ull * NOALLOC_MAX_ATOMS);
 constexpr size_t NA_SEGS = NA_VROWS + al256(72ull * NOALLOC_MAX_ATOMS);
 constexpr size_t NA_PARTIALS = NA_SEGS + al256(4ull * (2 * NOALLOC_MAX_SEGMENTS + 2));
 constexpr size_t NA_SUMS = NA_PARTIALS + al256(80ull * NOALLOC_MAX_SEGMENTS);
-constexpr size_t NA_TOTAL = NA_SUMS + al256(8ull * 20);
+constexpr size_t NA_CHECK = NA_SUMS + al256(8ull * 20);
+constexpr size_t NA_TOTAL = NA_CHECK + al256(4ull * 8);
 
 // The scratch array.  In host code this name is only a host-side stand-in:
 // its device address comes from cudaGetSymbolAddress (scratch_base below).
@@ -75,6 +76,50 @@ static int scratch_base(int device, unsigned char **base)
 }
 
 static inline int nblk_na(long n, int t) { return (int)((n + t - 1) / t); }
+
+// Input validation of a request, run before any kernel indexes with its
+// contents (the same checks mtpb_efs_csr makes on the host).  status[0..4]
+// start at NA_CHECK_NONE and receive the smallest offending position:
+// [0] offsets[0] != 0 (0), [1] first i with offsets[i+1] < offsets[i],
+// [2] first edge whose masked neighbour index is outside [0, ntotal),
+// [3] first atom whose type is outside [-1, K), [4] edge count above the limit;
+// status[5] = offsets[center_count].  Neighbour indices are only read when the
+// edge count is within [0, NOALLOC_MAX_EDGES] and the array is present (a
+// request without centres may pass none; its nonzero offsets[0] is reported).
+// The host clears the status words with the byte 0x7f, so "none" reads
+// 0x7f7f7f7f, larger than any index a request can hold.
+constexpr int NA_CHECK_NONE = 0x7f7f7f7f;
+
+__global__ void k_na_validate(int NC, int NT, const int *__restrict__ offsets,
+                              const int *__restrict__ nbr_in, int mask,
+                              const int *__restrict__ types, int K, int *__restrict__ status)
+{
+    const int E = offsets[NC];
+    const bool e_ok = E >= 0 && E <= NOALLOC_MAX_EDGES && (E == 0 || nbr_in);
+    const long stride = (long)gridDim.x * blockDim.x;
+    const long t0 = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t0 == 0) {
+        status[5] = E;
+        if (offsets[0] != 0)
+            atomicMin(status + 0, 0);
+        if (!e_ok)
+            atomicMin(status + 4, 0);
+    }
+    for (long i = t0; i < NC; i += stride)
+        if (offsets[i + 1] < offsets[i])
+            atomicMin(status + 1, (int)i);
+    if (e_ok)
+        for (long e = t0; e < E; e += stride) {
+            const int j = nbr_in[e] & mask;
+            if (j < 0 || j >= NT)
+                atomicMin(status + 2, (int)e);
+        }
+    for (long i = t0; i < NT; i += stride) {
+        const int t = types[i];
+        if (t < -1 || t >= K)
+            atomicMin(status + 3, (int)i);
+    }
+}
 
 __global__ void k_na_prepare(long E, const int *__restrict__ nbr_in, int mask,
                              int *__restrict__ nbr, int *__restrict__ in_count)
@@ -228,13 +273,32 @@ int noalloc_compute(mtpb_context *c, const mtpb_csr_request *r)
     if ((rc = scratch_base(c->device, &base)))
         return rc;
     cudaStream_t s = c->stream;
-    int E = 0;
-    CUDA_TRY(cudaMemcpyAsync(&E, r->offsets + NC, sizeof(int), cudaMemcpyDeviceToHost, s),
-             "read edge count");
+    c->ev_valid = false;   // no stage timings for this call
+    // validate offsets, neighbour indices and types on the device, then read
+    // the verdict and the edge count before any kernel indexes with them
+    int *check = (int *)(base + NA_CHECK);
+    CUDA_TRY(cudaMemsetAsync(check, 0x7f, sizeof(int) * 6, s), "clear check");
+    k_na_validate<<<16, 256, 0, s>>>(NC, NT, r->offsets, r->neighbors, r->neighbor_mask,
+                                     r->types, c->model.K, check);
+    CUDA_TRY(cudaGetLastError(), "validate request");
+    int hcheck[6];
+    CUDA_TRY(cudaMemcpyAsync(hcheck, check, sizeof(hcheck), cudaMemcpyDeviceToHost, s),
+             "read validation");
     CUDA_TRY(cudaStreamSynchronize(s), "sync");
-    if (E < 0 || E > NOALLOC_MAX_EDGES)
+    if (hcheck[4] != NA_CHECK_NONE)
         return fail(MTPB_ERR_ARGUMENT, "no-allocation path limit exceeded: at most " +
                                            std::to_string(NOALLOC_MAX_EDGES) + " edges");
+    if (hcheck[0] != NA_CHECK_NONE)
+        return fail(MTPB_ERR_ARGUMENT, "offsets[0] must be 0");
+    if (hcheck[1] != NA_CHECK_NONE)
+        return fail(MTPB_ERR_ARGUMENT, "offsets must be non-decreasing (at centre " +
+                                           std::to_string(hcheck[1]) + ")");
+    if (hcheck[2] != NA_CHECK_NONE)
+        return fail(MTPB_ERR_ARGUMENT, "neighbor index out of range at edge " +
+                                           std::to_string(hcheck[2]));
+    if (hcheck[3] != NA_CHECK_NONE)
+        return fail(MTPB_ERR_ARGUMENT, "type out of range at atom " + std::to_string(hcheck[3]));
+    const int E = hcheck[5];
     double *basic = (double *)(base + NA_BASIC), *adjoint = (double *)(base + NA_ADJ);
     double *rx = (double *)(base + NA_RX), *ry = (double *)(base + NA_RY),
            *rz = (double *)(base + NA_RZ);
@@ -253,7 +317,8 @@ int noalloc_compute(mtpb_context *c, const mtpb_csr_request *r)
     // the array keeps the previous call's contents: clear what accumulates
     CUDA_TRY(cudaMemsetAsync(in_count, 0, sizeof(int) * (NT + 1), s), "clear");
     CUDA_TRY(cudaMemsetAsync(cursor, 0, sizeof(int) * (NT + 1), s), "clear");
-    CUDA_TRY(cudaMemsetAsync(site_e_all, 0, sizeof(double) * (NT + 1), s), "clear");
+    if (NT)
+        CUDA_TRY(cudaMemsetAsync(site_e_all, 0, sizeof(double) * NT, s), "clear");
     if (E) {
         k_na_prepare<<<nblk_na(E, 256), 256, 0, s>>>(E, r->neighbors, r->neighbor_mask, nbr,
                                                      in_count);
@@ -320,7 +385,7 @@ int noalloc_compute(mtpb_context *c, const mtpb_csr_request *r)
     CUDA_TRY(cudaGetLastError(), "no-allocation EFS");
     // hseg lives on this host stack frame: wait for the copies before returning
     CUDA_TRY(cudaStreamSynchronize(s), "no-allocation EFS");
-    c->launches = 13;
+    c->launches = 14;
     return check_device_error(c);
 }
 

@@ -319,6 +319,17 @@ __global__ void k_assemble(int KK, int mu_total, int nmu, int R, int K, int S,
     }
 }
 
+// Finite check of [loss, metrics, gradient] (the reference's
+// training_finite_kernel, runtime/mtp/gpu-direct/mtp_gpu_direct.cu:5395-5420):
+// first_bad receives the smallest index of a NaN or infinite value (it starts
+// at INT_MAX).
+__global__ void k_finite_check(int n, const double *__restrict__ v, int *__restrict__ first_bad)
+{
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        if (!isfinite(v[i]))
+            atomicMin(first_bad, i);
+}
+
 // ---- host orchestration ------------------------------------------------------
 
 static int labels_on_device(mtpb_context *c, const mtpb_labels *labels, int memory,
@@ -509,8 +520,10 @@ int loss_grad_compute(mtpb_context *c, const mtpb_labels *labels, const mtpb_los
     const int ncoef = m.coeff_count();
     double *sums = c->arena.get<double>("train_sums", (size_t)KK * nout + NT + ne + 3);
     double *d_out = c->arena.get<double>("train_out", (size_t)ncoef + 8 + 1);
+    int *nonfinite = c->arena.get<int>("train_nonfinite", 1);
     if (!aoff || !dlde_atom || !dldf || !dlds || !terms || !wx || !wy || !wz || !tangent ||
-        !adjoint2 || !uv || !epart || !rpart || !sums || !d_out || !d_energy || !basic || !adjoint)
+        !adjoint2 || !uv || !epart || !rpart || !sums || !d_out || !d_energy || !basic || !adjoint ||
+        !nonfinite)
         return fail(MTPB_ERR_MEMORY, "device allocation for the gradient failed");
     double *rsum = sums, *tsum = sums + (size_t)KK * nout, *gsum = tsum + NT;
     CUDA_TRY(cudaMemcpyAsync(aoff, c->h_atom_offsets.data(), sizeof(int) * (S + 1),
@@ -579,7 +592,11 @@ int loss_grad_compute(mtpb_context *c, const mtpb_labels *labels, const mtpb_los
         KK, m.mu, nmu, m.R, K, m.S(), rsum, tsum, gsum, c->train.moment_energy, inv_norm, d_grad,
         d_out);
     CUDA_TRY(cudaGetLastError(), "assemble");
-    c->launches += ne > 0 ? 5 : 4;
+    CUDA_TRY(cudaMemsetAsync(nonfinite, 0x7f, sizeof(int), c->stream), "clear finite check");
+    k_finite_check<<<(ncoef + 8 + 255) / 256, 256, 0, c->stream>>>(ncoef + 8, d_out, nonfinite);
+    CUDA_TRY(cudaGetLastError(), "finite check");
+    c->train.nonfinite = nonfinite;
+    c->launches += ne > 0 ? 6 : 5;
     const cudaMemcpyKind kind =
         memory == MTPB_MEMORY_DEVICE ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
     if (loss)
@@ -596,8 +613,34 @@ int loss_grad_compute(mtpb_context *c, const mtpb_labels *labels, const mtpb_los
         CUDA_TRY(cudaStreamSynchronize(c->stream), "gradient");
         if ((rc = check_device_error(c)))
             return rc;
+        long bad = -1;
+        return training_values_status(c, &bad);
     }
     return MTPB_OK;
+}
+
+int training_values_status(mtpb_context *c, long *first_bad)
+{
+    *first_bad = -1;
+    if (!c->train.nonfinite)
+        return fail(MTPB_ERR_STATE, "no mtpb_loss_grad call to check");
+    int rc = set_device(c);
+    if (rc)
+        return rc;
+    int bad = 0;
+    CUDA_TRY(cudaMemcpyAsync(&bad, c->train.nonfinite, sizeof(int), cudaMemcpyDeviceToHost,
+                             c->stream),
+             "read finite check");
+    CUDA_TRY(cudaStreamSynchronize(c->stream), "finite check");
+    if (bad == 0x7f7f7f7f)
+        return MTPB_OK;
+    *first_bad = bad;
+    std::string where = bad == 0 ? "the loss"
+                        : bad <= TERMS ? "metric " + std::to_string(bad - 1)
+                                       : "gradient component " + std::to_string(bad - 1 - TERMS);
+    return fail(MTPB_ERR_NONFINITE, "non-finite training value: " + where +
+                                        " (a label, weight or coefficient is NaN or infinite, "
+                                        "or the loss overflowed)");
 }
 
 } // namespace mtpb

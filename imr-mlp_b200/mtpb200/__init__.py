@@ -323,6 +323,14 @@ class MTPGpuDirect:
                                        _lib.MEMORY_DEVICE, _tdp(loss), _tdp(metrics),
                                        _tdp(grad)))
 
+    def check_training_values(self) -> int:
+        """Finite check of the last loss_grad call: -1 when the loss, metrics
+        and gradient are all finite; otherwise raises MTPBError (status 6)
+        naming the first non-finite value."""
+        first = C.c_long()
+        _check(self.lib.mtpb_check_training_values(self.ctx, C.byref(first)))
+        return first.value
+
     def last_train_timings(self):
         t = np.zeros(6)
         _check(self.lib.mtpb_last_train_timings(self.ctx, _dp(t)))

@@ -1,112 +1,426 @@
-"""Slab decomposition of one periodic box over the ranks of a process group.
+"""Slab decomposition of one periodic box with a ghost-atom halo exchange.
 
-The box's atoms are grouped into slabs along the first lattice direction
-(fractional coordinate of the wrapped position), one slab per rank, and kept
-in slab order.  Rank r evaluates the site terms of its own atoms only: its
-library context sees the whole box in a *rotated* order that starts with its
-slab (so its centres are the first n_r atoms, mtpb_set_center_count), with
-neighbours drawn from every atom of the periodic box.  One EFS step is then
+The box is cut into slabs along its first lattice direction (by the
+fractional coordinate of each atom), one slab per rank.  A rank holds only
+its own atoms plus ghost copies of the atoms of its two neighbouring slabs
+that lie within `halo` = r_c + skin of its slab faces, exactly as a LAMMPS
+domain decomposition with `newton_pair on` does for the reference's pair
+style (LAMMPS/USER-MLIP/pair_MLIP_gpu_direct.cpp:457: full list, ghost
+forces returned by reverse communication).
 
-  1. all-gather of the owned positions (the exchange of the halo: NVLink moves
-     the whole box, ~25 MB for 1M atoms, in tens of microseconds);
-  2. EFS of the owned centres, giving partial forces for every atom (the
-     reverse ghost contributions of a LAMMPS newton-on step,
-     LAMMPS/USER-MLIP/pair_MLIP_gpu_direct.cpp:457);
-  3. reduce-scatter (sum) of the partial forces, all-reduce of the energy and
-     virial.
+The rank's atoms form one local periodic structure for the library: the
+cell's first lattice vector is stretched to cover the slab, both halo layers
+and an empty gap of one more halo thickness, so that no pair forms across the
+stretched direction; the other two directions keep the box's periodicity.
+Owned atoms come first and the library evaluates only them as centres
+(mtpb_set_center_count), with neighbours drawn from owned and ghost atoms.
+One EFS step is then
 
-No kernel reads another GPU's memory; all transfers are collectives into
-local buffers.  The functions take torch tensors and a torch.distributed
-process group (nccl on GPUs, gloo on the CPU in the tests).
+  1. forward exchange: the current positions of the atoms in the halo layers
+     go to the neighbouring ranks (one message per neighbour);
+  2. EFS of the owned centres: forces for owned and ghost atoms (partial sums);
+  3. reverse exchange: ghost forces go back to their owners and are added;
+  4. all-reduce of the 10 totals (energy and virial).
+
+At a neighbour-list rebuild, atoms that left the slab move to the
+neighbouring rank (positions, types, ids and their per-atom payload), and the
+halo send lists are rebuilt from the new positions.  Per-step traffic is the
+halo (two layers of thickness r_c + skin), and per-rank memory is the slab
+plus its halo: both shrink as 1/N.
+
+The exchanges are written as phases: `pack_*` returns one tensor per
+neighbouring rank, `unpack_*` consumes the tensors received from them, and
+`p2p_exchange` moves them with grouped torch.distributed P2P operations
+(ncclSend/ncclRecv on GPUs, gloo on the CPU).  `LocalRanks` runs every rank
+of a decomposition inside one process by handing the packed tensors over
+directly (tests).  No kernel reads another GPU's memory: every transfer lands
+in a local buffer.
 """
 from __future__ import annotations
 
-from typing import Sequence
+from typing import Dict, List, Optional
 
 import numpy as np
 
 
-class SlabLayout:
-    """Slab order of a box: `order[k]` is the input index of the atom at slab
-    position k; rank r owns slab positions starts[r] .. starts[r+1]."""
-
-    def __init__(self, cell: np.ndarray, positions: np.ndarray, nranks: int):
-        cell = np.asarray(cell, dtype=np.float64).reshape(3, 3)
-        frac = np.asarray(positions, dtype=np.float64) @ np.linalg.inv(cell)
-        fx = frac[:, 0] - np.floor(frac[:, 0])
-        slab = np.minimum((fx * nranks).astype(np.int64), nranks - 1)
-        self.nranks = nranks
-        self.order = np.argsort(slab, kind="stable")
-        self.counts = np.bincount(slab, minlength=nranks).astype(np.int64)
-        self.starts = np.concatenate([[0], np.cumsum(self.counts)]).astype(np.int64)
-        self.natoms = int(self.starts[-1])
-
-    def rotation(self, rank: int) -> np.ndarray:
-        """Slab positions in rank `rank`'s local order (its own slab first)."""
-        s = int(self.starts[rank])
-        return np.concatenate([np.arange(s, self.natoms), np.arange(0, s)])
-
-    def to_local(self, x, rank: int):
-        """Slab-ordered array -> rank-local order (torch or numpy)."""
-        s = int(self.starts[rank])
-        return _cat([x[s:], x[:s]])
-
-    def to_slab(self, x, rank: int):
-        """Rank-local array -> slab order."""
-        s = int(self.starts[rank])
-        n = self.natoms
-        return _cat([x[n - s:], x[:n - s]])
-
-
-def _cat(parts: Sequence):
-    if isinstance(parts[0], np.ndarray):
-        return np.concatenate(parts)
+def _torch():
     import torch
-    return torch.cat(list(parts))
+    return torch
 
 
-class SlabExchange:
-    """The collectives of one EFS step on a slab layout."""
+def interplanar_spacing(cell: np.ndarray) -> float:
+    """Distance between the lattice planes spanned by the 2nd and 3rd cell
+    vectors (the thickness of the box along its first direction)."""
+    cell = np.asarray(cell, dtype=np.float64).reshape(3, 3)
+    return abs(float(np.linalg.det(cell))) / float(np.linalg.norm(np.cross(cell[1], cell[2])))
 
-    def __init__(self, layout: SlabLayout, rank: int, dist, device):
-        import torch
-        self.L = layout
-        self.rank = rank
+
+class SlabDomain:
+    """One rank's slab of a periodic box and its ghost layers.
+
+    State (torch tensors on `device`): owned positions `pos` [n_own, 3] in the
+    box's Cartesian frame (continuous between rebuilds), `types` [n_own],
+    global atom `ids` [n_own], and an optional per-atom float64 `payload`
+    [n_own, P] that migrates with the atoms (a reference position, say).
+    Ghost layers: `n_ghost_lo` atoms from the lower neighbour then
+    `n_ghost_hi` from the upper one, with their types and ids.
+    """
+
+    def __init__(self, cell, nranks: int, rank: int, halo: float, device=None):
+        torch = _torch()
+        if nranks < 2:
+            raise ValueError("a slab decomposition needs at least two ranks")
+        self.cell = np.asarray(cell, dtype=np.float64).reshape(3, 3)
+        self.inv = np.linalg.inv(self.cell)
+        self.nranks, self.rank = nranks, rank
+        self.device = device if device is not None else torch.device("cpu")
+        self.spacing = interplanar_spacing(self.cell)
+        self.h = float(halo) / self.spacing          # halo thickness, fractional
+        self.width = 1.0 / nranks
+        if self.h > self.width:
+            raise ValueError(f"slabs of {self.width * self.spacing:.3f} A are thinner than the "
+                             f"halo of {halo:.3f} A: use fewer ranks")
+        self.lo, self.hi = rank * self.width, (rank + 1) * self.width
+        self.lower, self.upper = (rank - 1) % nranks, (rank + 1) % nranks
+        # a gap of one halo (plus a margin for atoms that drift between
+        # rebuilds) keeps the stretched direction free of pairs
+        self.extent = self.width + 2.0 * self.h + 1.05 * self.h
+        self.local_cell = self.cell.copy()
+        self.local_cell[0] *= self.extent
+        self.origin = (self.lo - self.h) * self.cell[0]
+        a = self.cell[0]
+        # Cartesian shift of each ghost block in the box frame: the lower
+        # neighbour of rank 0 and the upper neighbour of the last rank sit
+        # across the periodic boundary
+        self.shift_lo = -a if rank == 0 else np.zeros(3)
+        self.shift_hi = a if rank == nranks - 1 else np.zeros(3)
+        dt = torch.float64
+        self._inv_t = torch.as_tensor(self.inv, dtype=dt, device=self.device)
+        self._cell_t = torch.as_tensor(self.cell, dtype=dt, device=self.device)
+        self._origin_t = torch.as_tensor(self.origin, dtype=dt, device=self.device)
+        self.peers: List[int] = sorted({self.lower, self.upper})
+        self.pos = self.types = self.ids = self.payload = None
+        self.send_idx: Dict[int, object] = {}
+        self.n_ghost_lo = self.n_ghost_hi = 0
+        self.ghost_types = self.ghost_ids = None
+        self._ghost_shift = None
+        self.rebuilds = 0
+        self.migrated = 0
+
+    # ---- ownership -----------------------------------------------------
+    def _frac_x(self, pos):
+        return pos @ self._inv_t[:, 0]
+
+    def assign(self, positions, types, ids=None, payload=None):
+        """Keeps the atoms of this rank's slab out of a whole box (set-up)."""
+        torch = _torch()
+        pos = torch.as_tensor(np.asarray(positions), dtype=torch.float64, device=self.device)
+        fx = self._frac_x(pos)
+        fx = fx - torch.floor(fx)
+        slab = torch.clamp((fx * self.nranks).long(), max=self.nranks - 1)
+        keep = torch.nonzero(slab == self.rank).flatten()
+        n = pos.shape[0]
+        all_ids = (torch.arange(n, device=self.device) if ids is None
+                   else torch.as_tensor(np.asarray(ids), dtype=torch.int64, device=self.device))
+        self.pos = self._wrap_x(pos[keep])
+        self.types = torch.as_tensor(np.asarray(types), dtype=torch.int32,
+                                     device=self.device)[keep]
+        self.ids = all_ids[keep]
+        self.payload = None if payload is None else torch.as_tensor(
+            np.asarray(payload), dtype=torch.float64, device=self.device)[keep]
+
+    def _wrap_x(self, pos):
+        """Wraps positions into [0, 1) along the first lattice direction."""
+        torch = _torch()
+        fx = self._frac_x(pos)
+        return pos - torch.floor(fx).unsqueeze(1) * self._cell_t[0]
+
+    @property
+    def n_own(self) -> int:
+        return int(self.pos.shape[0])
+
+    @property
+    def n_ghost(self) -> int:
+        return self.n_ghost_lo + self.n_ghost_hi
+
+    # ---- migration (rebuild, phase 1) ------------------------------------
+    def pack_migration(self):
+        """Atoms that left the slab, grouped per destination neighbour:
+        returns ({peer: count tensor [1]}, {peer: float64 [m, 5 + P]} rows of
+        x, y, z, type, id, payload...).  The atoms are removed from this rank."""
+        torch = _torch()
+        self.pos = self._wrap_x(self.pos)
+        fx = self._frac_x(self.pos)
+        slab = torch.clamp((fx * self.nranks).long(), max=self.nranks - 1)
+        leave_lo = slab == self.lower
+        leave_hi = slab == self.upper
+        stay = slab == self.rank
+        if not bool(torch.all(stay | leave_lo | leave_hi)):
+            raise RuntimeError("an atom moved further than one slab between rebuilds")
+        if self.lower == self.upper:
+            leave_hi = leave_hi | leave_lo
+            leave_lo = torch.zeros_like(leave_lo)
+        counts, rows = {}, {}
+        for p in self.peers:
+            sel = torch.zeros_like(stay)
+            if p == self.lower:
+                sel |= leave_lo
+            if p == self.upper:
+                sel |= leave_hi
+            idx = torch.nonzero(sel).flatten()
+            cols = [self.pos[idx], self.types[idx].double().unsqueeze(1),
+                    self.ids[idx].double().unsqueeze(1)]
+            if self.payload is not None:
+                cols.append(self.payload[idx])
+            rows[p] = torch.cat(cols, dim=1)
+            counts[p] = torch.tensor([idx.numel()], dtype=torch.int64, device=self.device)
+        keep = torch.nonzero(stay).flatten()
+        self.migrated = sum(int(r.shape[0]) for r in rows.values())
+        self.pos, self.types, self.ids = self.pos[keep], self.types[keep], self.ids[keep]
+        if self.payload is not None:
+            self.payload = self.payload[keep]
+        return counts, rows
+
+    def row_width(self) -> int:
+        return 5 + (0 if self.payload is None else int(self.payload.shape[1]))
+
+    def unpack_migration(self, rows: Dict[int, object]):
+        """Appends the atoms received from the neighbours."""
+        torch = _torch()
+        parts = [rows[p] for p in self.peers if rows.get(p) is not None and rows[p].shape[0]]
+        if not parts:
+            return
+        r = torch.cat(parts)
+        self.pos = torch.cat([self.pos, self._wrap_x(r[:, 0:3].contiguous())])
+        self.types = torch.cat([self.types, r[:, 3].round().to(torch.int32)])
+        self.ids = torch.cat([self.ids, r[:, 4].round().to(torch.int64)])
+        if self.payload is not None:
+            self.payload = torch.cat([self.payload, r[:, 5:].contiguous()])
+
+    # ---- halo lists (rebuild, phase 2) -------------------------------------
+    def pack_halo(self):
+        """Builds the send lists from the current positions and returns
+        ({peer: count tensor [2]}, {peer: int64 [m, 2] rows of type, id}).
+        Message to peer p: its lower-ghost segment (my atoms within the halo
+        of my upper face, if p is my upper neighbour) then its upper-ghost
+        segment (my atoms within the halo of my lower face, if p is my lower
+        neighbour); counts hold both segment sizes."""
+        torch = _torch()
+        fx = self._frac_x(self.pos)
+        near_lo = torch.nonzero(fx < self.lo + self.h).flatten()
+        near_hi = torch.nonzero(fx >= self.hi - self.h).flatten()
+        empty = torch.zeros(0, dtype=torch.int64, device=self.device)
+        counts, rows = {}, {}
+        self.send_idx = {}
+        for p in self.peers:
+            seg_a = near_hi if p == self.upper else empty   # p's lower ghosts
+            seg_b = near_lo if p == self.lower else empty   # p's upper ghosts
+            idx = torch.cat([seg_a, seg_b])
+            self.send_idx[p] = idx
+            counts[p] = torch.tensor([seg_a.numel(), seg_b.numel()], dtype=torch.int64,
+                                     device=self.device)
+            rows[p] = torch.stack([self.types[idx].long(), self.ids[idx]], dim=1)
+        return counts, rows
+
+    def unpack_halo(self, counts: Dict[int, object], rows: Dict[int, object]):
+        """Lays out the ghosts: [lower block | upper block]."""
+        torch = _torch()
+        lo_parts, hi_parts = [], []
+        self._recv_split = {}
+        for q in self.peers:
+            c = [int(v) for v in counts[q].tolist()]
+            r = rows[q]
+            # q's message: [my lower ghosts (q is my lower), my upper ghosts (q is my upper)]
+            self._recv_split[q] = c
+            if q == self.lower:
+                lo_parts.append(r[:c[0]])
+            if q == self.upper:
+                hi_parts.append(r[c[0]:c[0] + c[1]])
+        cat = lambda ps: torch.cat(ps) if ps else torch.zeros((0, 2), dtype=torch.int64,   # noqa: E731
+                                                              device=self.device)
+        lo, hi = cat(lo_parts), cat(hi_parts)
+        self.n_ghost_lo, self.n_ghost_hi = int(lo.shape[0]), int(hi.shape[0])
+        g = torch.cat([lo, hi])
+        self.ghost_types = g[:, 0].to(torch.int32)
+        self.ghost_ids = g[:, 1]
+        sl = torch.as_tensor(self.shift_lo, dtype=torch.float64, device=self.device)
+        sh = torch.as_tensor(self.shift_hi, dtype=torch.float64, device=self.device)
+        self._ghost_shift = torch.cat([sl.expand(self.n_ghost_lo, 3),
+                                       sh.expand(self.n_ghost_hi, 3)]) - self._origin_t
+        self.rebuilds += 1
+
+    def recv_halo_counts(self):
+        """Shapes of the halo-count messages expected from each neighbour."""
+        return {q: ((2,), "int64") for q in self.peers}
+
+    # ---- per step: forward positions, reverse forces ----------------------
+    def send_counts(self) -> Dict[int, int]:
+        return {p: int(idx.numel()) for p, idx in self.send_idx.items()}
+
+    def recv_counts(self) -> Dict[int, int]:
+        return {q: sum(c) if (q == self.lower and q == self.upper) else
+                (c[0] if q == self.lower else c[1]) for q, c in self._recv_split.items()}
+
+    def pack_positions(self):
+        """{peer: float64 [m, 3]} current positions of the halo atoms."""
+        return {p: self.pos[idx] for p, idx in self.send_idx.items()}
+
+    def unpack_positions(self, msgs):
+        """Local positions [owned | lower ghosts | upper ghosts] in the frame
+        of the stretched local cell."""
+        torch = _torch()
+        lo_parts, hi_parts = [], []
+        for q in self.peers:
+            c = self._recv_split[q]
+            m = msgs[q]
+            if q == self.lower:
+                lo_parts.append(m[:c[0]])
+            if q == self.upper:
+                hi_parts.append(m[c[0]:c[0] + c[1]])
+        ghosts = torch.cat(lo_parts + hi_parts) if (lo_parts or hi_parts) else \
+            torch.zeros((0, 3), dtype=torch.float64, device=self.device)
+        return torch.cat([self.pos - self._origin_t, ghosts + self._ghost_shift])
+
+    def local_types(self):
+        return _torch().cat([self.types, self.ghost_types])
+
+    def pack_forces(self, forces):
+        """{peer: float64 [m, 3]} ghost rows of the local forces, in the
+        order the peer sent those atoms."""
+        torch = _torch()
+        n = self.n_own
+        lo = forces[n:n + self.n_ghost_lo]
+        hi = forces[n + self.n_ghost_lo:n + self.n_ghost]
+        out = {}
+        for q in self.peers:
+            parts = []
+            if q == self.lower:
+                parts.append(lo)
+            if q == self.upper:
+                parts.append(hi)
+            out[q] = torch.cat(parts) if len(parts) > 1 else parts[0]
+        return out
+
+    def unpack_forces(self, forces, msgs):
+        """Owned forces: own rows plus the ghost forces returned by the
+        neighbours (newton-on reverse communication)."""
+        f = forces[:self.n_own].clone()
+        for p, idx in self.send_idx.items():
+            if idx.numel():
+                f.index_add_(0, idx, msgs[p])
+        return f
+
+
+# ---- transports ---------------------------------------------------------
+def p2p_exchange(dist, sends: Dict[int, object], recv_shapes: Dict[int, tuple], dtype, device,
+                 group=None):
+    """Grouped send/receive of one tensor per peer (ncclSend/ncclRecv inside
+    one group on NCCL).  Empty messages are skipped on both sides (their sizes
+    are known to both)."""
+    torch = _torch()
+    recvs = {q: torch.empty(shape, dtype=dtype, device=device) for q, shape in
+             recv_shapes.items()}
+    ops = []
+    for p, t in sends.items():
+        if t.numel():
+            ops.append(dist.P2POp(dist.isend, t.contiguous(), p, group))
+    for q, t in recvs.items():
+        if t.numel():
+            ops.append(dist.P2POp(dist.irecv, t, q, group))
+    if ops:
+        for w in dist.batch_isend_irecv(ops):
+            w.wait()
+    return recvs
+
+
+class DistributedSlab:
+    """Drives one SlabDomain over a torch.distributed process group."""
+
+    def __init__(self, domain: SlabDomain, dist, group=None):
+        self.d = domain
         self.dist = dist
-        self.maxc = int(layout.counts.max())
-        self.nccl = dist.get_backend() == "nccl"
-        ws = layout.nranks
-        self.gbuf = torch.zeros((ws, self.maxc, 3), dtype=torch.float64, device=device)
-        self.sendbuf = torch.zeros((self.maxc, 3), dtype=torch.float64, device=device)
-        self.fbuf = torch.zeros((ws, self.maxc, 3), dtype=torch.float64, device=device)
-        self.fout = torch.zeros((self.maxc, 3), dtype=torch.float64, device=device)
+        self.group = group
 
-    def gather_positions(self, own):
-        """own: (n_rank, 3) positions of this rank's slab -> (N, 3) slab order."""
-        n = own.shape[0]
-        self.sendbuf[:n].copy_(own)
-        if self.nccl:
-            self.dist.all_gather_into_tensor(self.gbuf, self.sendbuf)
-        else:
-            parts = list(self.gbuf.unbind(0))
-            self.dist.all_gather(parts, self.sendbuf)
-            for r, p in enumerate(parts):
-                self.gbuf[r].copy_(p)
-        c = self.L.counts
-        return _cat([self.gbuf[r, :int(c[r])] for r in range(self.L.nranks)])
+    def rebuild(self):
+        torch = _torch()
+        d = self.d
+        counts, rows = d.pack_migration()
+        rc = p2p_exchange(self.dist, counts, {q: (1,) for q in d.peers}, torch.int64, d.device,
+                          self.group)
+        w = d.row_width()
+        recv = p2p_exchange(self.dist, rows, {q: (int(rc[q][0]), w) for q in d.peers},
+                            torch.float64, d.device, self.group)
+        d.unpack_migration(recv)
+        counts, rows = d.pack_halo()
+        hc = p2p_exchange(self.dist, counts, {q: (2,) for q in d.peers}, torch.int64, d.device,
+                          self.group)
+        hr = p2p_exchange(self.dist, rows, {q: (int(hc[q].sum()), 2) for q in d.peers},
+                          torch.int64, d.device, self.group)
+        d.unpack_halo(hc, hr)
 
-    def reduce_forces(self, partial):
-        """partial: (N, 3) slab-ordered partial forces -> (n_rank, 3) sums."""
-        c, st = self.L.counts, self.L.starts
-        for r in range(self.L.nranks):
-            self.fbuf[r, :int(c[r])].copy_(partial[int(st[r]):int(st[r + 1])])
-        if self.nccl:
-            self.dist.reduce_scatter_tensor(self.fout, self.fbuf)
-            return self.fout[:int(c[self.rank])]
-        self.dist.all_reduce(self.fbuf)
-        return self.fbuf[self.rank, :int(c[self.rank])]
+    def positions(self):
+        torch = _torch()
+        d = self.d
+        rc = d.recv_counts()
+        msgs = p2p_exchange(self.dist, d.pack_positions(), {q: (rc[q], 3) for q in d.peers},
+                            torch.float64, d.device, self.group)
+        return d.unpack_positions(msgs)
 
-    def reduce_totals(self, t):
-        """Sum of per-rank energy / virial totals (in place)."""
-        self.dist.all_reduce(t)
+    def forces(self, local_forces):
+        torch = _torch()
+        d = self.d
+        sc = d.send_counts()
+        msgs = p2p_exchange(self.dist, d.pack_forces(local_forces),
+                            {q: (sc[q], 3) for q in d.peers}, torch.float64, d.device,
+                            self.group)
+        return d.unpack_forces(local_forces, msgs)
+
+    def totals(self, t):
+        self.dist.all_reduce(t, group=self.group)
         return t
+
+
+class LocalRanks:
+    """Every rank of a decomposition in one process: the packed tensors are
+    handed to their receivers directly."""
+
+    def __init__(self, domains: List[SlabDomain]):
+        self.ds = domains
+
+    @staticmethod
+    def _route(sends: List[Dict[int, object]]):
+        return [{p: sends[p][r] for p in sends[r].keys()} for r in range(len(sends))]
+
+    def rebuild(self):
+        mig = [d.pack_migration()[1] for d in self.ds]
+        for d, got in zip(self.ds, self._route(mig)):
+            d.unpack_migration(got)
+        halo = [d.pack_halo() for d in self.ds]
+        counts = self._route([h[0] for h in halo])
+        rows = self._route([h[1] for h in halo])
+        for d, c, r in zip(self.ds, counts, rows):
+            d.unpack_halo(c, r)
+
+    def positions(self):
+        msgs = self._route([d.pack_positions() for d in self.ds])
+        return [d.unpack_positions(m) for d, m in zip(self.ds, msgs)]
+
+    def forces(self, local_forces):
+        msgs = self._route([d.pack_forces(f) for d, f in zip(self.ds, local_forces)])
+        return [d.unpack_forces(f, m) for d, f, m in zip(self.ds, local_forces, msgs)]
+
+
+def local_structure(domain: SlabDomain, positions) -> dict:
+    """The rank's atoms as one periodic structure for the library (numpy)."""
+    return dict(cell=domain.local_cell.copy(), pbc=np.ones(3, np.int32),
+                positions=positions.detach().cpu().numpy() if hasattr(positions, "detach")
+                else np.asarray(positions),
+                types=domain.local_types().cpu().numpy().astype(np.int32))
+
+
+def halo_bytes_per_step(domain: SlabDomain) -> Dict[str, int]:
+    """Bytes this rank sends per EFS step: ghost positions out (forward),
+    ghost forces out (reverse), plus the 10-double all-reduce."""
+    fwd = 24 * sum(domain.send_counts().values())
+    rev = 24 * domain.n_ghost
+    return {"forward": fwd, "reverse": rev, "totals": 80}

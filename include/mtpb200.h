@@ -42,7 +42,8 @@ enum mtpb_status {
     MTPB_ERR_UNSUPPORTED = 2,  /* model or geometry outside what the kernels implement */
     MTPB_ERR_CUDA = 3,         /* CUDA runtime error (message holds the CUDA text) */
     MTPB_ERR_MEMORY = 4,       /* device allocation failed */
-    MTPB_ERR_STATE = 5         /* call order violated (e.g. no neighbour list yet) */
+    MTPB_ERR_STATE = 5,        /* call order violated (e.g. no neighbour list yet) */
+    MTPB_ERR_NONFINITE = 6     /* a loss, metric or gradient value is NaN or infinite */
 };
 
 enum mtpb_memory { MTPB_MEMORY_HOST = 0, MTPB_MEMORY_DEVICE = 1 };
@@ -313,6 +314,17 @@ typedef struct mtpb_labels {
  * outputs are `memory`-side arrays. */
 int mtpb_loss_grad(mtpb_context *ctx, const mtpb_labels *labels, const mtpb_loss_weights *w,
                    int norm_count, int memory, double *loss, double *metrics, double *grad);
+
+/* Finite check of the last mtpb_loss_grad call's loss, metrics and gradient,
+ * made on the device by that call (the reference's check_training_values /
+ * training_finite_kernel, runtime/mtp/gpu-direct/mtp_gpu_direct.cu:5395-5420).
+ * Host-memory calls of mtpb_loss_grad run this check themselves and return
+ * MTPB_ERR_NONFINITE; device-memory calls do not synchronise, so their caller
+ * asks here (this call synchronises the context stream).  first_nonfinite
+ * receives -1 when every value is finite, else the smallest index into
+ * [loss, metrics[7], grad[...]] of a NaN or infinite value, and the call
+ * returns MTPB_ERR_NONFINITE. */
+int mtpb_check_training_values(mtpb_context *ctx, long *first_nonfinite);
 
 /* ---- diagnostics ---------------------------------------------------------- */
 

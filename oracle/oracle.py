@@ -271,6 +271,8 @@ class Reference:
                                        _dp, _dp, _dp, _dp]
         L.ref_mlip_compute_omp.argtypes = [C.c_void_p, C.c_int, C.c_int, _ip, C.c_int, _ip, _dp,
                                            _ip, _ip, _ip, _dp, _dp]
+        L.ref_mlip_efs_omp.argtypes = [C.c_void_p, C.c_int, C.c_int, _ip, C.c_int, _ip, _dp,
+                                       _ip, _ip, _ip, _dp, _dp, _dp, _dp]
 
     @staticmethod
     def available(path: Optional[str] = None) -> bool:
@@ -390,3 +392,87 @@ class ReferenceEFS:
         forces = f[:n].copy()
         np.add.at(forces, prob["nl"].nbr, f[n:])
         return float(en[0]), forces
+
+    def compute_full(self, prob):
+        """Energy, site energies[n], forces[n,3] (ghost rows folded onto their
+        owners) and the virial [xx yy zz xy xz yz] as the sum of MLIPCore's
+        per-atom virials over centres and ghosts."""
+        n = prob["n"]
+        ntot = len(prob["types"])
+        f = np.zeros((ntot, 3))
+        se = np.zeros(ntot)
+        sv = np.zeros((ntot, 6))
+        en = np.zeros(1)
+        ilist = np.arange(n, dtype=np.int32)
+        rc = self.ref.lib.ref_mlip_efs_omp(self.handle, self.threads, n, _i(ilist), ntot,
+                                           _i(prob["types"]), _d(prob["x"]),
+                                           _i(prob["numneigh"]), _i(prob["foff"]),
+                                           _i(prob["flat"]), _d(en), _d(f), _d(se), _d(sv))
+        if rc:
+            raise RuntimeError(self.ref._err())
+        forces = f[:n].copy()
+        np.add.at(forces, prob["nl"].nbr, f[n:])
+        return float(en[0]), se[:n], forces, sv.sum(axis=0)
+
+
+class ReferenceGpu:
+    """The reference's own GPU trainer core (MTPGpuDirect compute_batch ->
+    prepare_loss -> accumulate_gradient, deterministic FP64 reductions),
+    compiled from the reference sources into ``_ref/librefgpu.so`` by
+    ``oracle/Makefile`` (target ``refgpu``, ref_gpu_shim.cpp).  Test
+    infrastructure: the gradient pin of the GPU tests."""
+
+    def __init__(self, mtp_text: str, species: int, device: int = 0,
+                 path: Optional[str] = None):
+        self.lib = C.CDLL(path or os.path.join(HERE, "_ref", "librefgpu.so"))
+        L = self.lib
+        L.refgpu_last_error.restype = C.c_char_p
+        L.refgpu_create.restype = C.c_void_p
+        L.refgpu_create.argtypes = [C.c_char_p, C.c_int, C.c_int, _ip]
+        L.refgpu_destroy.argtypes = [C.c_void_p]
+        L.refgpu_loss_grad.argtypes = [C.c_void_p, C.c_int, _ip, _ip, _ip, _dp, _ip, _dp,
+                                       _dp, _dp, _dp, _dp, _dp, _dp, _dp, _dp, _dp, _dp, _dp]
+        n = C.c_int()
+        self.handle = L.refgpu_create(mtp_text.encode(), species, device, C.byref(n))
+        if not self.handle:
+            raise RuntimeError(L.refgpu_last_error().decode())
+        self.gradient_count = n.value
+
+    @staticmethod
+    def available(path: Optional[str] = None) -> bool:
+        return os.path.exists(path or os.path.join(HERE, "_ref", "librefgpu.so"))
+
+    def close(self):
+        if self.handle:
+            self.lib.refgpu_destroy(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def loss_grad(self, atom_offsets, nl: NeighborList, types, positions, target_energy,
+                  energy_weight, target_force, force_weight, target_stress, stress_weight):
+        """Metrics[7], un-normalised gradient, and the forward forces, site
+        energies and site virials (xx yy zz xy xz yz) of one batch."""
+        offs = np.ascontiguousarray(atom_offsets, dtype=np.int32)
+        S = len(offs) - 1
+        n = int(offs[-1])
+        metrics = np.zeros(7)
+        grad = np.zeros(self.gradient_count)
+        f = np.zeros((n, 3))
+        se = np.zeros(n)
+        sv = np.zeros((n, 6))
+        c = lambda a, t=np.float64: np.ascontiguousarray(a, dtype=t)   # noqa: E731
+        args = [c(nl.offsets, np.int32), c(nl.nbr, np.int32), c(nl.rij), c(types, np.int32),
+                c(positions), c(target_energy), c(energy_weight), c(target_force),
+                c(force_weight), c(target_stress), c(stress_weight)]
+        rc = self.lib.refgpu_loss_grad(
+            self.handle, S, _i(offs), _i(args[0]), _i(args[1]), _d(args[2]), _i(args[3]),
+            _d(args[4]), _d(args[5]), _d(args[6]), _d(args[7]), _d(args[8]), _d(args[9]),
+            _d(args[10]), _d(metrics), _d(grad), _d(f), _d(se), _d(sv))
+        if rc:
+            raise RuntimeError(self.lib.refgpu_last_error().decode())
+        return metrics, grad, f, se, sv

@@ -215,4 +215,71 @@ int ref_mlip_compute_omp(void *handle, int threads, int inum, const int *ilist, 
     }
 }
 
+// MLIPCore::compute driven by OpenMP over centres for problems where every
+// neighbour of every centre is its own ghost row (the explicit-image form the
+// Python wrapper builds): each row of f, site_energy and site_virial is then
+// written by the one thread that owns its centre, so all threads share the
+// output arrays.  f[3*ntotal] and site_virial[6*ntotal] (may be null) are
+// accumulated, site_energy[ntotal] (may be null) written for the centres; the
+// energy is the sum of the per-thread energies in thread order.
+int ref_mlip_efs_omp(void *handle, int threads, int inum, const int *ilist, int ntotal,
+                     const int *type, const double *x, const int *numneigh,
+                     const int *firstneigh_off, const int *firstneigh_flat, double *energy,
+                     double *f, double *site_energy, double *site_virial)
+{
+    try
+    {
+        auto *p = static_cast<MLIPCore::mlip *>(handle);
+        if (threads <= 0)
+            threads = omp_get_max_threads();
+        std::vector<double *> xptr(ntotal), fptr(ntotal), vptr(site_virial ? ntotal : 0);
+        std::vector<int *> nptr(ntotal);
+        for (int i = 0; i < ntotal; ++i)
+        {
+            xptr[i] = const_cast<double *>(x) + 3 * static_cast<std::size_t>(i);
+            fptr[i] = f + 3 * static_cast<std::size_t>(i);
+            if (site_virial)
+                vptr[i] = site_virial + 6 * static_cast<std::size_t>(i);
+            nptr[i] = const_cast<int *>(firstneigh_flat) + firstneigh_off[i];
+        }
+        std::vector<double> ebuf(threads, 0.0);
+        int failed = 0;
+#pragma omp parallel num_threads(threads) reduction(| : failed)
+        {
+            const int t = omp_get_thread_num();
+            const int nt = omp_get_num_threads();
+            const int b = (int)((long)inum * t / nt), e = (int)((long)inum * (t + 1) / nt);
+            try
+            {
+                MLIPCore::mlip_buffers *buf = MLIPCore::create_mlip_buffer(p);
+                double en = 0;
+                MLIPCore::compute(p, buf, ilist + b, numneigh, e - b, type, xptr.data(),
+                                  nptr.data(), &en, site_energy,
+                                  site_virial ? vptr.data() : nullptr, fptr.data());
+                MLIPCore::destroy_mlip_buffer(buf);
+                ebuf[t] = en;
+            }
+            catch (...)
+            {
+                failed |= 1;
+            }
+        }
+        if (failed)
+        {
+            g_error = "MLIPCore::compute failed in a worker thread";
+            return -1;
+        }
+        double en = 0;
+        for (int t = 0; t < threads; ++t)
+            en += ebuf[t];
+        *energy = en;
+        return 0;
+    }
+    catch (const std::exception &ex)
+    {
+        g_error = ex.what();
+        return -1;
+    }
+}
+
 } // extern "C"

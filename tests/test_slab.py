@@ -1,8 +1,12 @@
-"""Host logic of the slab decomposition (mtpb200.slab) on two gloo ranks on
-the CPU: each rank evaluates the site terms of its own slab with the C oracle
-on its rotated view of the whole box, then the collectives of SlabExchange
-assemble forces, energy and virial, which must equal the single-process
-oracle result.  Needs no GPU."""
+"""Host logic of the slab decomposition with a ghost-atom halo exchange
+(mtpb200.slab) on the CPU: 2 and 3 gloo ranks, and every rank of a
+decomposition in one process (LocalRanks).  Each rank evaluates the site
+terms of its owned atoms with the C oracle on its local structure (owned
+atoms plus the ghost layers in the stretched periodic cell); the reverse
+exchange returns the ghost forces to their owners.  Forces (by global atom
+id), energy and virial must equal the single-process oracle on the whole box
+after a rebuild, after reuse steps that only exchange positions, and after a
+rebuild at which atoms migrate between slabs.  Needs no GPU."""
 import os
 import socket
 
@@ -10,9 +14,9 @@ import numpy as np
 import pytest
 
 from mtpb200 import configs
-from mtpb200.slab import SlabLayout
 
-WS = 2
+SKIN = 0.5
+REPS = 6          # 21.1 A box: slabs of 10.6 / 7.0 A at 2 / 3 ranks, halo 5.5 A
 
 
 def _free_port():
@@ -22,26 +26,90 @@ def _free_port():
 
 
 def _box():
-    st = configs.ni3al_l12(3, 3.52, 0.08, seed=5)
-    return st
+    return configs.ni3al_l12(REPS, 3.52, 0.08, seed=5)
 
 
-def _partial_efs(oracle, model, st, pos, types, ncenter):
-    """Site terms of centres [0, ncenter) of a box given in local order."""
-    nl = oracle.neighbors(st["cell"], st["pbc"], pos, model.cutoff)
+def _moves(n, seed=17):
+    """Per-atom displacements by global id: none for the first build, two
+    small ones (below skin/2) for the reuse steps, then 0.9 A along x (plus
+    noise) for the second rebuild, so that the atoms next to every slab face
+    cross it and migrate."""
+    rng = np.random.default_rng(seed)
+    small = rng.uniform(-0.12, 0.12, (2, n, 3))
+    big = np.zeros((n, 3))
+    big[:, 0] = 0.9
+    big += rng.uniform(-0.1, 0.1, (n, 3))
+    return [np.zeros((n, 3)), small[0], small[1], big]
+
+
+STEPS = [(True, 0), (False, 1), (False, 2), (True, 3)]   # (rebuild, displacement index)
+
+
+def _partial_efs(oracle, model, cell, pos, types, ncenter):
+    """Site terms of centres [0, ncenter) of a local structure: energy,
+    forces on every local atom, virial."""
+    nl = oracle.neighbors(cell, np.ones(3, np.int32), pos, model.cutoff)
     se, d = oracle.site_derivatives(model, types, nl)
-    n = len(types)
-    f = np.zeros((n, 3))
+    f = np.zeros((len(types), 3))
     w = np.zeros((3, 3))
     for i in range(ncenter):
         for e in range(nl.offsets[i], nl.offsets[i + 1]):
             f[i] += d[e]
             f[nl.nbr[e]] -= d[e]
             w -= np.outer(d[e], nl.rij[e])
-    return se[:ncenter].sum(), f, w
+    return float(se[:ncenter].sum()), f, w
 
 
-def _rank_main(rank, port, result_dir):
+def _reference(oracle, model, st, disp):
+    pos = st["positions"] + disp
+    nl = oracle.neighbors(st["cell"], st["pbc"], pos, model.cutoff)
+    e, _, f, w = oracle.efs(model, st["types"], nl)
+    return e, f, w.reshape(3, 3)
+
+
+def test_local_ranks_match_single_process(oracle, model_l16):
+    """All ranks in one process (LocalRanks) for 2 and 3 ranks."""
+    torch = pytest.importorskip("torch")
+    from mtpb200.slab import LocalRanks, SlabDomain
+    st = _box()
+    n = len(st["types"])
+    moves = _moves(n)
+    for nranks in (2, 3):
+        ds = [SlabDomain(st["cell"], nranks, r, model_l16.cutoff + SKIN) for r in range(nranks)]
+        for d in ds:
+            d.assign(st["positions"], st["types"])
+        assert sum(d.n_own for d in ds) == n
+        lr = LocalRanks(ds)
+        migrated = 0
+        prev = 0
+        for rebuild, k in STEPS:
+            for d in ds:   # positions move continuously (the domain wraps them)
+                ids = d.ids.numpy()
+                d.pos = d.pos + torch.as_tensor(moves[k][ids] - moves[prev][ids])
+            prev = k
+            if rebuild:
+                lr.rebuild()
+                migrated += sum(d.migrated for d in ds)
+            xs = lr.positions()
+            parts = [_partial_efs(oracle, model_l16, d.local_cell, x.numpy(),
+                                  d.local_types().numpy(), d.n_own) for d, x in zip(ds, xs)]
+            fo = lr.forces([torch.from_numpy(p[1]) for p in parts])
+            f = np.zeros((n, 3))
+            seen = np.zeros(n, np.int64)
+            for d, ff in zip(ds, fo):
+                f[d.ids.numpy()] = ff.numpy()
+                seen[d.ids.numpy()] += 1
+            assert np.all(seen == 1)
+            e_ref, f_ref, w_ref = _reference(oracle, model_l16, st, moves[k])
+            assert abs(sum(p[0] for p in parts) - e_ref) / n < 1e-10
+            assert np.max(np.abs(f - f_ref)) < 1e-9
+            assert np.max(np.abs(sum(p[2] for p in parts) - w_ref)) < 1e-9
+            # the halo is two layers, far less than the box
+            assert all(d.n_ghost < n for d in ds)
+        assert migrated > 0   # the last rebuild moved atoms between slabs
+
+
+def _rank_main(rank, ws, port, result_dir):
     import sys
     import torch
     import torch.distributed as dist
@@ -51,56 +119,77 @@ def _rank_main(rank, port, result_dir):
     sys.path.insert(0, os.path.join(root, "oracle"))
     from oracle import Oracle
     from mtpb200 import read_mtp
-    from mtpb200.slab import SlabExchange, SlabLayout
+    from mtpb200.slab import DistributedSlab, SlabDomain
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=WS)
+    dist.init_process_group("gloo", rank=rank, world_size=ws)
     try:
         O = Oracle()
         model = read_mtp(os.path.join(root, "tests", "golden", "models", "l16_k2.mtp"))
         st = _box()
-        L = SlabLayout(st["cell"], st["positions"], WS)
-        pos_slab = st["positions"][L.order]
-        types_slab = st["types"][L.order]
-        own = torch.from_numpy(pos_slab[L.starts[rank]:L.starts[rank + 1]].copy())
-        X = SlabExchange(L, rank, dist, torch.device("cpu"))
-        full = X.gather_positions(own).numpy()
-        assert np.array_equal(full, pos_slab)
-        pos_loc = L.to_local(full, rank)
-        types_loc = L.to_local(types_slab, rank)
-        e, f_loc, w = _partial_efs(O, model, st, pos_loc, types_loc, int(L.counts[rank]))
-        f_own = X.reduce_forces(torch.from_numpy(L.to_slab(f_loc, rank).copy())).numpy()
-        tot = X.reduce_totals(torch.tensor([e] + list(w.reshape(9)), dtype=torch.float64))
-        np.savez(os.path.join(result_dir, f"rank{rank}.npz"), f_own=f_own, tot=tot.numpy())
+        n = len(st["types"])
+        moves = _moves(n)
+        d = SlabDomain(st["cell"], ws, rank, model.cutoff + SKIN)
+        d.assign(st["positions"], st["types"])
+        ds = DistributedSlab(d, dist)
+        res = {}
+        prev = 0
+        for s, (rebuild, k) in enumerate(STEPS):
+            ids = d.ids.numpy()
+            d.pos = d.pos + torch.as_tensor(moves[k][ids] - moves[prev][ids])
+            prev = k
+            if rebuild:
+                ds.rebuild()
+            x = ds.positions()
+            e, f, w = _partial_efs(O, model, d.local_cell, x.numpy(),
+                                   d.local_types().numpy(), d.n_own)
+            fo = ds.forces(torch.from_numpy(f))
+            tot = ds.totals(torch.tensor([e] + list(w.reshape(9)), dtype=torch.float64))
+            res[f"ids{s}"] = d.ids.numpy()
+            res[f"f{s}"] = fo.numpy()
+            res[f"tot{s}"] = tot.numpy()
+            res[f"mig{s}"] = np.array([d.migrated if rebuild else 0])
+        np.savez(os.path.join(result_dir, f"rank{rank}.npz"), **res)
     finally:
         dist.destroy_process_group()
 
 
-def test_layout_rotation_roundtrip():
-    st = _box()
-    L = SlabLayout(st["cell"], st["positions"], 3)
-    assert L.counts.sum() == len(st["types"]) and np.all(L.counts > 0)
-    x = np.arange(L.natoms * 3, dtype=np.float64).reshape(-1, 3)
-    for r in range(3):
-        loc = L.to_local(x, r)
-        assert np.array_equal(loc[:L.counts[r]], x[L.starts[r]:L.starts[r + 1]])
-        assert np.array_equal(L.to_slab(loc, r), x)
-        assert np.array_equal(loc, x[L.rotation(r)])
-
-
-def test_two_gloo_ranks_match_single_process(oracle, model_l16, tmp_path):
-    torch = pytest.importorskip("torch")
+@pytest.mark.parametrize("ws", [2, 3])
+def test_gloo_ranks_match_single_process(oracle, model_l16, tmp_path, ws):
+    pytest.importorskip("torch")
     import torch.multiprocessing as mp
     port = _free_port()
-    mp.spawn(_rank_main, args=(port, str(tmp_path)), nprocs=WS, join=True)
+    mp.spawn(_rank_main, args=(ws, port, str(tmp_path)), nprocs=ws, join=True)
     st = _box()
-    L = SlabLayout(st["cell"], st["positions"], WS)
-    pos_slab = st["positions"][L.order]
-    types_slab = st["types"][L.order]
-    nl = oracle.neighbors(st["cell"], st["pbc"], pos_slab, model_l16.cutoff)
-    e, _, f, w = oracle.efs(model_l16, types_slab, nl)
-    for r in range(WS):
-        d = np.load(os.path.join(tmp_path, f"rank{r}.npz"))
-        assert np.max(np.abs(d["f_own"] - f[L.starts[r]:L.starts[r + 1]])) < 1e-11
-        assert abs(d["tot"][0] - e) < 1e-10 * len(types_slab)
-        assert np.max(np.abs(d["tot"][1:] - w.reshape(9))) < 1e-9
+    n = len(st["types"])
+    moves = _moves(n)
+    migrated = 0
+    for s, (_, k) in enumerate(STEPS):
+        e_ref, f_ref, w_ref = _reference(oracle, model_l16, st, moves[k])
+        f = np.zeros((n, 3))
+        seen = np.zeros(n, np.int64)
+        for r in range(ws):
+            d = np.load(os.path.join(tmp_path, f"rank{r}.npz"))
+            f[d[f"ids{s}"]] = d[f"f{s}"]
+            seen[d[f"ids{s}"]] += 1
+            assert abs(d[f"tot{s}"][0] - e_ref) / n < 1e-10
+            assert np.max(np.abs(d[f"tot{s}"][1:] - w_ref.reshape(9))) < 1e-9
+            migrated += int(d[f"mig{s}"][0])
+        assert np.all(seen == 1)
+        assert np.max(np.abs(f - f_ref)) < 1e-9
+    assert migrated > 0
+
+
+def test_domain_geometry_and_limits():
+    from mtpb200.slab import SlabDomain, interplanar_spacing
+    st = _box()
+    L = interplanar_spacing(st["cell"])
+    assert abs(L - 3.52 * REPS) < 1e-9
+    d = SlabDomain(st["cell"], 3, 1, 5.5)
+    assert abs(d.h * L - 5.5) < 1e-12
+    # the stretched direction holds slab + two halos + a gap wider than the halo
+    assert d.extent * L > (d.width + 2 * d.h) * L + 5.5
+    with pytest.raises(ValueError):
+        SlabDomain(st["cell"], 4, 0, 5.5)     # 5.3 A slabs, thinner than the halo
+    with pytest.raises(ValueError):
+        SlabDomain(st["cell"], 1, 0, 5.5)
