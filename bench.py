@@ -4,9 +4,10 @@
 Workload (configs[2] of BASELINE.json): 1,048,576-atom Ni3Al L1_2 box (64^3
 fcc cells, a = 3.52 A, Gaussian sigma 0.08 A, seed 3), level-20 MTP
 (Shapeev level-20 graph, 2 species, R = 8, r_cut = 5 A, seeded U(-0.1, 0.1)
-coefficients), repeated EFS steps with a GPU neighbour-list rebuild every 10
-steps (steps between rebuilds upload positions and refresh the edge vectors
-from the stored periodic images).  Synthetic seeded data; the working set
+coefficients), MD-style EFS steps: the positions move every step (seeded
+displacement fields, any two steps within skin/2), the GPU neighbour lists are
+built with a 0.5 A skin every 10 steps, and the steps between upload the new
+positions and recompute every edge vector from the stored periodic images.  Synthetic seeded data; the working set
 (~6 GB) is far larger than the 126 MB L2, so no L2 flush is needed.
 
 The same line carries a "train" object for the second half of the metric,
@@ -20,11 +21,14 @@ configurations (EFS pass, loss, gradient kernels, reductions).
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 Multi-GPU: launched by torch.distributed.run, one rank per GPU; the box is
-split into x-slabs, one per rank (mtpb200/slab.py): every step all-gathers the
-positions, evaluates the rank's own centres against the whole periodic box,
-reduce-scatters the partial forces and all-reduces energy and virial (strong
-scaling: total atoms of the one box per second); the training leg shards the 8192 configurations over the ranks and sums loss,
-metrics and gradient with an NCCL all-reduce (strong scaling).
+split into x-slabs, one per rank, each with ghost layers of r_c + skin from
+its two neighbours (mtpb200/slab.py): every step exchanges the halo positions
+with grouped ncclSend/ncclRecv, evaluates the rank's owned centres over owned
+and ghost atoms, returns the ghost forces to their owners and all-reduces
+energy and virial; atoms migrate between slabs at rebuilds (strong scaling:
+total atoms of the one box per second).  The training leg shards the 8192
+configurations over the ranks and sums loss, metrics and gradient with an
+NCCL all-reduce (strong scaling).
 """
 from __future__ import annotations
 
@@ -45,6 +49,10 @@ MODEL = os.path.join(ROOT, "tests", "golden", "models", "l20_k2.mtp")
 METRIC = "MTP EFS atoms/sec (1M-atom, level 20)"
 UNIT = "atoms/s"
 REBUILD_EVERY = 10
+SKIN = 0.5             # neighbour-list skin, Angstrom
+N_DISP = 4             # seeded per-step displacement fields, cycled
+DISP_AMPLITUDE = 0.07  # Angstrom per component: two steps differ by < skin / 2
+DISP_SEED = 31
 TRAIN_METRIC = "MTP train configs/sec (config 4: 8192 configs of 64-216 atoms, level 24)"
 TRAIN_UNIT = "configs/s"
 TRAIN_WEIGHTS = (1.0, 0.01, 0.001, 1.0, 0.0, 1.0)   # E, F, S and the default powers
@@ -287,19 +295,6 @@ def batch_problem(name):
             "K=3, R=10, r_cut=6")
 
 
-def shard_lpt(sizes, nranks):
-    """Greedy longest-processing-time assignment of structures to ranks by
-    size (edge counts are proportional to atom counts within a config)."""
-    order = np.argsort(-np.asarray(sizes), kind="stable")
-    load = np.zeros(nranks)
-    owner = np.zeros(len(sizes), dtype=np.int64)
-    for i in order:
-        r = int(np.argmin(load))
-        owner[i] = r
-        load[r] += sizes[i]
-    return owner
-
-
 def cpu_batch_sample(model, sts, threads, n_sample):
     """Reference CPU path per structure (Neighborhoods build + MLIPCore over
     OpenMP centres), the calc_efs loop, on the first n_sample structures."""
@@ -328,10 +323,11 @@ def run_batch(name, args, torch, dist, ws, rank, local, dev, stream):
     (no data-path collective; one all-reduce of the energy total per step),
     neighbour lists built every step as a calc_efs pass does."""
     from mtpb200 import MTPGpuDirect, StructureBatch
+    from mtpb200.shards import shard_lpt, shard_of
     sts, model, desc = batch_problem(name)
     sizes = [len(x["types"]) for x in sts]
     owner = shard_lpt(sizes, ws)
-    mine = [x for x, o in zip(sts, owner) if o == rank]
+    mine, _ = shard_of(sts, owner, rank)
     b = StructureBatch.from_structures(mine)
     gpu = MTPGpuDirect(model, local)
     gpu.set_stream(stream.cuda_stream)
@@ -492,9 +488,10 @@ def train_ref_flops(model, edges, atoms, configs_count):
 def run_train(args, torch, dist, ws, rank, local, dev, stream):
     """Training leg on every rank; returns the JSON object on rank 0."""
     from mtpb200 import MTPGpuDirect, StructureBatch
+    from mtpb200.shards import allreduce_loss_grad, shard_lpt, shard_of
     sts, teacher, student = train_problem(args.train_configs)
     owner = shard_lpt([len(x["types"]) for x in sts], ws)   # whole structures, balanced
-    mine = [x for x, o in zip(sts, owner) if o == rank]
+    mine, _ = shard_of(sts, owner, rank)
     batch = StructureBatch.from_structures(mine)
     with MTPGpuDirect(teacher, local) as tg:   # labels (untimed)
         e, f, st, _ = tg.efs(batch)
@@ -512,7 +509,7 @@ def run_train(args, torch, dist, ws, rank, local, dev, stream):
         gpu.loss_grad_device(te_d, tf_d, ts_d, loss_d, metrics_d, grad_d, TRAIN_WEIGHTS,
                              norm_count=total)
         if ws > 1:
-            dist.all_reduce(out)
+            allreduce_loss_grad(dist, out)
 
     for _ in range(args.train_warmup):
         step()
@@ -619,50 +616,57 @@ def run_ours(args):
                                 device_id=dev)
     model = read_mtp(MODEL)
     st = configs.config3(reps=args.reps)
-    slab = ws > 1   # one box over all ranks: slabs along x, collectives per step
-    if slab:
-        from mtpb200.slab import SlabExchange, SlabLayout
-        L = SlabLayout(st["cell"], st["positions"], ws)
-        pos_slab = np.ascontiguousarray(st["positions"][L.order])
-        types_slab = np.ascontiguousarray(st["types"][L.order]).astype(np.int32)
-        st = dict(st, positions=L.to_local(pos_slab, rank), types=L.to_local(types_slab, rank))
-        n_own = int(L.counts[rank])
-    batch = StructureBatch.from_structures([st])
-    N = batch.n_atoms
+    N = len(st["types"])
+    # MD-style steps: positions of step k are base + D[k % 4], with four
+    # seeded displacement fields |D| <= DISP_AMPLITUDE per component, so any
+    # two steps differ by less than skin/2 and the lists stay valid between
+    # rebuilds (the reuse steps recompute every edge vector)
+    rng = np.random.default_rng(DISP_SEED)
+    disp = rng.uniform(-DISP_AMPLITUDE, DISP_AMPLITUDE, (N, 3 * N_DISP))
+    assert 2 * DISP_AMPLITUDE * 3 ** 0.5 < SKIN / 2
     gpu = MTPGpuDirect(model, local)
+    gpu.set_skin(SKIN)
     # a dedicated stream shared by the library and the timing events
     stream = torch.cuda.Stream(dev)
     torch.cuda.set_stream(stream)
     gpu.set_stream(stream.cuda_stream)
+    slab = ws > 1   # one box over all ranks: x-slabs with a ghost-atom halo
     if slab:
-        gpu.set_center_count(n_own)
-        X = SlabExchange(L, rank, dist, dev)
-        own_d = torch.from_numpy(pos_slab[L.starts[rank]:L.starts[rank + 1]]).to(dev)
-
-    # device-resident inputs and outputs
-    offs_d = torch.from_numpy(batch.atom_offsets).to(dev)
-    cells_d = torch.from_numpy(batch.cells).to(dev)
-    pbc_d = torch.ones((1, 3), dtype=torch.int32, device=dev)
-    pos_d = torch.from_numpy(batch.positions).to(dev)
-    types_d = torch.from_numpy(batch.types).to(dev)
-    energy_d = torch.zeros(1, dtype=torch.float64, device=dev)
-    forces_d = torch.zeros((N, 3), dtype=torch.float64, device=dev)
-    stress_d = torch.zeros((1, 9), dtype=torch.float64, device=dev)
-    totals_d = torch.zeros(10, dtype=torch.float64, device=dev)
-    f_own = None
+        from mtpb200.slab import DistributedSlab, SlabDomain, SlabEFS, halo_bytes_per_step
+        D = SlabDomain(st["cell"], ws, rank, model.cutoff + SKIN, device=dev)
+        D.assign(st["positions"], st["types"], payload=disp)
+        S = SlabEFS(gpu, DistributedSlab(D, dist))
+        base = None
+        f_own = None
+    else:
+        batch = StructureBatch.from_structures([st])
+        offs_d = torch.from_numpy(batch.atom_offsets).to(dev)
+        cells_d = torch.from_numpy(batch.cells).to(dev)
+        pbc_d = torch.ones((1, 3), dtype=torch.int32, device=dev)
+        base_d = torch.from_numpy(batch.positions).to(dev)
+        disp_d = torch.from_numpy(disp).to(dev)
+        pos_d = torch.empty_like(base_d)
+        types_d = torch.from_numpy(batch.types).to(dev)
+        energy_d = torch.zeros(1, dtype=torch.float64, device=dev)
+        forces_d = torch.zeros((N, 3), dtype=torch.float64, device=dev)
+        stress_d = torch.zeros((1, 9), dtype=torch.float64, device=dev)
+    totals_d = None
 
     def step(k):
-        nonlocal f_own
-        x = pos_d
-        if slab:   # (1) positions of every slab, in this rank's rotated order
-            x = L.to_local(X.gather_positions(own_d), rank)
-        gpu.efs_device(offs_d, cells_d, pbc_d, x, types_d, energy_d, forces_d, stress_d,
-                       reuse_neighbors=(k % REBUILD_EVERY) != 0)
-        if slab:   # (3) sum partial forces into the owners, totals everywhere
-            f_own = X.reduce_forces(L.to_slab(forces_d, rank))
-            totals_d[0:1].copy_(energy_d)
-            totals_d[1:].copy_(stress_d.view(-1))
-            X.reduce_totals(totals_d)
+        nonlocal base, f_own, totals_d
+        j = 3 * (k % N_DISP)
+        rebuild = k % REBUILD_EVERY == 0
+        if slab:
+            if base is not None:
+                D.pos = base + D.payload[:, j:j + 3]
+            if rebuild:    # migration, halo lists, then a list build
+                S.rebuild()
+                base = D.pos - D.payload[:, j:j + 3]
+            f_own, totals_d = S.compute()
+        else:
+            torch.add(base_d, disp_d[:, j:j + 3], out=pos_d)
+            gpu.efs_device(offs_d, cells_d, pbc_d, pos_d, types_d, energy_d, forces_d, stress_d,
+                           reuse_neighbors=not rebuild)
 
     def barrier():
         if ws > 1:
@@ -696,6 +700,9 @@ def run_ours(args):
     barrier()
     clocks = sampler.stop()
     ms = max_over_ranks(t0.elapsed_time(t1))
+    halo = halo_bytes_per_step(D) if slab else None
+    n_centers = D.n_own if slab else N
+    n_ghost = D.n_ghost if slab else 0
     # per-kernel device time of a reuse step and of a rebuild step (events
     # recorded by the library on the same stream)
     step(1)
@@ -714,35 +721,46 @@ def run_ours(args):
             dist.destroy_process_group()
         return None
     # end-to-end through the public host API: pinned host buffers, H2D of the
-    # positions every step (types and cell too on rebuild steps), D2H of the
-    # energy, forces and virial every step; with slabs each rank copies its own
-    # slab in and its own forces and the totals out
+    # positions every step, D2H of the energy, forces and virial every step.
+    # With slabs each rank copies its owned atoms' positions in and their
+    # forces and the totals out, and at a rebuild (which changes ownership)
+    # reads the new owned positions back.
     n_rebuild = sum(1 for k in range(args.steps) if k % REBUILD_EVERY == 0)
     if slab:
-        own_h = torch.from_numpy(pos_slab[L.starts[rank]:L.starts[rank + 1]].copy()).pin_memory()
-        f_h = torch.zeros((n_own, 3), dtype=torch.float64).pin_memory()
+        cap = N
+        base_h = torch.zeros((cap, 3), dtype=torch.float64).pin_memory()
+        f_h = torch.zeros((cap, 3), dtype=torch.float64).pin_memory()
         t_h = torch.zeros(10, dtype=torch.float64).pin_memory()
+        base_h[:base.shape[0]].copy_(base)
+        own_n = [base.shape[0]]
 
         def e2e_step(k):
-            own_d.copy_(own_h, non_blocking=True)
+            nonlocal base
+            n = own_n[0]
+            base = base_h[:n].to(dev, non_blocking=True)
             step(k)
-            f_h.copy_(f_own, non_blocking=True)
+            if k % REBUILD_EVERY == 0:
+                own_n[0] = base.shape[0]
+                base_h[:own_n[0]].copy_(base, non_blocking=True)
+            f_h[:f_own.shape[0]].copy_(f_own, non_blocking=True)
             t_h.copy_(totals_d, non_blocking=True)
             stream.synchronize()
 
-        h2d = n_own * 24
-        d2h = n_own * 24 + 80
+        h2d = n_centers * 24
+        d2h = n_centers * 24 + 80 + n_rebuild * n_centers * 24 / args.steps
     else:
-        pos_h = torch.from_numpy(batch.positions).pin_memory()
+        pos_h = [torch.from_numpy(st["positions"] + disp[:, 3 * j:3 * j + 3]).pin_memory()
+                 for j in range(N_DISP)]
         types_h = torch.from_numpy(batch.types).pin_memory()
-        hb = StructureBatch(batch.atom_offsets, batch.cells, None, pos_h.numpy(),
-                            types_h.numpy())
+        hbs = [StructureBatch(batch.atom_offsets, batch.cells, None, p.numpy(), types_h.numpy())
+               for p in pos_h]
         out = {"energy": torch.zeros(1, dtype=torch.float64).pin_memory().numpy(),
                "forces": torch.zeros((N, 3), dtype=torch.float64).pin_memory().numpy(),
                "stress": torch.zeros((1, 9), dtype=torch.float64).pin_memory().numpy()}
 
         def e2e_step(k):
-            gpu.efs_structures(hb, reuse_neighbors=(k % REBUILD_EVERY) != 0, out=out)
+            gpu.efs_structures(hbs[k % N_DISP], reuse_neighbors=(k % REBUILD_EVERY) != 0,
+                               out=out)
 
         h2d = (N * 24 * args.steps + n_rebuild * (N * 4 + 9 * 8 + 8)) / args.steps
         d2h = N * 24 + 8 + 72
@@ -758,7 +776,14 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    # both loops end on step steps-1 from the same rebuild, so the energies agree
+    step_last = args.steps - 1
     e2e_energy = float(t_h[0]) if slab else float(out["energy"][0])
+    step(step_last - step_last % REBUILD_EVERY)
+    for k in range(step_last - step_last % REBUILD_EVERY + 1, step_last + 1):
+        step(k)
+    torch.cuda.synchronize()
+    energy = float(totals_d[0].item()) if slab else float(energy_d.item())
     e2e_ok = abs(e2e_energy - energy) <= 1e-9 * max(1.0, abs(energy))
 
     train = None if args.no_train else run_train(args, torch, dist, ws, rank, local, dev, stream)
@@ -772,12 +797,12 @@ def run_ours(args):
         return None
     # roofline of the dominant kernel (FP64 CUDA-core bound)
     recs = dag_record_count(model)
-    fm = flop_model(model, len([v for v in model.basis_shape() if v >= 0]), edges / N, recs)
+    fm = flop_model(model, len([v for v in model.basis_shape() if v >= 0]), edges / n_centers,
+                    recs)
     names = {1: ("k_moments<fwd>", fm["fwd_per_atom"]), 2: ("k_dag", fm["dag_per_atom"]),
              3: ("k_moments<rev>", fm["rev_per_atom"])}
     dom = max(names, key=lambda i: kernel_ms[i])
     kname, kflops = names[dom]
-    n_centers = n_own if slab else N
     achieved = kflops * n_centers / (kernel_ms[dom] / 1e3) / 1e12
     total_atoms = N * (1 if slab else ws) * args.steps
     value = total_atoms / (ms / 1e3)
@@ -811,16 +836,27 @@ def run_ours(args):
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-        "scaling": "strong" if slab else "weak", "vs_baseline": None, "dtype": "f64",
-        "data": "synthetic (seeded Ni3Al L1_2 box, seeded level-20 coefficients)",
-        "config": {"workload": f"config 3: {N}-atom Ni3Al box, level-20 MTP, EFS steps with a "
-                               f"neighbour rebuild every {REBUILD_EVERY} steps"
-                               + (f"; one box over {ws} GPUs in x-slabs (all-gather of "
-                                  "positions, reduce-scatter of partial forces, all-reduce "
-                                  "of energy and virial every step)" if slab else ""),
-                   "atoms_per_gpu": n_centers, "edges_per_gpu": edges, "level": 20,
-                   "species": 2, "rb_size": 8, "r_cut": 5.0, "skin": 0.0,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (seeded Ni3Al L1_2 box, seeded level-20 coefficients, seeded "
+                "per-step displacements)",
+        "config": {"workload": f"config 3: {N}-atom Ni3Al box, level-20 MTP, MD-style EFS "
+                               f"steps (positions move every step by seeded displacements, "
+                               f"neighbour lists with a {SKIN} A skin rebuilt every "
+                               f"{REBUILD_EVERY} steps, every edge vector recomputed on the "
+                               "steps between)"
+                               + (f"; one box over {ws} GPUs in x-slabs with ghost layers of "
+                                  f"r_c + skin: per step a grouped P2P exchange of halo "
+                                  "positions, EFS of the owned atoms, reverse exchange of "
+                                  "ghost forces, all-reduce of energy and virial; atoms "
+                                  "migrate between slabs at rebuilds" if slab else ""),
+                   "atoms_per_gpu": n_centers, "ghost_atoms_per_gpu": n_ghost,
+                   "edges_per_gpu": edges, "level": 20,
+                   "species": 2, "rb_size": 8, "r_cut": 5.0, "skin": SKIN,
+                   "displacement": f"{N_DISP} seeded fields U(-{DISP_AMPLITUDE}, "
+                                   f"{DISP_AMPLITUDE}) A per component, cycled (seed "
+                                   f"{DISP_SEED}); any two steps differ by < skin/2",
                    "parallelism": f"slab{ws}" if slab else "single",
+                   "halo_bytes_per_step_rank0": halo,
                    "l2": "working set ~6 GB per GPU, larger than L2 (no flush)"},
         "e2e": {"value": total_atoms / (e2e_ms / 1e3), "unit": UNIT,
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
@@ -831,8 +867,9 @@ def run_ours(args):
                       "moments_fwd": float(kernel_ms[1]), "graph": float(kernel_ms[2]),
                       "moments_rev": float(kernel_ms[3]), "gather_reduce": float(kernel_ms[4])},
         "step_tflops_executed": (fm["fwd_per_atom"] + fm["rev_per_atom"] + fm["dag_per_atom"])
-        * N / (step_ms / 1e3) / 1e12,
-        "step_tflops_ref_formulation": fm["ref_formulation_per_atom"] * N / (step_ms / 1e3) / 1e12,
+        * n_centers / (step_ms / 1e3) / 1e12,
+        "step_tflops_ref_formulation": fm["ref_formulation_per_atom"] * n_centers
+        / (step_ms / 1e3) / 1e12,
         "clocks": clocks,
         "energy_eV": energy,
     }

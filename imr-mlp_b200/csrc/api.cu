@@ -239,7 +239,8 @@ EdgeArgs edge_args(const mtpb_context *c, int ncenter, const int *types, const i
 // forward moments -> graph -> reverse moments for ncenter centres.
 int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offsets,
                 const int *nbr, const double *rx, const double *ry, const double *rz,
-                double *site_energy, double *dx, double *dy, double *dz, bool reverse)
+                double *site_energy, double *dx, double *dy, double *dz, bool reverse,
+                long nedges, bool beyond_cutoff)
 {
     c->npad = ((ncenter + 31) / 32) * 32;
     c->d_group_maxdeg = c->arena.get<int>("group_maxdeg", c->npad / 32 + 1);
@@ -250,6 +251,23 @@ int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offse
     CUDA_TRY(launch_group_maxdeg(ncenter, offsets, c->d_group_maxdeg, c->stream), "group_maxdeg");
     c->launches++;
     EdgeArgs a = edge_args(c, ncenter, types, offsets, nbr, rx, ry, rz);
+    // lists that hold pairs beyond the cutoff (a skin, a caller's list) are
+    // staged through their active edges; the training kernels keep the full
+    // list and its degree table
+    if (beyond_cutoff && nedges > 0 && ncenter > 0) {
+        int *active = c->arena.get<int>("active_edges", nedges + 1);
+        int *nact = c->arena.get<int>("active_count", ncenter + 1);
+        int *gmax = c->arena.get<int>("group_maxdeg_active", c->npad / 32 + 1);
+        if (!active || !nact || !gmax)
+            return fail(MTPB_ERR_MEMORY, "device allocation for the active edges failed");
+        CUDA_TRY(launch_active_edges(a, active, nact, gmax, reverse ? dx : nullptr,
+                                     reverse ? dy : nullptr, reverse ? dz : nullptr, c->stream),
+                 "active edges");
+        c->launches += 2;
+        a.active = active;
+        a.nact = nact;
+        a.group_maxdeg = gmax;
+    }
     CUDA_TRY(cudaEventRecord(c->ev[1], c->stream), "event");
     CUDA_TRY(launch_moments_fwd(c->shape, a, basic, c->stream), "moments forward");
     c->launches += moment_kernel_parts(c->shape, false);
@@ -766,8 +784,9 @@ int mtpb::efs_compute(mtpb_context *c, int memory, const mtpb_efs_output *out,
                                                  : c->arena.get<double>("stress", 9 * (size_t)S + 9);
     if (!site_energy || !dx || !dy || !dz || !forces || !avir || !partials || !energy || !stress)
         return fail(MTPB_ERR_MEMORY, "device allocation failed");
+    // with a skin the list holds pairs up to r_c + skin
     rc = run_moments(c, N, c->d_types, c->nb.offsets, c->nb.nbr, c->nb.rx, c->nb.ry, c->nb.rz,
-                     site_energy, dx, dy, dz, forces_needed);
+                     site_energy, dx, dy, dz, forces_needed, E, c->skin > 0.0);
     if (rc)
         return rc;
     if (forces_needed) {

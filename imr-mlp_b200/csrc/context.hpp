@@ -108,9 +108,12 @@ int set_device(mtpb_context *c);
 int check_device_error(mtpb_context *c);
 EdgeArgs edge_args(const mtpb_context *c, int ncenter, const int *types, const int *offsets,
                    const int *nbr, const double *rx, const double *ry, const double *rz);
+// beyond_cutoff: the list may hold pairs beyond the model cutoff (a skin or a
+// caller's list), which are then skipped through an active-edge list
 int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offsets,
                 const int *nbr, const double *rx, const double *ry, const double *rz,
-                double *site_energy, double *dx, double *dy, double *dz, bool reverse = true);
+                double *site_energy, double *dx, double *dy, double *dz, bool reverse,
+                long nedges, bool beyond_cutoff);
 int efs_compute(mtpb_context *c, int memory, const mtpb_efs_output *out, bool forces_needed);
 int csr_compute(mtpb_context *c, const mtpb_csr_request *req, int memory);
 int lammps_compute(mtpb_context *c, const mtpb_lammps_request *req);

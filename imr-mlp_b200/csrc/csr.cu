@@ -183,7 +183,10 @@ int csr_compute_impl(mtpb_context *c, const mtpb_csr_request *r, int memory,
     NbResult res;
     CUDA_TRY(build_in_edges(NT, E, d_nbr, c->arena, res, s), "in-edge lists");
     CUDA_TRY(cudaEventRecord(c->ev[0], s), "event");
-    rc = run_moments(c, NC, d_types, d_off, d_nbr, rx, ry, rz, site_energy, dx, dy, dz);
+    // caller lists (LAMMPS full lists with their skin) may hold pairs beyond
+    // the cutoff
+    rc = run_moments(c, NC, d_types, d_off, d_nbr, rx, ry, rz, site_energy, dx, dy, dz, true, E,
+                     true);
     if (rc)
         return rc;
     CUDA_TRY(launch_force_gather(NC, NT, d_off, res.in_offsets, res.in_edges, dx, dy, dz, rx, ry,

@@ -45,6 +45,21 @@ template <class S, bool REV> constexpr int smem_doubles(int K, int R)
     return n;
 }
 
+// Edge id of staging slot `slot` of centre `atom`, through the active-edge
+// list when the call has one; false past the centre's (active) edges.
+__device__ __forceinline__ bool slot_edge(const EdgeArgs &p, int atom, int slot, int &e)
+{
+    const int b = __ldg(p.offsets + atom);
+    if (p.active) {
+        if (slot >= __ldg(p.nact + atom))
+            return false;
+        e = __ldg(p.active + b + slot);
+        return true;
+    }
+    e = b + slot;
+    return e < __ldg(p.offsets + atom + 1);
+}
+
 struct StageView {
     double *st;       // [rows][KS][STR]
     double *part;     // [NW][3][KS][32] (reverse only)
@@ -75,9 +90,9 @@ __device__ __forceinline__ void stage_chunk(const EdgeArgs &p, const StageView &
         bool have = false;
         double x = 0.0, y = 0.0, z = 0.0;
         int pair = -1;
+        int e = 0;
         if (atom < p.natoms) {
-            const int e = __ldg(p.offsets + atom) + chunk * KS + k;
-            if (e < __ldg(p.offsets + atom + 1)) {
+            if (slot_edge(p, atom, chunk * KS + k, e)) {
                 have = true;
                 x = __ldg(p.rx + e);
                 y = __ldg(p.ry + e);
@@ -396,8 +411,8 @@ __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, 
             const int at = atom0 + ln;
             if (k >= kend || at >= p.natoms)
                 continue;
-            const int e = __ldg(p.offsets + at) + ch * KS + k;
-            if (e >= __ldg(p.offsets + at + 1))
+            int e;
+            if (!slot_edge(p, at, ch * KS + k, e))
                 continue;
             double sx = 0.0, sy = 0.0, sz = 0.0;
 #pragma unroll
@@ -568,6 +583,80 @@ int shape_slot(int id, int mu, int a, int b, int c)
 }
 
 // ----------------------------------------------------------------------------
+// Active-edge lists: one warp per centre tests its edges against the pair
+// cutoff with the staging arithmetic (r = sqrt((x*x + y*y) + z*z), the pair's
+// rmax, atoms of type -1 and r = 0 excluded) and compacts the active edge ids
+// in list order with a ballot, so that the moment kernels stage the same
+// edges in the same order as without the list and skip only slots that would
+// add exact zeros.  Inactive edges get zero derivatives.
+// ----------------------------------------------------------------------------
+__global__ void k_active_edges(EdgeArgs p, int *__restrict__ active, int *__restrict__ nact,
+                               double *__restrict__ dx, double *__restrict__ dy,
+                               double *__restrict__ dz)
+{
+    const int lane = threadIdx.x & 31;
+    const int atom = (int)(((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    if (atom >= p.natoms)
+        return;
+    const int b = __ldg(p.offsets + atom), end = __ldg(p.offsets + atom + 1);
+    const int it = __ldg(p.types + atom);
+    int count = 0;
+    for (int base = b; base < end; base += 32) {
+        const int e = base + lane;
+        bool act = false;
+        if (e < end) {
+            int pair;
+            if (p.pair) {
+                pair = __ldg(p.pair + e);
+            } else {
+                const int jt = __ldg(p.types + __ldg(p.nbr + e));
+                pair = (it >= 0 && jt >= 0) ? it * p.K + jt : -1;
+            }
+            if (pair >= 0) {
+                const double x = __ldg(p.rx + e), y = __ldg(p.ry + e), z = __ldg(p.rz + e);
+                const double r2 = __dadd_rn(__dadd_rn(__dmul_rn(x, x), __dmul_rn(y, y)),
+                                            __dmul_rn(z, z));
+                const double r = sqrt(r2);
+                act = r > 0.0 && r <= p.pairs[pair].rmax;
+            }
+            if (!act && dx) {
+                dx[e] = 0.0;
+                dy[e] = 0.0;
+                dz[e] = 0.0;
+            }
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, act);
+        if (act)
+            active[b + count + __popc(m & ((1u << lane) - 1u))] = e;
+        count += __popc(m);
+    }
+    if (lane == 0)
+        nact[atom] = count;
+}
+
+__global__ void k_group_max_count(int natoms, const int *__restrict__ count, int *out)
+{
+    const int atom = blockIdx.x * blockDim.x + threadIdx.x;
+    int deg = atom < natoms ? count[atom] : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        deg = max(deg, __shfl_xor_sync(0xffffffffu, deg, o));
+    if ((threadIdx.x & 31) == 0 && atom - (int)(threadIdx.x & 31) < natoms)
+        out[atom >> 5] = deg;
+}
+
+cudaError_t launch_active_edges(const EdgeArgs &a, int *active, int *nact, int *group_maxdeg,
+                                double *dx, double *dy, double *dz, cudaStream_t s)
+{
+    if (a.natoms == 0)
+        return cudaSuccess;
+    const long threads = 32L * a.natoms;
+    k_active_edges<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(a, active, nact, dx, dy, dz);
+    k_group_max_count<<<(a.natoms + 255) / 256, 256, 0, s>>>(a.natoms, nact, group_maxdeg);
+    return cudaGetLastError();
+}
+
+// ----------------------------------------------------------------------------
 // Per-32-atom-group maximum neighbour count (chunk count of the edge kernels)
 // ----------------------------------------------------------------------------
 __global__ void k_group_maxdeg(int natoms, const int *offsets, int *out)
@@ -607,6 +696,27 @@ cudaError_t launch_group_maxdeg(int natoms, const int *offsets, int *group_maxde
 //   END:    GLOBAL ? adjoint[out][atom] = acc : row[out] = acc
 //   ENERGY: E += c * acc          (its own product is 0 * 0)
 // ----------------------------------------------------------------------------
+// Operand values of one device record for this lane's two atoms.  The
+// record's operand word holds two 16-bit row indices; the values DEV_ROW_ONE
+// (1.0) and DEV_ROW_ZERO (0.0) stand for constant rows and DEV_ROW_SAME as the
+// second index repeats the first (a square), so those operands cost no
+// shared-memory load.
+template <bool GR>
+__device__ __forceinline__ void dag_operands(const Rows<GR> &rowsA, unsigned ops, unsigned rs,
+                                             double2 &x, double2 &y)
+{
+    const unsigned i1 = ops & 0xffffu, i2 = ops >> 16;
+    if (i1 >= DEV_ROW_ZERO)
+        x = i1 == DEV_ROW_ONE ? make_double2(1.0, 1.0) : make_double2(0.0, 0.0);
+    else
+        x = rowsA.ld(i1 << rs);
+    if (i2 >= DEV_ROW_ZERO)
+        y = i2 == DEV_ROW_ONE ? make_double2(1.0, 1.0)
+                              : (i2 == DEV_ROW_SAME ? x : make_double2(0.0, 0.0));
+    else
+        y = rowsA.ld(i2 << rs);
+}
+
 // Runs n consecutive records of one stream.  All records belong to one
 // phase, so a row written here is never read here and record loads may move
 // ahead of stores.
@@ -654,8 +764,7 @@ __device__ __forceinline__ void dag_segment(unsigned rec_addr, const Rows<GR> &r
             const uint4 w = lds128(rec_addr + (k + u) * REC_STRIDE);
             g.of[u] = w.y;
             g.c[u] = __hiloint2double((int)w.w, (int)w.z);
-            g.x[u] = rowsA.ld((w.x & 0xffffu) << RS);
-            g.y[u] = rowsA.ld((w.x >> 16) << RS);
+            dag_operands(rowsA, w.x, RS, g.x[u], g.y[u]);
         }
     };
     auto accumulate = [&](const Grp &g) {
@@ -686,7 +795,8 @@ __device__ __forceinline__ void dag_segment(unsigned rec_addr, const Rows<GR> &r
     }
     for (; k < n; ++k) {
         const uint4 w = lds128(rec_addr + k * REC_STRIDE);
-        const double2 x = rowsA.ld((w.x & 0xffffu) << RS), y = rowsA.ld((w.x >> 16) << RS);
+        double2 x, y;
+        dag_operands(rowsA, w.x, RS, x, y);
         const double c = __hiloint2double((int)w.w, (int)w.z);
         acc[0] = fma(c * x.x, y.x, acc[0]);
         acc[1] = fma(c * x.y, y.y, acc[1]);
@@ -837,6 +947,24 @@ __global__ void __launch_bounds__(DagGeom<ATOMS, STREAMS>::THREADS)
     }
 }
 
+// Operand word of a device record: constant rows and squares become the
+// markers of dag_operands (a product with the zero row is zero whatever the
+// other operand, so both become DEV_ROW_ZERO; the constant one goes second).
+static unsigned dev_operands(const DagPlan &plan, unsigned s12)
+{
+    unsigned a = s12 & 0xffffu, b = s12 >> 16;
+    const unsigned one = (unsigned)plan.one_row, zero = (unsigned)plan.zero_row;
+    if (a == zero || b == zero)
+        return DEV_ROW_ZERO | (DEV_ROW_ZERO << 16);
+    if (a == one)
+        std::swap(a, b);
+    if (b == one)
+        return a == one ? (DEV_ROW_ONE | (DEV_ROW_ONE << 16)) : (a | (DEV_ROW_ONE << 16));
+    if (a == b)
+        return a | (DEV_ROW_SAME << 16);
+    return a | (b << 16);
+}
+
 // Device records of a plan: warp-major per phase ([phase][warp][row][SPW
 // streams]) for the selected block geometry; store targets become byte
 // offsets, operand rows stay indices.
@@ -854,7 +982,7 @@ std::vector<DagDevRec> dag_device_records(const DagPlan &plan)
                 for (int s = 0; s < spw; ++s) {
                     const DagRec &in = plan.recs[(row0 + r) * S + w * spw + s];
                     DagDevRec d{};
-                    d.rows = in.s12;   // row indices; the kernel scales them
+                    d.rows = dev_operands(plan, in.s12);   // the kernel scales row indices
                     d.c = in.c;
                     const unsigned flags = in.outf >> 16, out_ = in.outf & 0xffffu;
                     unsigned f = 0;

@@ -132,6 +132,11 @@ struct EdgeArgs {
     const double *rx, *ry, *rz;  // [E]
     const int *pair;             // [E] species pair it*K+jt (-1: a type is -1), or NULL
     const int *group_maxdeg;     // [ceil(natoms/32)]
+    // optional active-edge list (edges inside the pair cutoff): the k-th
+    // active edge of centre i is active[offsets[i] + k], k < nact[i]; NULL
+    // stages every edge of the list
+    const int *active;
+    const int *nact;
     int K, R, mu_total;
     double scaling;
     const double *radial;          // [K*K][mu_total][R]
@@ -143,6 +148,12 @@ struct EdgeArgs {
 int moment_kernel_parts(int shape, bool rev);
 int grad_kernel_launches(int shape, bool edge);
 cudaError_t launch_moments_fwd(int shape, const EdgeArgs &a, double *basic, cudaStream_t s);
+// Active-edge list of a neighbour list whose edges may reach beyond the pair
+// cutoff (a skin or a caller's list): active/nact as in EdgeArgs, the largest
+// active count of every 32-centre group in group_maxdeg, and zero per-edge
+// derivatives dx/dy/dz (may be NULL) for the inactive edges.
+cudaError_t launch_active_edges(const EdgeArgs &a, int *active, int *nact, int *group_maxdeg,
+                                double *dx, double *dy, double *dz, cudaStream_t s);
 cudaError_t launch_moments_rev(int shape, const EdgeArgs &a, const double *adjoint, double *dx,
                                double *dy, double *dz, cudaStream_t s);
 size_t dag_ring_bytes(int atoms);

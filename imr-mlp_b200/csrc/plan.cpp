@@ -450,7 +450,9 @@ static bool build_dag_plan_streams(const ModelHost &m, int shape,
         nrev += emit_phase(items, plan, pool);
     }
     plan.n_rev = nrev;
-    if (plan.nrows >= 65535 || (int)plan.phase_rows.size() > DAG_MAX_PHASES) {
+    // row indices are 16-bit and the graph kernel reserves 0xfffd-0xffff as
+    // operand markers
+    if (plan.nrows >= 0xfffd || (int)plan.phase_rows.size() > DAG_MAX_PHASES) {
         if (err)
             *err = "moment graph too large (" + std::to_string(plan.nrows) + " rows, " +
                    std::to_string(plan.phase_rows.size()) + " phases)";
@@ -476,9 +478,9 @@ bool build_dag_plan(const ModelHost &m, int shape, const std::vector<int> &slot_
     return true;
 }
 
-// Eigen fixed-size 3x3 inverse order (see oracle/mtp_oracle.c inverse3 for
-// the bit-level check against Eigen): det = (c0*m00 + c1*m10) + c2*m20,
-// inv(i,j) = cofactor(j,i) * (1/det).
+// Eigen's fixed-size 3x3 inverse in its own operation order (the order the
+// reference's Atoms::cell_.inverse() rounds in, base/neighborhoods_base.h:
+// 113-126): det = (c0*m00 + c1*m10) + c2*m20, inv(i,j) = cofactor(j,i) * (1/det).
 static double cof3(const double *m, int i, int j)
 {
     int i1 = (i + 1) % 3, i2 = (i + 2) % 3, j1 = (j + 1) % 3, j2 = (j + 2) % 3;

@@ -424,3 +424,51 @@ def halo_bytes_per_step(domain: SlabDomain) -> Dict[str, int]:
     fwd = 24 * sum(domain.send_counts().values())
     rev = 24 * domain.n_ghost
     return {"forward": fwd, "reverse": rev, "totals": 80}
+
+
+class SlabEFS:
+    """One rank's EFS step of a slab decomposition through the library: the
+    step a domain-decomposed MD code runs every time step.  `rebuild()` (every
+    few steps) migrates atoms and remakes the halo, and the next `compute`
+    rebuilds the neighbour lists of the local structure; `compute()` exchanges
+    ghost positions, evaluates the owned centres (device arrays, the
+    library's context stream), returns ghost forces to their owners and
+    all-reduces energy and virial.  Returns (owned forces [n_own, 3],
+    totals [10] = energy, virial row-major)."""
+
+    def __init__(self, gpu, transport: DistributedSlab):
+        torch = _torch()
+        self.gpu = gpu
+        self.t = transport
+        self.d = transport.d
+        dev = self.d.device
+        self.totals = torch.zeros(10, dtype=torch.float64, device=dev)
+        self._pbc = torch.ones((1, 3), dtype=torch.int32, device=dev)
+        self._cell = torch.as_tensor(self.d.local_cell.reshape(1, 9), dtype=torch.float64,
+                                     device=dev)
+        self._built = False
+
+    def rebuild(self):
+        torch = _torch()
+        d = self.d
+        self.t.rebuild()
+        n_local = d.n_own + d.n_ghost
+        self.gpu.set_center_count(d.n_own)
+        dev = d.device
+        self._offs = torch.tensor([0, n_local], dtype=torch.int32, device=dev)
+        self._types = d.local_types().contiguous()
+        self._e = torch.zeros(1, dtype=torch.float64, device=dev)
+        self._f = torch.zeros((n_local, 3), dtype=torch.float64, device=dev)
+        self._s = torch.zeros((1, 9), dtype=torch.float64, device=dev)
+        self._built = False
+
+    def compute(self):
+        x = self.t.positions()
+        self.gpu.efs_device(self._offs, self._cell, self._pbc, x, self._types, self._e, self._f,
+                            self._s, reuse_neighbors=self._built)
+        self._built = True
+        f_own = self.t.forces(self._f)
+        self.totals[0:1].copy_(self._e)
+        self.totals[1:].copy_(self._s.view(-1))
+        self.t.totals(self.totals)
+        return f_own, self.totals

@@ -476,3 +476,76 @@ class ReferenceGpu:
         if rc:
             raise RuntimeError(self.lib.refgpu_last_error().decode())
         return metrics, grad, f, se, sv
+
+
+class ReferenceBinding:
+    """The reference-side binding (MTPB200Direct, imr-mlp_b200/bindings/
+    mtpb_direct.hpp) compiled against the reference headers with its
+    mlip.cpp into ``_ref/librefdirect.so`` (ref_direct_shim.cpp).  Test
+    infrastructure: checks that a maintainer's drop-in of the binding
+    reproduces MLIPCore::compute."""
+
+    def __init__(self, mtp_text: str, species: int, device: int = 0,
+                 path: Optional[str] = None):
+        self.lib = L = C.CDLL(path or os.path.join(HERE, "_ref", "librefdirect.so"))
+        L.refdirect_last_error.restype = C.c_char_p
+        L.refdirect_create.restype = C.c_void_p
+        L.refdirect_create.argtypes = [C.c_char_p, C.c_int, C.c_int]
+        L.refdirect_destroy.argtypes = [C.c_void_p]
+        L.refdirect_compute_batch.argtypes = [C.c_void_p, C.c_int, C.c_int, _ip, _ip, _dp, _ip,
+                                              _dp, _dp, _dp, _dp, _dp, _dp]
+        L.refdirect_compute_lammps.argtypes = [C.c_void_p, C.c_int, _ip, C.c_int, _ip, _dp, _ip,
+                                               _ip, _ip, C.c_int, _dp, _dp, _dp, _dp, _dp]
+        self.handle = L.refdirect_create(mtp_text.encode(), species, device)
+        if not self.handle:
+            raise RuntimeError(L.refdirect_last_error().decode())
+
+    @staticmethod
+    def available(path: Optional[str] = None) -> bool:
+        return os.path.exists(path or os.path.join(HERE, "_ref", "librefdirect.so"))
+
+    def close(self):
+        if self.handle:
+            self.lib.refdirect_destroy(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def compute_batch(self, center_count, offsets, neighbors, types, x, vectors=None):
+        nt = len(types)
+        f = np.zeros((nt, 3))
+        e = np.zeros(1)
+        se = np.zeros(max(center_count, 1))
+        sv = np.zeros((nt, 6))
+        gv = np.zeros(6)
+        c = lambda a, t=np.float64: np.ascontiguousarray(a, dtype=t)   # noqa: E731
+        off, nbr, ty, xx = c(offsets, np.int32), c(neighbors, np.int32), c(types, np.int32), c(x)
+        vec = None if vectors is None else c(vectors)
+        rc = self.lib.refdirect_compute_batch(self.handle, center_count, nt, _i(off), _i(nbr),
+                                              _d(vec), _i(ty), _d(xx), _d(f), _d(e), _d(se),
+                                              _d(sv), _d(gv))
+        if rc:
+            raise RuntimeError(self.lib.refdirect_last_error().decode())
+        return dict(energy=float(e[0]), force=f, site_energy=se[:center_count], site_virial=sv,
+                    virial=gv)
+
+    def compute_lammps(self, ilist, types, x, numneigh, first_off, flat, mask, force,
+                       site_virial):
+        """Adds forces into `force` (and per-atom virials into site_virial)."""
+        nt = len(types)
+        e = np.zeros(1)
+        se = np.zeros(nt)
+        gv = np.zeros(6)
+        c = lambda a, t=np.int32: np.ascontiguousarray(a, dtype=t)   # noqa: E731
+        xx = np.ascontiguousarray(x, dtype=np.float64)
+        rc = self.lib.refdirect_compute_lammps(self.handle, len(ilist), _i(c(ilist)), nt,
+                                               _i(c(types)), _d(xx), _i(c(numneigh)),
+                                               _i(c(first_off)), _i(c(flat)), mask, _d(e), _d(se),
+                                               _d(force), _d(site_virial), _d(gv))
+        if rc:
+            raise RuntimeError(self.lib.refdirect_last_error().decode())
+        return float(e[0]), se, gv

@@ -94,7 +94,8 @@ def small_cells(seed: int = 21):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("IMRMLP_REFERENCE", "/root/reference"),
+                    help="reference checkout (default: $IMRMLP_REFERENCE)")
     args = ap.parse_args()
     from oracle import Oracle, Reference
     O, R = Oracle(), Reference()

@@ -77,7 +77,8 @@ def test_mtp_parser_rejects_bad_graph():
 def test_mtp_parser_reads_reference_templates():
     """The shipped Shapeev templates parse with the PotMTP scaling default."""
     from mtpb200 import read_mtp
-    corpus = "/root/reference/unitest/test-data/mtp-basis-corpus"
+    corpus = os.path.join(os.environ.get("IMRMLP_REFERENCE", "/root/reference"),
+                          "unitest", "test-data", "mtp-basis-corpus")
     if not os.path.isdir(corpus):
         pytest.skip("reference checkout absent")
     m = read_mtp(os.path.join(corpus, "shapeev-20.mtp"))
