@@ -112,8 +112,6 @@ template <> struct Rows<true> {
 };
 
 constexpr unsigned DEV_END = 1u << 28, DEV_GLOBAL = 2u << 28, DEV_ENERGY = 4u << 28;
-// operand markers of k_dag device records (row indices stay below them)
-constexpr unsigned DEV_ROW_ZERO = 0xfffdu, DEV_ROW_SAME = 0xfffeu, DEV_ROW_ONE = 0xffffu;
 constexpr unsigned DEV_OUT_MASK = (1u << 28) - 1;
 
 __device__ __forceinline__ void cp_async16(unsigned dst, const void *src)

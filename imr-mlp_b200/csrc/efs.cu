@@ -45,19 +45,23 @@ template <class S, bool REV> constexpr int smem_doubles(int K, int R)
     return n;
 }
 
-// Edge id of staging slot `slot` of centre `atom`, through the active-edge
-// list when the call has one; false past the centre's (active) edges.
+// Edge id of staging slot `slot` of centre `atom`: through the active-edge
+// list (ACT) or directly; false past the centre's (active) edges.  ACT is a
+// compile-time choice so that each moment kernel carries one path only (the
+// reverse kernel runs at the limit of the instruction cache).
+template <bool ACT>
 __device__ __forceinline__ bool slot_edge(const EdgeArgs &p, int atom, int slot, int &e)
 {
     const int b = __ldg(p.offsets + atom);
-    if (p.active) {
+    if constexpr (ACT) {
         if (slot >= __ldg(p.nact + atom))
             return false;
         e = __ldg(p.active + b + slot);
         return true;
+    } else {
+        e = b + slot;
+        return e < __ldg(p.offsets + atom + 1);
     }
-    e = b + slot;
-    return e < __ldg(p.offsets + atom + 1);
 }
 
 struct StageView {
@@ -71,7 +75,7 @@ struct StageView {
 // atoms of this block.  Every thread of the block takes part.
 // RG: the model has radial families other than RBChebyshev (radial.cuh);
 // the RBChebyshev-only kernels carry none of their code.
-template <class S, int NW, bool REV, bool RG>
+template <class S, int NW, bool REV, bool RG, bool ACT>
 __device__ __forceinline__ void stage_chunk(const EdgeArgs &p, const StageView &v, int atom0,
                                             int chunk)
 {
@@ -92,7 +96,7 @@ __device__ __forceinline__ void stage_chunk(const EdgeArgs &p, const StageView &
         int pair = -1;
         int e = 0;
         if (atom < p.natoms) {
-            if (slot_edge(p, atom, chunk * KS + k, e)) {
+            if (slot_edge<ACT>(p, atom, chunk * KS + k, e)) {
                 have = true;
                 x = __ldg(p.rx + e);
                 y = __ldg(p.ry + e);
@@ -161,7 +165,7 @@ __device__ __forceinline__ void stage_chunk(const EdgeArgs &p, const StageView &
 // other over each chunk's edges (one pass per member keeps the
 // unrolled per-edge code small).
 // ----------------------------------------------------------------------------
-template <class S, int NW, int W0, int SUB, bool RG>
+template <class S, int NW, int W0, int SUB, bool RG, bool ACT>
 __device__ __forceinline__ void fwd_warp(const EdgeArgs &p, const StageView &v, int atom0,
                                          int maxdeg, double *basic)
 {
@@ -175,7 +179,7 @@ __device__ __forceinline__ void fwd_warp(const EdgeArgs &p, const StageView &v, 
         acc[i] = 0.0;
     const int nchunks = (maxdeg + KS - 1) / KS;
     for (int ch = 0; ch < nchunks; ++ch) {
-        stage_chunk<S, NW / SUB, false, RG>(p, v, atom0, ch);
+        stage_chunk<S, NW / SUB, false, RG, ACT>(p, v, atom0, ch);
         __syncthreads();
         const int kend = min(KS, maxdeg - ch * KS);
         static_for<SUB>([&](auto is) {
@@ -346,7 +350,7 @@ __device__ __forceinline__ void rev_edge(const StageView &v, int k, int lane,
 // order.  NWB is the warps of this block; the first part stores the sums,
 // later parts add to them.
 // ----------------------------------------------------------------------------
-template <class S, int NW, int W0, int SUB, int NWB, bool FIRST, bool RG>
+template <class S, int NW, int W0, int SUB, int NWB, bool FIRST, bool RG, bool ACT>
 __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, int atom0,
                                          int maxdeg, const double *adjoint, double *dx,
                                          double *dy, double *dz)
@@ -378,7 +382,7 @@ __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, 
     const int nchunks = (maxdeg + KS - 1) / KS;
     double *part = v.part + (size_t)(W0 % NWB) * 3 * KS * 32;
     for (int ch = 0; ch < nchunks; ++ch) {
-        stage_chunk<S, NW / SUB, true, RG>(p, v, atom0, ch);
+        stage_chunk<S, NW / SUB, true, RG, ACT>(p, v, atom0, ch);
         __syncthreads();
         const int kend = min(KS, maxdeg - ch * KS);
         static_for<SUB>([&](auto is) {
@@ -412,7 +416,7 @@ __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, 
             if (k >= kend || at >= p.natoms)
                 continue;
             int e;
-            if (!slot_edge(p, at, ch * KS + k, e))
+            if (!slot_edge<ACT>(p, at, ch * KS + k, e))
                 continue;
             double sx = 0.0, sy = 0.0, sz = 0.0;
 #pragma unroll
@@ -438,7 +442,7 @@ __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, 
 
 // PART: which block of NW warps of the NW * NPART chain partition this launch
 // runs
-template <class S, bool REV, int PART, bool RG>
+template <class S, bool REV, int PART, bool RG, bool ACT>
 __global__ void __launch_bounds__(ShapeCfg<S>::NW * 32, KCfg<S, REV>::BLOCKS)
     k_moments(EdgeArgs p, double *basic, const double *adjoint, double *dx, double *dy,
               double *dz)
@@ -477,10 +481,10 @@ __global__ void __launch_bounds__(ShapeCfg<S>::NW * 32, KCfg<S, REV>::BLOCKS)
         constexpr int W = PART * NW + WL;
         if (warp == WL) {
             if constexpr (REV)
-                rev_warp<S, NWT * SUB, W, SUB, NW, PART == 0, RG>(p, v, atom0, maxdeg, adjoint,
+                rev_warp<S, NWT * SUB, W, SUB, NW, PART == 0, RG, ACT>(p, v, atom0, maxdeg, adjoint,
                                                                   dx, dy, dz);
             else
-                fwd_warp<S, NWT * SUB, W, SUB, RG>(p, v, atom0, maxdeg, basic);
+                fwd_warp<S, NWT * SUB, W, SUB, RG, ACT>(p, v, atom0, maxdeg, basic);
         }
     });
 }
@@ -500,7 +504,10 @@ template <class S, bool REV> static cudaError_t launch_shape(const EdgeArgs &a, 
         constexpr int P = decltype(ip)::value;
         if (err != cudaSuccess)
             return;
-        auto kern = a.rb_generic ? k_moments<S, REV, P, true> : k_moments<S, REV, P, false>;
+        auto kern = a.rb_generic ? (a.active ? k_moments<S, REV, P, true, true>
+                                             : k_moments<S, REV, P, true, false>)
+                                 : (a.active ? k_moments<S, REV, P, false, true>
+                                             : k_moments<S, REV, P, false, false>);
         err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (err == cudaSuccess) {
             kern<<<groups, NW * 32, smem, s>>>(a, basic, adjoint, dx, dy, dz);
@@ -616,8 +623,15 @@ __global__ void k_active_edges(EdgeArgs p, int *__restrict__ active, int *__rest
                 const double x = __ldg(p.rx + e), y = __ldg(p.ry + e), z = __ldg(p.rz + e);
                 const double r2 = __dadd_rn(__dadd_rn(__dmul_rn(x, x), __dmul_rn(y, y)),
                                             __dmul_rn(z, z));
-                const double r = sqrt(r2);
-                act = r > 0.0 && r <= p.pairs[pair].rmax;
+                // the staging's test is sqrt(r2) <= rmax (sqrt correctly
+                // rounded, monotonic); r2 outside rmax^2 (1 -+ 4 eps) decides
+                // it without the square root, the thin band in between takes
+                // the staging's own expression
+                const double rmax = p.pairs[pair].rmax, q = rmax * rmax;
+                if (r2 <= q * (1.0 - 8.9e-16))
+                    act = r2 > 0.0;
+                else if (r2 < q * (1.0 + 8.9e-16))
+                    act = sqrt(r2) <= rmax;
             }
             if (!act && dx) {
                 dx[e] = 0.0;
@@ -696,27 +710,6 @@ cudaError_t launch_group_maxdeg(int natoms, const int *offsets, int *group_maxde
 //   END:    GLOBAL ? adjoint[out][atom] = acc : row[out] = acc
 //   ENERGY: E += c * acc          (its own product is 0 * 0)
 // ----------------------------------------------------------------------------
-// Operand values of one device record for this lane's two atoms.  The
-// record's operand word holds two 16-bit row indices; the values DEV_ROW_ONE
-// (1.0) and DEV_ROW_ZERO (0.0) stand for constant rows and DEV_ROW_SAME as the
-// second index repeats the first (a square), so those operands cost no
-// shared-memory load.
-template <bool GR>
-__device__ __forceinline__ void dag_operands(const Rows<GR> &rowsA, unsigned ops, unsigned rs,
-                                             double2 &x, double2 &y)
-{
-    const unsigned i1 = ops & 0xffffu, i2 = ops >> 16;
-    if (i1 >= DEV_ROW_ZERO)
-        x = i1 == DEV_ROW_ONE ? make_double2(1.0, 1.0) : make_double2(0.0, 0.0);
-    else
-        x = rowsA.ld(i1 << rs);
-    if (i2 >= DEV_ROW_ZERO)
-        y = i2 == DEV_ROW_ONE ? make_double2(1.0, 1.0)
-                              : (i2 == DEV_ROW_SAME ? x : make_double2(0.0, 0.0));
-    else
-        y = rowsA.ld(i2 << rs);
-}
-
 // Runs n consecutive records of one stream.  All records belong to one
 // phase, so a row written here is never read here and record loads may move
 // ahead of stores.
@@ -764,7 +757,8 @@ __device__ __forceinline__ void dag_segment(unsigned rec_addr, const Rows<GR> &r
             const uint4 w = lds128(rec_addr + (k + u) * REC_STRIDE);
             g.of[u] = w.y;
             g.c[u] = __hiloint2double((int)w.w, (int)w.z);
-            dag_operands(rowsA, w.x, RS, g.x[u], g.y[u]);
+            g.x[u] = rowsA.ld((w.x & 0xffffu) << RS);
+            g.y[u] = rowsA.ld((w.x >> 16) << RS);
         }
     };
     auto accumulate = [&](const Grp &g) {
@@ -795,8 +789,7 @@ __device__ __forceinline__ void dag_segment(unsigned rec_addr, const Rows<GR> &r
     }
     for (; k < n; ++k) {
         const uint4 w = lds128(rec_addr + k * REC_STRIDE);
-        double2 x, y;
-        dag_operands(rowsA, w.x, RS, x, y);
+        const double2 x = rowsA.ld((w.x & 0xffffu) << RS), y = rowsA.ld((w.x >> 16) << RS);
         const double c = __hiloint2double((int)w.w, (int)w.z);
         acc[0] = fma(c * x.x, y.x, acc[0]);
         acc[1] = fma(c * x.y, y.y, acc[1]);
@@ -947,24 +940,6 @@ __global__ void __launch_bounds__(DagGeom<ATOMS, STREAMS>::THREADS)
     }
 }
 
-// Operand word of a device record: constant rows and squares become the
-// markers of dag_operands (a product with the zero row is zero whatever the
-// other operand, so both become DEV_ROW_ZERO; the constant one goes second).
-static unsigned dev_operands(const DagPlan &plan, unsigned s12)
-{
-    unsigned a = s12 & 0xffffu, b = s12 >> 16;
-    const unsigned one = (unsigned)plan.one_row, zero = (unsigned)plan.zero_row;
-    if (a == zero || b == zero)
-        return DEV_ROW_ZERO | (DEV_ROW_ZERO << 16);
-    if (a == one)
-        std::swap(a, b);
-    if (b == one)
-        return a == one ? (DEV_ROW_ONE | (DEV_ROW_ONE << 16)) : (a | (DEV_ROW_ONE << 16));
-    if (a == b)
-        return a | (DEV_ROW_SAME << 16);
-    return a | (b << 16);
-}
-
 // Device records of a plan: warp-major per phase ([phase][warp][row][SPW
 // streams]) for the selected block geometry; store targets become byte
 // offsets, operand rows stay indices.
@@ -982,7 +957,7 @@ std::vector<DagDevRec> dag_device_records(const DagPlan &plan)
                 for (int s = 0; s < spw; ++s) {
                     const DagRec &in = plan.recs[(row0 + r) * S + w * spw + s];
                     DagDevRec d{};
-                    d.rows = dev_operands(plan, in.s12);   // the kernel scales row indices
+                    d.rows = in.s12;   // row indices; the kernel scales them
                     d.c = in.c;
                     const unsigned flags = in.outf >> 16, out_ = in.outf & 0xffffu;
                     unsigned f = 0;

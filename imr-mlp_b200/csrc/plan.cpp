@@ -450,9 +450,7 @@ static bool build_dag_plan_streams(const ModelHost &m, int shape,
         nrev += emit_phase(items, plan, pool);
     }
     plan.n_rev = nrev;
-    // row indices are 16-bit and the graph kernel reserves 0xfffd-0xffff as
-    // operand markers
-    if (plan.nrows >= 0xfffd || (int)plan.phase_rows.size() > DAG_MAX_PHASES) {
+    if (plan.nrows >= 65535 || (int)plan.phase_rows.size() > DAG_MAX_PHASES) {
         if (err)
             *err = "moment graph too large (" + std::to_string(plan.nrows) + " rows, " +
                    std::to_string(plan.phase_rows.size()) + " phases)";
