@@ -16,7 +16,8 @@
 // (mtp_gpu_direct.cu:6814-6870): the alpha index tables, the scalar mapping,
 // the coefficients and, per ordered species pair, the radial basis descriptor
 // (mlip::radial_basis_t, runtime/mtp/mlip.h:166-186), whose rb / cutoff /
-// transform enums share the numbering of mtpb_radial_family.  Atom types of
+// transform enums share the numbering of mtpb_radial_family; RBPolyB pairs
+// hand over the loader's orthogonalisation matrix and normalisations.  Atom types of
 // both requests go through the model's type mapping (mlip::mapping_data(), as
 // MLIPCore::compute does, mlip.cpp:910-964).
 #pragma once
@@ -74,6 +75,15 @@ class MTPB200Direct {
                 fam.push_back(family(b.rb, b.cutoff, b.transform, b.one_minus_chebyshev,
                                      b.cutoff_parameter, b.cutoff_r1, b.cutoff_r2,
                                      b.transform_parameter, b.transform_scale_parameter));
+                // RBPolyB / RBPolyBCos: the loader's own orthogonalisation
+                // matrix (ill-conditioned: it is data, not recomputed)
+                if (b.rb == MLIPCore::mlip::RB_POLYB || b.rb == MLIPCore::mlip::RB_POLYBCOS) {
+                    if (b.polynomial_matrix.size() != (size_t)p.rb_size * p.rb_size ||
+                        b.polynomial_normalizations.size() != (size_t)p.rb_size)
+                        return fail("RBPolyB pair without its polynomial data", error);
+                    fam.back().poly_matrix = b.polynomial_matrix.data();
+                    fam.back().poly_norm = b.polynomial_normalizations.data();
+                }
             }
         } else {
             rmin.push_back(p.min_dist);
@@ -83,9 +93,9 @@ class MTPB200Direct {
                                  0.0));
         }
         for (const auto &f : fam)
-            if (f.type > MTPB_RB_CHEBY_POLY4)
+            if (f.type > MTPB_RB_POLYB_COS || (!np && f.type >= MTPB_RB_POLYB))
                 return fail("radial basis family not implemented on the B200 path "
-                            "(RBPolyB, RBPolyBCos and the legacy families)",
+                            "(the legacy families)",
                             error);
         mtpb_model_view v{};
         v.species_count = p.species_count;

@@ -90,6 +90,14 @@ static bool copy_model(const mtpb_model_view *v, ModelHost &m, std::string *err)
             h.r2 = f.r2;
             h.lambda = f.lambda;
             h.scale_lambda = f.scale_lambda;
+            if (f.type == MTPB_RB_POLYB || f.type == MTPB_RB_POLYB_COS) {
+                if (!f.poly_matrix || !f.poly_norm) {
+                    *err = "RBPolyB / RBPolyBCos need poly_matrix and poly_norm";
+                    return false;
+                }
+                h.poly_matrix.assign(f.poly_matrix, f.poly_matrix + (size_t)m.R * m.R);
+                h.poly_norm.assign(f.poly_norm, f.poly_norm + m.R);
+            }
             m.family.push_back(h);
         }
     }
@@ -166,9 +174,48 @@ static int upload_model(mtpb_context *c)
         q.den = f.lambda != 0.0 ? std::expm1(f.lambda) : 0.0;
         q.sden = f.scale_lambda != 0.0 ? std::tanh(f.scale_lambda) : 0.0;
         q.type = f.type;
-        q.cutoff = f.cutoff;
+        q.cutoff = f.type == RB_POLYB_COS ? CUT_COSINE_LEFT : f.cutoff;
         q.shift = f.shift;
         q.flipped = f.flipped;
+    }
+    // RBPolyB / RBPolyBCos (runtime/mtp/radial_basis.h:223-290):
+    // Q_i = fc sum_j M(i, j) N_j s (max - r)^(j + first).  The device evaluates
+    // the powers and the matrix and normalisations are folded into the
+    // coefficients, c'[mu][j] = N_j sum_i c[mu][i] M(i, j), so that
+    // f_mu = sum_j c'[mu][j] s (max - r)^(j + first) fc; the same sums in
+    // another order (checked against the reference loader's matrix in the
+    // tests).  T_p(i, j) = N_j M(i, j) maps gradients back (training.cu).
+    std::vector<double> radial_dev = m.radial;
+    std::vector<double> poly_t;
+    for (int p = 0; p < KK; ++p) {
+        const RadialFamily f = m.pair_family(p);
+        if (f.type != RB_POLYB && f.type != RB_POLYB_COS)
+            continue;
+        const int R = m.R;
+        if (poly_t.empty())
+            poly_t.assign((size_t)KK * R * R, 0.0);
+        for (int i = 0; i < R; ++i)
+            for (int j = 0; j < R; ++j)
+                poly_t[((size_t)p * R + i) * R + j] = f.poly_norm[j] * f.poly_matrix[i + (size_t)j * R];
+        for (int mu = 0; mu < m.mu; ++mu) {
+            const double *cin = &m.radial[((size_t)p * m.mu + mu) * R];
+            double *cout = &radial_dev[((size_t)p * m.mu + mu) * R];
+            for (int j = 0; j < R; ++j) {
+                double acc = 0.0;
+                for (int i = 0; i < R; ++i)
+                    acc += cin[i] * f.poly_matrix[i + (size_t)j * R];
+                cout[j] = f.poly_norm[j] * acc;
+            }
+        }
+    }
+    c->d_poly = nullptr;
+    if (!poly_t.empty()) {
+        c->d_poly = c->arena.get<double>("model_poly", poly_t.size());
+        if (!c->d_poly)
+            return fail(MTPB_ERR_MEMORY, "device allocation for the model failed");
+        CUDA_TRY(cudaMemcpyAsync(c->d_poly, poly_t.data(), sizeof(double) * poly_t.size(),
+                                 cudaMemcpyHostToDevice, c->stream),
+                 "upload PolyB matrices");
     }
     c->d_radial = c->arena.get<double>("model_radial", m.radial.size());
     c->d_species = c->arena.get<double>("model_species", m.K);
@@ -186,7 +233,7 @@ static int upload_model(mtpb_context *c)
     }
     if (!c->d_radial || !c->d_species || !c->d_pairs || !c->d_recs || !c->d_phase_row0)
         return fail(MTPB_ERR_MEMORY, "device allocation for the model failed");
-    CUDA_TRY(cudaMemcpyAsync(c->d_radial, m.radial.data(), sizeof(double) * m.radial.size(),
+    CUDA_TRY(cudaMemcpyAsync(c->d_radial, radial_dev.data(), sizeof(double) * radial_dev.size(),
                              cudaMemcpyHostToDevice, c->stream),
              "upload radial");
     CUDA_TRY(cudaMemcpyAsync(c->d_species, m.species.data(), sizeof(double) * m.K,
@@ -260,6 +307,7 @@ int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offse
         int *gmax = c->arena.get<int>("group_maxdeg_active", c->npad / 32 + 1);
         if (!active || !nact || !gmax)
             return fail(MTPB_ERR_MEMORY, "device allocation for the active edges failed");
+        NvtxRange range("mtpb:active_edges");
         CUDA_TRY(launch_active_edges(a, active, nact, gmax, reverse ? dx : nullptr,
                                      reverse ? dy : nullptr, reverse ? dz : nullptr, c->stream),
                  "active edges");
@@ -269,7 +317,10 @@ int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offse
         a.group_maxdeg = gmax;
     }
     CUDA_TRY(cudaEventRecord(c->ev[1], c->stream), "event");
-    CUDA_TRY(launch_moments_fwd(c->shape, a, basic, c->stream), "moments forward");
+    {
+        NvtxRange range("mtpb:moments_fwd");
+        CUDA_TRY(launch_moments_fwd(c->shape, a, basic, c->stream), "moments forward");
+    }
     c->launches += moment_kernel_parts(c->shape, false);
     CUDA_TRY(cudaEventRecord(c->ev[2], c->stream), "event");
     double *gscratch = nullptr;
@@ -279,12 +330,17 @@ int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offse
         if (!gscratch)
             return fail(MTPB_ERR_MEMORY, "device allocation for graph rows failed");
     }
-    CUDA_TRY(launch_dag(c->plan, c->d_recs, c->d_phase_row0, c->nslot, ncenter, c->npad, types,
-                        c->d_species, basic, adjoint, site_energy, gscratch, c->d_err, c->stream),
-             "moment graph");
+    {
+        NvtxRange range("mtpb:moment_graph");
+        CUDA_TRY(launch_dag(c->plan, c->d_recs, c->d_phase_row0, c->nslot, ncenter, c->npad,
+                            types, c->d_species, basic, adjoint, site_energy, gscratch, c->d_err,
+                            c->stream),
+                 "moment graph");
+    }
     c->launches++;
     CUDA_TRY(cudaEventRecord(c->ev[3], c->stream), "event");
     if (reverse) {   // energy-only calls stop at the site energies and adjoints
+        NvtxRange range("mtpb:moments_rev");
         CUDA_TRY(launch_moments_rev(c->shape, a, adjoint, dx, dy, dz, c->stream),
                  "moments reverse");
         c->launches += moment_kernel_parts(c->shape, true);
@@ -515,6 +571,7 @@ int mtpb_set_center_count(mtpb_context *c, int center_count)
 
 int mtpb_build_neighbors(mtpb_context *c, const mtpb_structures *in, int memory)
 {
+    mtpb::NvtxRange range("mtpb:build_neighbors");
     if (!c)
         return fail(MTPB_ERR_ARGUMENT, "ctx is NULL");
     int rc = check_structures(c, in);
@@ -789,6 +846,7 @@ int mtpb::efs_compute(mtpb_context *c, int memory, const mtpb_efs_output *out,
                      site_energy, dx, dy, dz, forces_needed, E, c->skin > 0.0);
     if (rc)
         return rc;
+    NvtxRange range_gather("mtpb:force_gather_reduce");
     if (forces_needed) {
         CUDA_TRY(launch_force_gather(N, NT, c->nb.offsets, c->nb.in_offsets, c->nb.in_edges, dx,
                                      dy, dz, c->nb.rx, c->nb.ry, c->nb.rz, forces, avir, 0,
@@ -882,10 +940,14 @@ int mtpb_efs_structures(mtpb_context *c, const mtpb_structures *in, int memory,
         if (!unwrapped)
             return fail(MTPB_ERR_MEMORY, "device allocation failed");
         CUDA_TRY(cudaEventRecord(c->ev[0], c->stream), "event");
-        CUDA_TRY(refresh_edges(N, c->d_ns, c->nb.struct_of, c->nb, c->d_x_build, x, unwrapped,
-                               const_cast<double *>(c->nb.rx), const_cast<double *>(c->nb.ry),
-                               const_cast<double *>(c->nb.rz), c->stream),
-                 "refresh edge vectors");
+        {
+            NvtxRange range("mtpb:refresh_edges");
+            CUDA_TRY(refresh_edges(N, c->d_ns, c->nb.struct_of, c->nb, c->d_x_build, x,
+                                   unwrapped, const_cast<double *>(c->nb.rx),
+                                   const_cast<double *>(c->nb.ry),
+                                   const_cast<double *>(c->nb.rz), c->stream),
+                     "refresh edge vectors");
+        }
         c->edge_epoch++;
         c->nb_built_this_call = true;   // ev[0] marks the refresh
         c->pending_launches = c->nedges ? 2 : 0;
@@ -1031,6 +1093,7 @@ int mtpb_graph_program(const mtpb_model_view *view, int *nslot, int *slot_of_bas
 
 int mtpb_efs_csr(mtpb_context *c, const mtpb_csr_request *req, int memory)
 {
+    mtpb::NvtxRange range("mtpb:efs_csr");
     return csr_compute(c, req, memory);
 }
 

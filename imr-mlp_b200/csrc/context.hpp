@@ -61,6 +61,9 @@ struct mtpb_context {
     double skin = 0.0;
     // device model data
     double *d_radial = nullptr, *d_species = nullptr;
+    // RBPolyB pairs: T_p(i, j) = N_j M_p(i, j), [K*K][R][R], which maps the
+    // gradient of the folded coefficients back to the model's (NULL: none)
+    double *d_poly = nullptr;
     mtpb::PairParams *d_pairs = nullptr;
     mtpb::DagDevRec *d_recs = nullptr;
     int *d_phase_row0 = nullptr;

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <cstddef>
 #include <cstdint>
@@ -9,6 +10,18 @@
 #include <vector>
 
 namespace mtpb {
+
+// NVTX range over one stage of a call (the kernels it launches), named
+// "mtpb:<stage>" in profiler timelines; with no tool attached a push/pop is a
+// check of a function pointer (NVTX v3 is header-only).  The reference wraps
+// its kernels the same way (runtime/mtp/gpu-direct/mtp_gpu_direct.cu:46-65).
+struct NvtxRange {
+    explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange &) = delete;
+    NvtxRange &operator=(const NvtxRange &) = delete;
+};
+
 
 // Identifies one instantiated basis shape (see shapes.cuh).
 enum ShapeId : int {
@@ -36,7 +49,7 @@ int shape_slot(int id, int mu, int a, int b, int c);
 // mult = 2 / (rmax - rmin), rmax is also the pair cutoff.
 // Radial family of a pair (mtpb_radial_family of include/mtpb200.h).
 enum RadialType { RB_CHEBYSHEV = 0, RB_CHEBY_COS = 1, RB_CHEBY_POLY5 = 2, RB_CONFIGURABLE = 3,
-                  RB_CHEBY_POLY4 = 4 };
+                  RB_CHEBY_POLY4 = 4, RB_POLYB = 5, RB_POLYB_COS = 6 };
 enum RadialCutoffType { CUT_QUADRATIC = 0, CUT_COSINE = 1, CUT_POLY5 = 2,
                         CUT_NORMALIZED_QUADRATIC = 3, CUT_COSINE_LEFT = 4,
                         CUT_COSINE_UNSCALED = 5, CUT_COSINE_SQUARED = 6, CUT_SINE_SQUARED = 7,
@@ -46,6 +59,9 @@ enum RadialShiftType { SHIFT_LINEAR = 0, SHIFT_EXPONENTIAL = 1, SHIFT_EXPONENTIA
 struct RadialFamily {
     int type = RB_CHEBYSHEV, cutoff = CUT_QUADRATIC, shift = SHIFT_LINEAR, flipped = 0;
     double b = 0.0, r1 = 0.0, r2 = 0.0, lambda = 0.0, scale_lambda = 0.0;
+    // RBPolyB / RBPolyBCos: orthogonalisation matrix [R*R] (column-major) and
+    // power normalisations [R], as the reference's loader computes them
+    std::vector<double> poly_matrix, poly_norm;
 };
 
 // Device parameters of a pair's radial basis (filled by upload_model, api.cu):

@@ -393,5 +393,6 @@ int noalloc_compute(mtpb_context *c, const mtpb_csr_request *r)
 
 extern "C" int mtpb_efs_csr_noalloc(mtpb_context *c, const mtpb_csr_request *req)
 {
+    mtpb::NvtxRange range("mtpb:efs_csr_noalloc");
     return mtpb::noalloc_compute(c, req);
 }

@@ -40,10 +40,20 @@ bool validate_model(const ModelHost &m, std::string *err)
     for (int p = 0; p < (int)m.family.size(); ++p) {
         const RadialFamily &f = m.family[p];
         const double lo = m.min_dist[p], hi = m.max_dist[p];
-        if (f.type < RB_CHEBYSHEV || f.type > RB_CHEBY_POLY4)
+        if (f.type < RB_CHEBYSHEV || f.type > RB_POLYB_COS)
             return fail("unsupported radial basis type " + std::to_string(f.type) +
-                        " (RBChebyshev, RBChebyCos, RBChebyshevPoly4/5 and "
-                        "RBChebyshevConfigurable are implemented)");
+                        " (RBChebyshev, RBChebyCos, RBChebyshevPoly4/5, "
+                        "RBChebyshevConfigurable, RBPolyB and RBPolyBCos are implemented)");
+        if (f.type == RB_POLYB || f.type == RB_POLYB_COS) {
+            if (f.poly_matrix.size() != (size_t)m.R * m.R || f.poly_norm.size() != (size_t)m.R)
+                return fail("RBPolyB needs an R x R matrix and R normalisations");
+            for (double v : f.poly_matrix)
+                if (!std::isfinite(v))
+                    return fail("non-finite RBPolyB orthogonalisation matrix");
+            for (double v : f.poly_norm)
+                if (!std::isfinite(v) || !(v > 0))
+                    return fail("invalid RBPolyB normalisation");
+        }
         if (!std::isfinite(f.b) || !std::isfinite(f.r1) || !std::isfinite(f.r2) ||
             !std::isfinite(f.lambda) || !std::isfinite(f.scale_lambda))
             return fail("non-finite radial parameter");

@@ -258,6 +258,27 @@ __device__ __forceinline__ bool radial_basis(const PairParams &pp, double s, int
                                              Emit &&emit)
 {
     double x, dx, q0, d0, q1, d1;
+    if (pp.type == RB_POLYB || pp.type == RB_POLYB_COS) {
+        // powers s (max - r)^(xi + first) and their r-derivatives, times the
+        // CosineLeft envelope for RBPolyBCos (runtime/mtp/radial_basis.h:
+        // 223-290); the orthogonalisation matrix and normalisations are folded
+        // into the coefficients at upload
+        const int first = pp.type == RB_POLYB ? 3 : 2;
+        double fc = 1.0, dfc = 0.0;
+        if (pp.type == RB_POLYB_COS)
+            radial_cutoff(pp, r, fc, dfc);
+        const double delta = pp.rmax - r;
+        double prev = s * delta;   // s delta^(first - 1)
+        if (first == 3)
+            prev *= delta;
+        for (int xi = 0; xi < R; ++xi) {
+            const double q = prev * delta;
+            const double dq = -(double)(xi + first) * prev;
+            emit(xi, q * fc, dq * fc + q * dfc);
+            prev = q;
+        }
+        return true;
+    }
     if (pp.type == RB_CHEBYSHEV) {
         x = (2.0 * r - pp.pu) / pp.su;
         dx = pp.mult;

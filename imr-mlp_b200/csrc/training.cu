@@ -290,10 +290,14 @@ __global__ void k_colsum(const double *__restrict__ in, long nrows, int ncols,
         out[j] = s;
 }
 
-// grad = [radial K*K x mu x R | species K | moment S] / norm; loss and metrics
+// grad = [radial K*K x mu x R | species K | moment S] / norm; loss and metrics.
+// RBPolyB pairs were evaluated with folded coefficients c' = c T_p (api.cu
+// upload_model), so their radial gradient is T_p applied to the gradient of
+// c': g[mu][i] = sum_j g'[mu][j] T_p(i, j), poly[(p R + i) R + j] = T_p(i, j)
 __global__ void k_assemble(int KK, int mu_total, int nmu, int R, int K, int S,
                            const double *__restrict__ rsum, const double *__restrict__ tsum,
                            const double *__restrict__ gsum, const int *__restrict__ moment_energy,
+                           const PairParams *__restrict__ pairs, const double *__restrict__ poly,
                            double inv_norm, double *__restrict__ grad, double *__restrict__ lm)
 {
     const int rsize = KK * mu_total * R;
@@ -303,7 +307,17 @@ __global__ void k_assemble(int KK, int mu_total, int nmu, int R, int K, int S,
         if (i < rsize) {
             const int p = i / (mu_total * R), rem = i - p * mu_total * R;
             const int m = rem / R, xi = rem - m * R;
-            g = m < nmu ? rsum[(p * nmu + m) * R + xi] : 0.0;
+            if (m >= nmu) {
+                g = 0.0;
+            } else if (poly && (pairs[p].type == RB_POLYB || pairs[p].type == RB_POLYB_COS)) {
+                const double *t = poly + ((size_t)p * R + xi) * R;
+                const double *gp = rsum + (size_t)(p * nmu + m) * R;
+                g = 0.0;
+                for (int j = 0; j < R; ++j)
+                    g += gp[j] * t[j];
+            } else {
+                g = rsum[(p * nmu + m) * R + xi];
+            }
         } else if (i < rsize + K) {
             g = tsum[TERMS + (i - rsize)];
         } else {
@@ -533,6 +547,7 @@ int loss_grad_compute(mtpb_context *c, const mtpb_labels *labels, const mtpb_los
                   w->weight_force_power, w->weight_stress_power,
                   te != nullptr && w->weight_eng > 0, tf != nullptr && w->weight_force > 0,
                   ts != nullptr && w->weight_stress > 0, K};
+    NvtxRange range_loss("mtpb:train_loss_weights");
     if (S > 0) {
         k_loss_struct<<<S, LOSS_THREADS, 0, c->stream>>>(aoff, c->d_types, d_energy, d_forces,
                                                          d_stress, te, tf, ts, lp, dlde_atom,
@@ -559,9 +574,12 @@ int loss_grad_compute(mtpb_context *c, const mtpb_labels *labels, const mtpb_los
         CUDA_TRY(cudaMemsetAsync(tangent, 0, sizeof(double) * (size_t)c->nslot * c->npad,
                                  c->stream),
                  "zero tangent");
-    else
+    else {
+        NvtxRange range("mtpb:train_tangent_moments");
         CUDA_TRY(launch_moments_tangent(c->shape, a, wx, wy, wz, tangent, c->stream), "tangent");
+    }
     CUDA_TRY(cudaEventRecord(tev[3], c->stream), "event");
+    NvtxRange range_dual("mtpb:train_dual_graph_edge_grad");
     CUDA_TRY(launch_dag_grad(c->plan, c->train.recs, c->d_phase_row0, grid, c->nslot, N, c->npad,
                              basic, tangent, dlde_atom, adjoint2, epart, gscratch, c->d_err,
                              c->stream),
@@ -589,8 +607,8 @@ int loss_grad_compute(mtpb_context *c, const mtpb_labels *labels, const mtpb_los
     const double inv_norm = cnt > 0 ? 1.0 / cnt : 1.0;
     double *d_grad = d_out + 8;
     k_assemble<<<(ncoef + 255) / 256, 256, 0, c->stream>>>(
-        KK, m.mu, nmu, m.R, K, m.S(), rsum, tsum, gsum, c->train.moment_energy, inv_norm, d_grad,
-        d_out);
+        KK, m.mu, nmu, m.R, K, m.S(), rsum, tsum, gsum, c->train.moment_energy, c->d_pairs,
+        c->d_poly, inv_norm, d_grad, d_out);
     CUDA_TRY(cudaGetLastError(), "assemble");
     CUDA_TRY(cudaMemsetAsync(nonfinite, 0x7f, sizeof(int), c->stream), "clear finite check");
     k_finite_check<<<(ncoef + 8 + 255) / 256, 256, 0, c->stream>>>(ncoef + 8, d_out, nonfinite);

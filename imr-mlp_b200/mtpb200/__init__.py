@@ -89,7 +89,7 @@ class _ModelKeep:
         self.radial = _f64(m.radial_coeffs)
         self.species = _f64(m.species_coeffs)
         self.moment = _f64(m.moment_coeffs)
-        self.families = _lib.radial_family_array(m)
+        self.families, self.family_arrays = _lib.radial_family_array(m)
         self.view = _lib.ModelView(
             m.species_count, m.radial_func_count, m.rb_size, int(m.radial_basis_split),
             _dp(self.mins), _dp(self.maxs), float(m.scaling), m.alpha_moments_count,

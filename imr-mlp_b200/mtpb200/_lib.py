@@ -9,6 +9,8 @@ from __future__ import annotations
 import ctypes as C
 import os
 
+import numpy as np
+
 PKG_ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LIB_PATH = os.environ.get("MTPB200_LIB", os.path.join(PKG_ROOT, "libmtpb200.so"))
 
@@ -29,7 +31,7 @@ class RadialFamilyView(C.Structure):
     _fields_ = [("type", C.c_int), ("cutoff_type", C.c_int), ("shift_type", C.c_int),
                 ("one_minus_chebyshev", C.c_int), ("b", C.c_double), ("r1", C.c_double),
                 ("r2", C.c_double), ("shift_lambda", C.c_double),
-                ("shift_scale_lambda", C.c_double)]
+                ("shift_scale_lambda", C.c_double), ("poly_matrix", _dp), ("poly_norm", _dp)]
 
 
 class ModelView(C.Structure):
@@ -46,18 +48,25 @@ class ModelView(C.Structure):
 
 
 def radial_family_array(model):
-    """ctypes array of the model's radial families (None for RBChebyshev)."""
+    """ctypes array of the model's radial families (None for RBChebyshev) and
+    the numpy arrays its RBPolyB pointers refer to (keep both alive)."""
     from .mtpfile import CUTOFF_TYPES, SHIFT_TYPES
     fams = model.radial_family
     if not fams:
-        return None
+        return None, []
     arr = (RadialFamilyView * len(fams))()
+    keep = []
     for i, f in enumerate(fams):
+        pm = pn = None
+        if f.poly_matrix is not None:
+            keep += [np.ascontiguousarray(f.poly_matrix, dtype=np.float64),
+                     np.ascontiguousarray(f.poly_norm, dtype=np.float64)]
+            pm, pn = keep[-2].ctypes.data_as(_dp), keep[-1].ctypes.data_as(_dp)
         arr[i] = RadialFamilyView(f.type_id, CUTOFF_TYPES[f.cutoff_type],
                                   SHIFT_TYPES[f.shift_type], int(f.one_minus_chebyshev),
                                   float(f.b), float(f.r1), float(f.r2), float(f.shift_lambda),
-                                  float(f.shift_scale_lambda))
-    return arr
+                                  float(f.shift_scale_lambda), pm, pn)
+    return arr, keep
 
 
 class Structures(C.Structure):

@@ -38,7 +38,32 @@ __all__ = ["MTPModel", "RadialFamily", "parse_mtp", "read_mtp", "write_mtp", "fo
 # (include/mtpb200.h; RadialBasis, RadialCutoff, RadialTransform of
 # runtime/mtp/gpu-direct/mtp_gpu_direct.h:152-186)
 RADIAL_TYPES = {"RBChebyshev": 0, "RBChebyCos": 1, "RBChebyshevPoly5": 2,
-                "RBChebyshevConfigurable": 3, "RBChebyshevPoly4": 4}
+                "RBChebyshevConfigurable": 3, "RBChebyshevPoly4": 4, "RBPolyB": 5,
+                "RBPolyBCos": 6}
+POLYB_TYPES = ("RBPolyB", "RBPolyBCos")
+
+
+def polyb_data(rmin: float, rmax: float, size: int):
+    """Orthogonalisation matrix (column-major, flattened [size*size]) and power
+    normalisations [size] of the RBPolyB families, by their definition
+    (runtime/mtp/radial_basis_setup.cpp, basis/basis.cpp): the power p = i + 1
+    has normalisation sqrt((2p + 5) / (max - min)^(2p + 5)); the overlap matrix
+    S_ij = sqrt((2p_i + 5)(2p_j + 5)) / (p_i + p_j + 5) gives M = S^(-1/2)
+    through its eigendecomposition.  S is ill-conditioned (1.3e13 at R = 8), so
+    M depends on the eigensolver's rounding: numpy's differs from the
+    reference's (Eigen's) at ~1e-4 of its largest entry, which moves energies
+    by ~1e-8 eV/atom.  For parity with the reference, a model must carry the
+    reference loader's own matrix (the C++ binding passes it; the tests take it
+    from the compiled reference); this one is an approximation for models
+    that never met the reference."""
+    p = np.arange(1, size + 1, dtype=np.float64)
+    norm = np.sqrt((2 * p + 5) / np.power(rmax - rmin, 2 * p + 5))
+    S = np.sqrt(np.outer(2 * p + 5, 2 * p + 5)) / (p[:, None] + p[None, :] + 5)
+    w, V = np.linalg.eigh(S)
+    if not np.all(w > 0):
+        raise ValueError("RBPolyB overlap matrix is not positive definite")
+    M = (V * (1.0 / np.sqrt(w))) @ V.T
+    return np.ascontiguousarray(M.reshape(-1, order="F")), norm
 CUTOFF_TYPES = {"quadratic": 0, "cosine": 1, "poly5": 2, "normalized_quadratic": 3,
                 "cosine_left": 4, "cosine_unscaled": 5, "cosine_squared": 6,
                 "sine_squared": 7, "poly3": 8, "poly4": 9, "smoothstep5": 10,
@@ -59,6 +84,12 @@ class RadialFamily:
     r2: float = 0.0                        # cutoff_r2
     shift_lambda: float = 0.0
     shift_scale_lambda: float = 0.0
+    # RBPolyB / RBPolyBCos: orthogonalisation matrix (column-major [R*R]) and
+    # normalisations [R] (polyb_data, or the reference loader's own)
+    poly_matrix: Optional[np.ndarray] = dataclasses.field(default=None, compare=False,
+                                                          repr=False)
+    poly_norm: Optional[np.ndarray] = dataclasses.field(default=None, compare=False,
+                                                        repr=False)
 
     @property
     def type_id(self) -> int:
@@ -250,6 +281,8 @@ def parse_mtp(text: str) -> MTPModel:
         if size <= 0 or not rmax > rmin:
             raise ValueError("invalid radial basis interval or size")
         fam = RadialFamily(name=btype)
+        if btype in POLYB_TYPES:
+            fam.poly_matrix, fam.poly_norm = polyb_data(rmin, rmax, size)
         if btype in ("RBChebyshevPoly4", "RBChebyshevPoly5"):
             fam.b = float(tk.assignment("rb_b"))
         elif btype == "RBChebyshevConfigurable":

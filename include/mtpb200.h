@@ -34,7 +34,7 @@ extern "C" {
 #pragma GCC visibility push(default)
 #endif
 
-#define MTPB_ABI_VERSION 2
+#define MTPB_ABI_VERSION 3
 
 enum mtpb_status {
     MTPB_OK = 0,
@@ -61,13 +61,23 @@ typedef struct mtpb_context mtpb_context;
  *   RBChebyshevConfigurable  x from shift_type, fc from cutoff_type, optionally
  *                      the 1 - T_(i+1) polynomials (basis.cpp:937-1013,
  *                      cutoff.cpp, xtrans.cpp)
+ *   RBPolyB / RBPolyBCos  Q_i = fc sum_j M(i,j) N_j s (max - r)^(j + first),
+ *                      first 3 with fc = 1 / first 2 with fc = (1 + cos(pi r / max))/2
+ *                      (runtime/mtp/radial_basis.h:223-290); M and N are the
+ *                      orthogonalisation matrix and normalisations of the
+ *                      reference's loader (radial_basis_t::polynomial_matrix,
+ *                      polynomial_normalizations), passed in poly_matrix / poly_norm:
+ *                      M is ill-conditioned (1e13 at R = 8), so it is taken as data
+ *                      rather than recomputed.
  * Poly4, Poly5 and the configurable family are zero below min_dist. */
 enum mtpb_radial_type {
     MTPB_RB_CHEBYSHEV = 0,
     MTPB_RB_CHEBY_COS = 1,
     MTPB_RB_CHEBY_POLY5 = 2,
     MTPB_RB_CHEBY_CONFIGURABLE = 3,
-    MTPB_RB_CHEBY_POLY4 = 4
+    MTPB_RB_CHEBY_POLY4 = 4,
+    MTPB_RB_POLYB = 5,
+    MTPB_RB_POLYB_COS = 6
 };
 enum mtpb_radial_cutoff {   /* cutoff_type of RBChebyshevConfigurable */
     MTPB_CUT_QUADRATIC = 0, MTPB_CUT_COSINE = 1, MTPB_CUT_POLY5 = 2,
@@ -88,6 +98,8 @@ typedef struct mtpb_radial_family {
     double r1, r2;             /* cutoff_r1, cutoff_r2 (smoothstep7) */
     double lambda;             /* shift_lambda */
     double scale_lambda;       /* shift_scale_lambda */
+    const double *poly_matrix; /* RBPolyB / RBPolyBCos: M [R*R], column-major; else NULL */
+    const double *poly_norm;   /* RBPolyB / RBPolyBCos: N [R]; else NULL */
 } mtpb_radial_family;
 
 /* Linear MTP.  Field meaning follows MTPGpuPotentialView

@@ -584,6 +584,54 @@ static void rb_calc_der(const oracle_model *m, int pair, int R, double r, double
         return;
     }
     const double mult = 2.0 / (hi - lo), su = hi - lo, pu = hi + lo;
+    if (f->type == 5 || f->type == 6) {
+        /* RBPolyB / RBPolyBCos: MLIPCore::Radial::evaluate_polynomial
+         * (runtime/mtp/radial_basis.h:223-290) in its order: column 0 seeds
+         * the sums, the other columns add in j order; the CosineLeft envelope
+         * of RBPolyBCos is applied last.  excludes() zeroes r >= max_dist. */
+        if (r >= hi) {
+            for (int i = 0; i < R; ++i)
+                val[i] = der[i] = 0.0;
+            return;
+        }
+        const double *M = f->poly_matrix, *N = f->poly_norm;
+        const double delta = hi - r;
+        const int first = f->type == 5 ? 3 : 2;
+        double fc = 1.0, dfc = 0.0;
+        if (first == 2) {
+            const double freq = ORACLE_PI / hi;
+            fc = 0.5 * (1.0 + cos(r * freq));
+            dfc = -0.5 * sin(r * freq) * freq;
+        }
+        double previous = s * delta;
+        if (first == 3)
+            previous *= delta;
+        const double first_power = previous * delta;
+        const double first_value = N[0] * first_power;
+        const double first_derivative = -(N[0] * first) * previous;
+        for (int i = 0; i < R; ++i) {
+            val[i] = 0.0 + M[i] * first_value;
+            der[i] = 0.0 + M[i] * first_derivative;
+        }
+        previous = first_power;
+        for (int j = 1; j < R; ++j) {
+            const double power = previous * delta;
+            const double value = N[j] * power;
+            const double derivative = -(N[j] * (j + first)) * previous;
+            const double *column = M + (size_t)j * R;
+            for (int i = 0; i < R; ++i) {
+                val[i] += column[i] * value;
+                der[i] += column[i] * derivative;
+            }
+            previous = power;
+        }
+        if (first == 2)
+            for (int i = 0; i < R; ++i) {
+                der[i] = der[i] * fc + val[i] * dfc;
+                val[i] *= fc;
+            }
+        return;
+    }
     if (f->type == 3) { /* RBasis_ChebyshevConfigurable::calculate, order 1 */
         if (r < lo || r > hi) {
             for (int i = 0; i < R; ++i)

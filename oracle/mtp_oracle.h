@@ -41,6 +41,8 @@ extern "C" {
 typedef struct oracle_radial_family {
     int type, cutoff_type, shift_type, one_minus_chebyshev;
     double b, r1, r2, lambda, scale_lambda;
+    const double *poly_matrix;   /* RBPolyB / RBPolyBCos: [R*R] column-major */
+    const double *poly_norm;     /* RBPolyB / RBPolyBCos: [R] */
 } oracle_radial_family;
 
 /* Flat model description.  Same field order as mtpb_model_view in

@@ -36,11 +36,12 @@ class OracleRadialFamily(C.Structure):
     _fields_ = [("type", C.c_int), ("cutoff_type", C.c_int), ("shift_type", C.c_int),
                 ("one_minus_chebyshev", C.c_int), ("b", C.c_double), ("r1", C.c_double),
                 ("r2", C.c_double), ("shift_lambda", C.c_double),
-                ("shift_scale_lambda", C.c_double)]
+                ("shift_scale_lambda", C.c_double), ("poly_matrix", _dp), ("poly_norm", _dp)]
 
 
 _RB_TYPES = {"RBChebyshev": 0, "RBChebyCos": 1, "RBChebyshevPoly5": 2,
-             "RBChebyshevConfigurable": 3, "RBChebyshevPoly4": 4}
+             "RBChebyshevConfigurable": 3, "RBChebyshevPoly4": 4, "RBPolyB": 5,
+             "RBPolyBCos": 6}
 _CUTOFFS = {"quadratic": 0, "cosine": 1, "poly5": 2, "normalized_quadratic": 3,
             "cosine_left": 4, "cosine_unscaled": 5, "cosine_squared": 6, "sine_squared": 7,
             "poly3": 8, "poly4": 9, "smoothstep5": 10, "smoothstep7": 11}
@@ -83,11 +84,19 @@ def model_struct(model):
     fam_ptr = None
     if fams:
         arr = (OracleRadialFamily * len(fams))()
+        poly = []
         for i, f in enumerate(fams):
+            pm = pn = None
+            if getattr(f, "poly_matrix", None) is not None:
+                poly += [np.ascontiguousarray(f.poly_matrix, dtype=np.float64),
+                         np.ascontiguousarray(f.poly_norm, dtype=np.float64)]
+                pm, pn = _d(poly[-2]), _d(poly[-1])
             arr[i] = OracleRadialFamily(_RB_TYPES[f.name], _CUTOFFS[f.cutoff_type],
                                         _SHIFTS[f.shift_type], int(f.one_minus_chebyshev),
-                                        f.b, f.r1, f.r2, f.shift_lambda, f.shift_scale_lambda)
+                                        f.b, f.r1, f.r2, f.shift_lambda, f.shift_scale_lambda,
+                                        pm, pn)
         keep["families"] = arr
+        keep["poly"] = poly
         fam_ptr = C.cast(arr, C.POINTER(OracleRadialFamily))
     s = OracleModel(model.species_count, model.radial_func_count, model.rb_size,
                     int(model.radial_basis_split), _d(keep["mins"]), _d(keep["maxs"]),
@@ -271,6 +280,7 @@ class Reference:
                                        _dp, _dp, _dp, _dp]
         L.ref_mlip_compute_omp.argtypes = [C.c_void_p, C.c_int, C.c_int, _ip, C.c_int, _ip, _dp,
                                            _ip, _ip, _ip, _dp, _dp]
+        L.ref_mlip_polyb.argtypes = [C.c_void_p, C.c_int, _dp, _dp]
         L.ref_mlip_efs_omp.argtypes = [C.c_void_p, C.c_int, C.c_int, _ip, C.c_int, _ip, _dp,
                                        _ip, _ip, _ip, _dp, _dp, _dp, _dp]
 
@@ -294,6 +304,31 @@ class Reference:
         rij = np.zeros((E, 3))
         self.lib.ref_neighbors(_d(cell), _i(pbc), n, _d(pos), cutoff, _i(off), _i(nbr), _d(rij))
         return NeighborList(off, nbr, rij)
+
+    def polyb(self, mtp_text: str, species: int):
+        """Per ordered species pair, the RBPolyB orthogonalisation matrix
+        (column-major, flattened) and normalisations that MLIPCore's loader
+        computed for this model text (runtime/mtp/radial_basis_setup.cpp), or
+        None for pairs of other families."""
+        tmap = np.arange(species, dtype=np.int32)
+        cut = np.zeros(1)
+        h = self.lib.ref_mlip_setup(mtp_text.encode(), _i(tmap), species, _d(cut))
+        if not h:
+            raise RuntimeError(self._err())
+        try:
+            out = []
+            for p in range(species * species):
+                n = self.lib.ref_mlip_polyb(h, p, None, None)
+                if n <= 0:
+                    out.append(None)
+                    continue
+                M = np.zeros(n * n)
+                N = np.zeros(n)
+                self.lib.ref_mlip_polyb(h, p, _d(M), _d(N))
+                out.append((M, N))
+            return out
+        finally:
+            self.lib.ref_mlip_destroy(h)
 
     def mlip_efs(self, mtp_text: str, types, nl: NeighborList, positions):
         """MLIPCore::compute on explicit ghost atoms: every edge gets a ghost

@@ -13,6 +13,7 @@
 #include "base/structures.h"
 #include "runtime/mtp/mlip.h"
 
+#include <algorithm>
 #include <cstring>
 #include <omp.h>
 #include <exception>
@@ -97,6 +98,27 @@ void *ref_mlip_setup(const char *text, const int *type_map, int type_count, doub
         g_error = ex.what();
         return nullptr;
     }
+}
+
+// PolyB / PolyBCos data of one ordered species pair as MLIPCore's loader
+// computed it (runtime/mtp/radial_basis_setup.cpp): the column-major
+// orthogonalisation matrix [size*size] and the power normalisations [size].
+// Returns the basis size, 0 when the pair's basis is not a PolyB family, -1 on
+// a bad pair index.  Either output may be null.
+int ref_mlip_polyb(void *handle, int pair, double *matrix, double *normalizations)
+{
+    auto *p = static_cast<MLIPCore::mlip *>(handle);
+    if (pair < 0 || pair >= p->pair_radial_basis_count)
+        return -1;
+    const auto &b = p->pair_radial_bases[pair];
+    if (b.rb != MLIPCore::mlip::RB_POLYB && b.rb != MLIPCore::mlip::RB_POLYBCOS)
+        return 0;
+    if (matrix)
+        std::copy(b.polynomial_matrix.begin(), b.polynomial_matrix.end(), matrix);
+    if (normalizations)
+        std::copy(b.polynomial_normalizations.begin(), b.polynomial_normalizations.end(),
+                  normalizations);
+    return b.size;
 }
 
 void ref_mlip_destroy(void *handle)

@@ -85,3 +85,30 @@ def with_radial_family(model, case):
     if lo is not None:
         mins[:] = lo
     return dataclasses.replace(model, radial_family=[fam] * n, min_dist=mins)
+
+
+def with_polyb(model, name, reference=None, split=False):
+    """The model with every pair's radial basis replaced by RBPolyB or
+    RBPolyBCos (`name`); with `reference` the orthogonalisation matrices are the
+    ones the compiled reference loader computes for the same text (the
+    parity pin), else numpy's (mtpfile.polyb_data).  `split` writes one basis
+    per ordered pair."""
+    import dataclasses
+    from mtpb200 import format_mtp
+    from mtpb200.mtpfile import RadialFamily, polyb_data
+    K = model.species_count
+    n = K * K if split else 1
+    mins = np.full(n, float(model.min_dist[0]))
+    maxs = np.full(n, float(model.max_dist[0]))
+    fams = []
+    for p in range(n):
+        pm, pn = polyb_data(mins[p], maxs[p], model.rb_size)
+        fams.append(RadialFamily(name=name, poly_matrix=pm, poly_norm=pn))
+    m = dataclasses.replace(model, radial_family=fams, radial_basis_split=split,
+                            min_dist=mins, max_dist=maxs)
+    if reference is not None:
+        data = reference.polyb(format_mtp(m), K)
+        for p in range(n):
+            assert data[p] is not None, "the reference loader has no RBPolyB data"
+            fams[p].poly_matrix, fams[p].poly_norm = data[p]
+    return m

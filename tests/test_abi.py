@@ -35,7 +35,7 @@ def test_python_signatures_cover_header():
 def test_abi_version_and_error_without_device():
     import mtpb200
     lib = mtpb200.library()
-    assert lib.mtpb_abi_version() == 2
+    assert lib.mtpb_abi_version() == 3
     if mtpb200.device_count() > 0:
         pytest.skip("a device is present")
     m = load_model("pair_k1.mtp")
@@ -89,7 +89,8 @@ def test_mtp_parser_reads_reference_templates():
 
 
 @pytest.mark.parametrize("field,value,message", [
-    ("type", 5, b"unsupported radial basis type 5"),          # RBPolyB
+    ("type", 7, b"unsupported radial basis type 7"),          # a legacy family
+    ("type", 5, b"RBPolyB / RBPolyBCos need poly_matrix"),    # RBPolyB without its matrix
     ("cutoff_type", 12, b"unknown configurable cutoff_type"),
     ("r2", 6.0, b"smoothstep7 cutoff requires"),
     ("shift_lambda", float("nan"), b"non-finite radial parameter"),

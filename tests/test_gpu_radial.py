@@ -1,5 +1,6 @@
-"""Radial basis families on the GPU (RBChebyCos, RBChebyshevPoly4/5 and every
-cutoff / shift of RBChebyshevConfigurable) against the C restatement, which
+"""Radial basis families on the GPU (RBChebyCos, RBChebyshevPoly4/5, every
+cutoff / shift of RBChebyshevConfigurable, RBPolyB and RBPolyBCos) against the
+C restatement, which
 is pinned to the compiled reference MLIPCore in test_oracle.py: EFS of a
 level-16 model on the config-1 box and of a split level-20 model on strained
 alloys, and the loss gradient (the radial-coefficient gradient uses the
@@ -71,3 +72,19 @@ def test_radial_family_gradient(oracle, model_l16, case):
     te, tf, ts = _labels(sts, 9)
     _close(_gpu_grad(m, sts, te, tf, ts), _oracle_grad(oracle, m, sts, te, tf, ts))
 
+
+
+@pytest.mark.parametrize("name,split", [("RBPolyB", False), ("RBPolyBCos", False),
+                                        ("RBPolyB", True)])
+def test_polyb_efs_and_gradient(oracle, reference, model_l16, name, split):
+    """RBPolyB / RBPolyBCos with the reference loader's orthogonalisation
+    matrix: the device evaluates powers of (max - r) with the matrix and
+    normalisations folded into the coefficients, and maps the radial gradient
+    back through them."""
+    from helpers import with_polyb
+    from test_gpu_train import _close, _gpu_grad, _labels, _mixed, _oracle_grad
+    m = with_polyb(model_l16, name, reference, split=split)
+    _check_efs(oracle, m, [configs.config1()])
+    sts = _mixed(2, 84, m.species_count)
+    te, tf, ts = _labels(sts, 10)
+    _close(_gpu_grad(m, sts, te, tf, ts), _oracle_grad(oracle, m, sts, te, tf, ts))

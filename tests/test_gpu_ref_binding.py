@@ -97,3 +97,26 @@ def test_binding_compute_lammps_matches_batch(oracle, reference, binding_availab
     assert np.max(np.abs(f - f_ref)) < 1e-9
     assert np.max(np.abs(sv - vir_ref)) < 1e-9
 
+
+
+@pytest.mark.parametrize("name", ["RBPolyB", "RBPolyBCos"])
+def test_binding_polyb_matches_mlipcore(oracle, reference, binding_available, model_l16, name):
+    """A PolyB model loaded by MLIPCore goes through the binding with the
+    loader's own orthogonalisation matrix."""
+    from helpers import with_polyb
+    from oracle import ReferenceBinding
+    from mtpb200 import format_mtp
+    model = with_polyb(model_l16, name)      # the text only; the loader makes the matrix
+    st = configs.config1()
+    nl, x, types, nbr = _ghost_problem(oracle, model, st)
+    n = len(st["types"])
+    text = format_mtp(model)
+    e_ref, se_ref, f_ref, vir_ref = reference.mlip_efs(text, st["types"], nl, x[:n])
+    with ReferenceBinding(text, model.species_count, 0) as b:
+        out = b.compute_batch(n, nl.offsets, nbr, types, x)
+    f = out["force"][:n].copy()
+    np.add.at(f, nl.nbr, out["force"][n:])
+    assert abs(out["energy"] - e_ref) / n < 1e-10
+    assert np.max(np.abs(out["site_energy"] - se_ref)) < 1e-10
+    assert np.max(np.abs(f - f_ref)) < 1e-9
+    assert np.max(np.abs(out["site_virial"] - vir_ref)) < 1e-9
