@@ -135,14 +135,3 @@ def test_gradient_weight_powers_level16(oracle, refgpu_available, model_l16, wei
         s["types"] = np.minimum(s["types"], 1).astype(np.int32)
     _compare(oracle, model_l16, sts, weights, 24)
 
-
-@pytest.mark.parametrize("name", ["RBPolyB", "RBPolyBCos"])
-def test_gradient_polyb(oracle, reference, refgpu_available, model_l16, name):
-    """RBPolyB / RBPolyBCos: the reference GPU core reads the .mtp text and
-    builds its matrix in its own loader; this library gets the same matrix."""
-    from helpers import with_polyb
-    m = with_polyb(model_l16, name, reference)
-    sts = configs.config2(4, seed=67)
-    for s in sts:
-        s["types"] = np.minimum(s["types"], 1).astype(np.int32)
-    _compare(oracle, m, sts, CONFIG4_WEIGHTS, 25)
