@@ -22,9 +22,11 @@ from typing import Dict, List, Optional, Sequence
 import numpy as np
 
 from . import _lib
+from .gpm import read_gpm, write_gpm
 from .mtpfile import MTPModel, format_mtp, parse_mtp, read_mtp, write_mtp
 
 __all__ = ["MTPGpuDirect", "PotMTP", "MTPBError", "MTPModel", "read_mtp", "parse_mtp",
+           "read_gpm", "write_gpm",
            "write_mtp", "format_mtp", "device_count", "library"]
 
 _LIB: Optional[C.CDLL] = None

@@ -281,6 +281,8 @@ class Reference:
         L.ref_mlip_compute_omp.argtypes = [C.c_void_p, C.c_int, C.c_int, _ip, C.c_int, _ip, _dp,
                                            _ip, _ip, _ip, _dp, _dp]
         L.ref_mlip_polyb.argtypes = [C.c_void_p, C.c_int, _dp, _dp]
+        L.ref_read_model_text.restype = C.c_long
+        L.ref_read_model_text.argtypes = [C.c_char_p, C.c_char_p, C.c_long]
         L.ref_mlip_efs_omp.argtypes = [C.c_void_p, C.c_int, C.c_int, _ip, C.c_int, _ip, _dp,
                                        _ip, _ip, _ip, _dp, _dp, _dp, _dp]
 
@@ -304,6 +306,16 @@ class Reference:
         rij = np.zeros((E, 3))
         self.lib.ref_neighbors(_d(cell), _i(pbc), n, _d(pos), cutoff, _i(off), _i(nbr), _d(rij))
         return NeighborList(off, nbr, rij)
+
+    def model_text(self, path: str) -> str:
+        """The .mtp text MLIPCore's loader reads from a model file (GPM bundles
+        included)."""
+        n = self.lib.ref_read_model_text(path.encode(), None, 0)
+        if n < 0:
+            raise RuntimeError(self._err())
+        buf = C.create_string_buffer(n + 1)
+        self.lib.ref_read_model_text(path.encode(), buf, n + 1)
+        return buf.value.decode()
 
     def polyb(self, mtp_text: str, species: int):
         """Per ordered species pair, the RBPolyB orthogonalisation matrix

@@ -121,6 +121,29 @@ int ref_mlip_polyb(void *handle, int pair, double *matrix, double *normalization
     return b.size;
 }
 
+// The .mtp text MLIPCore's loader derives from a model file (a GPM bundle or
+// an .mtp file; runtime/mtp/mlip.cpp:350-423).  Returns the text length and
+// copies at most cap bytes (with a terminating zero) into buf; -1 on error.
+long ref_read_model_text(const char *path, char *buf, long cap)
+{
+    try
+    {
+        const std::string text = MLIPCore::read_model_text(path);
+        if (buf && cap > 0)
+        {
+            const long n = std::min<long>(cap - 1, (long)text.size());
+            std::memcpy(buf, text.data(), (size_t)n);
+            buf[n] = 0;
+        }
+        return (long)text.size();
+    }
+    catch (const std::exception &ex)
+    {
+        g_error = ex.what();
+        return -1;
+    }
+}
+
 void ref_mlip_destroy(void *handle)
 {
     if (handle)
