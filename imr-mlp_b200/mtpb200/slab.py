@@ -152,30 +152,31 @@ class SlabDomain:
         self.pos = self._wrap_x(self.pos)
         fx = self._frac_x(self.pos)
         slab = torch.clamp((fx * self.nranks).long(), max=self.nranks - 1)
-        leave_lo = slab == self.lower
-        leave_hi = slab == self.upper
-        stay = slab == self.rank
-        if not bool(torch.all(stay | leave_lo | leave_hi)):
+        # destination code: 0 stays, 1 goes to the lower neighbour, 2 to the
+        # upper one (one neighbour at two ranks), 3 is further away; one
+        # host read of the counts, the index lists by a stable sort
+        code = torch.full_like(slab, 3)
+        code = torch.where(slab == self.upper, 2 if self.lower != self.upper else 1, code)
+        code = torch.where(slab == self.lower, 1, code)
+        code = torch.where(slab == self.rank, 0, code)
+        n_stay, n_lo, n_hi, n_far = torch.bincount(code, minlength=4).tolist()
+        if n_far:
             raise RuntimeError("an atom moved further than one slab between rebuilds")
-        if self.lower == self.upper:
-            leave_hi = leave_hi | leave_lo
-            leave_lo = torch.zeros_like(leave_lo)
+        order = torch.argsort(code, stable=True)
+        keep = order[:n_stay]
+        moving = {self.lower: order[n_stay:n_stay + n_lo]}
+        if self.upper != self.lower:
+            moving[self.upper] = order[n_stay + n_lo:n_stay + n_lo + n_hi]
         counts, rows = {}, {}
         for p in self.peers:
-            sel = torch.zeros_like(stay)
-            if p == self.lower:
-                sel |= leave_lo
-            if p == self.upper:
-                sel |= leave_hi
-            idx = torch.nonzero(sel).flatten()
+            idx = moving[p]
             cols = [self.pos[idx], self.types[idx].double().unsqueeze(1),
                     self.ids[idx].double().unsqueeze(1)]
             if self.payload is not None:
                 cols.append(self.payload[idx])
             rows[p] = torch.cat(cols, dim=1)
             counts[p] = torch.tensor([idx.numel()], dtype=torch.int64, device=self.device)
-        keep = torch.nonzero(stay).flatten()
-        self.migrated = sum(int(r.shape[0]) for r in rows.values())
+        self.migrated = n_lo + n_hi
         self.pos, self.types, self.ids = self.pos[keep], self.types[keep], self.ids[keep]
         if self.payload is not None:
             self.payload = self.payload[keep]
@@ -207,8 +208,11 @@ class SlabDomain:
         neighbour); counts hold both segment sizes."""
         torch = _torch()
         fx = self._frac_x(self.pos)
-        near_lo = torch.nonzero(fx < self.lo + self.h).flatten()
-        near_hi = torch.nonzero(fx >= self.hi - self.h).flatten()
+        m_lo = fx < self.lo + self.h
+        m_hi = fx >= self.hi - self.h
+        c_lo, c_hi = torch.stack([m_lo.sum(), m_hi.sum()]).tolist()   # one host read
+        near_lo = torch.argsort((~m_lo).to(torch.int8), stable=True)[:c_lo]
+        near_hi = torch.argsort((~m_hi).to(torch.int8), stable=True)[:c_hi]
         empty = torch.zeros(0, dtype=torch.int64, device=self.device)
         counts, rows = {}, {}
         self.send_idx = {}
@@ -228,7 +232,7 @@ class SlabDomain:
         lo_parts, hi_parts = [], []
         self._recv_split = {}
         for q in self.peers:
-            c = [int(v) for v in counts[q].tolist()]
+            c = counts[q] if isinstance(counts[q], list) else [int(v) for v in counts[q].tolist()]
             r = rows[q]
             # q's message: [my lower ghosts (q is my lower), my upper ghosts (q is my upper)]
             self._recv_split[q] = c
@@ -347,16 +351,19 @@ class DistributedSlab:
         counts, rows = d.pack_migration()
         rc = p2p_exchange(self.dist, counts, {q: (1,) for q in d.peers}, torch.int64, d.device,
                           self.group)
+        n_in = torch.cat([rc[q] for q in d.peers]).tolist()   # one host read
         w = d.row_width()
-        recv = p2p_exchange(self.dist, rows, {q: (int(rc[q][0]), w) for q in d.peers},
+        recv = p2p_exchange(self.dist, rows, {q: (n, w) for q, n in zip(d.peers, n_in)},
                             torch.float64, d.device, self.group)
         d.unpack_migration(recv)
         counts, rows = d.pack_halo()
         hc = p2p_exchange(self.dist, counts, {q: (2,) for q in d.peers}, torch.int64, d.device,
                           self.group)
-        hr = p2p_exchange(self.dist, rows, {q: (int(hc[q].sum()), 2) for q in d.peers},
+        flat = torch.cat([hc[q] for q in d.peers]).tolist()   # one host read
+        hcl = {q: flat[2 * k:2 * k + 2] for k, q in enumerate(d.peers)}
+        hr = p2p_exchange(self.dist, rows, {q: (sum(hcl[q]), 2) for q in d.peers},
                           torch.int64, d.device, self.group)
-        d.unpack_halo(hc, hr)
+        d.unpack_halo(hcl, hr)
 
     def positions(self):
         torch = _torch()
