@@ -251,6 +251,14 @@ class SlabDomain:
         sh = torch.as_tensor(self.shift_hi, dtype=torch.float64, device=self.device)
         self._ghost_shift = torch.cat([sl.expand(self.n_ghost_lo, 3),
                                        sh.expand(self.n_ghost_hi, 3)]) - self._origin_t
+        # per-step buffers: the local positions (the ghosts are received in
+        # place), one send buffer per neighbour, the returned ghost forces
+        n = self.n_own
+        self._local = torch.empty((n + self.n_ghost, 3), dtype=torch.float64, device=self.device)
+        self._send = {p: torch.empty((int(idx.numel()), 3), dtype=torch.float64,
+                                     device=self.device) for p, idx in self.send_idx.items()}
+        self._frecv = {p: torch.empty((int(idx.numel()), 3), dtype=torch.float64,
+                                      device=self.device) for p, idx in self.send_idx.items()}
         self.rebuilds += 1
 
     def recv_halo_counts(self):
@@ -265,50 +273,60 @@ class SlabDomain:
         return {q: sum(c) if (q == self.lower and q == self.upper) else
                 (c[0] if q == self.lower else c[1]) for q, c in self._recv_split.items()}
 
+    def _ghost_rows(self, q):
+        """Row range of the local arrays that peer q's message covers: its
+        lower-ghost segment and / or its upper-ghost segment, which are
+        adjacent (the lower block, the upper block, or both at two ranks)."""
+        n, lo, hi = self.n_own, self.n_ghost_lo, self.n_ghost_hi
+        a = n if q == self.lower else n + lo
+        b = n + lo + hi if q == self.upper else n + lo
+        return a, b
+
     def pack_positions(self):
-        """{peer: float64 [m, 3]} current positions of the halo atoms."""
-        return {p: self.pos[idx] for p, idx in self.send_idx.items()}
+        """{peer: float64 [m, 3]} current positions of the halo atoms (into
+        the send buffers; gathered in the order of the send lists)."""
+        torch = _torch()
+        out = {}
+        for p, idx in self.send_idx.items():
+            torch.index_select(self.pos, 0, idx, out=self._send[p])
+            out[p] = self._send[p]
+        return out
+
+    def recv_views(self):
+        """{peer: the rows of the local positions its message lands in}."""
+        return {q: self._local[slice(*self._ghost_rows(q))] for q in self.peers}
+
+    def finish_positions(self):
+        """Local positions [owned | lower ghosts | upper ghosts] in the frame
+        of the stretched local cell, once the ghost rows hold the received
+        box-frame positions."""
+        torch = _torch()
+        n = self.n_own
+        self._local[n:] += self._ghost_shift
+        torch.sub(self.pos, self._origin_t, out=self._local[:n])
+        return self._local
 
     def unpack_positions(self, msgs):
-        """Local positions [owned | lower ghosts | upper ghosts] in the frame
-        of the stretched local cell."""
-        torch = _torch()
-        lo_parts, hi_parts = [], []
-        for q in self.peers:
-            c = self._recv_split[q]
-            m = msgs[q]
-            if q == self.lower:
-                lo_parts.append(m[:c[0]])
-            if q == self.upper:
-                hi_parts.append(m[c[0]:c[0] + c[1]])
-        ghosts = torch.cat(lo_parts + hi_parts) if (lo_parts or hi_parts) else \
-            torch.zeros((0, 3), dtype=torch.float64, device=self.device)
-        return torch.cat([self.pos - self._origin_t, ghosts + self._ghost_shift])
+        for q, view in self.recv_views().items():
+            view.copy_(msgs[q])
+        return self.finish_positions()
 
     def local_types(self):
         return _torch().cat([self.types, self.ghost_types])
 
     def pack_forces(self, forces):
         """{peer: float64 [m, 3]} ghost rows of the local forces, in the
-        order the peer sent those atoms."""
-        torch = _torch()
-        n = self.n_own
-        lo = forces[n:n + self.n_ghost_lo]
-        hi = forces[n + self.n_ghost_lo:n + self.n_ghost]
-        out = {}
-        for q in self.peers:
-            parts = []
-            if q == self.lower:
-                parts.append(lo)
-            if q == self.upper:
-                parts.append(hi)
-            out[q] = torch.cat(parts) if len(parts) > 1 else parts[0]
-        return out
+        order the peer sent those atoms (views, no copy)."""
+        return {q: forces[slice(*self._ghost_rows(q))] for q in self.peers}
+
+    def force_recv_buffers(self):
+        return self._frecv
 
     def unpack_forces(self, forces, msgs):
         """Owned forces: own rows plus the ghost forces returned by the
-        neighbours (newton-on reverse communication)."""
-        f = forces[:self.n_own].clone()
+        neighbours (newton-on reverse communication), added in place into
+        the owned rows of `forces`; returns that view."""
+        f = forces[:self.n_own]
         for p, idx in self.send_idx.items():
             if idx.numel():
                 f.index_add_(0, idx, msgs[p])
@@ -324,6 +342,11 @@ def p2p_exchange(dist, sends: Dict[int, object], recv_shapes: Dict[int, tuple], 
     torch = _torch()
     recvs = {q: torch.empty(shape, dtype=dtype, device=device) for q, shape in
              recv_shapes.items()}
+    return p2p_exchange_into(dist, sends, recvs, group)
+
+
+def p2p_exchange_into(dist, sends: Dict[int, object], recvs: Dict[int, object], group=None):
+    """p2p_exchange into preallocated (contiguous) receive tensors."""
     ops = []
     for p, t in sends.items():
         if t.numel():
@@ -366,20 +389,14 @@ class DistributedSlab:
         d.unpack_halo(hcl, hr)
 
     def positions(self):
-        torch = _torch()
         d = self.d
-        rc = d.recv_counts()
-        msgs = p2p_exchange(self.dist, d.pack_positions(), {q: (rc[q], 3) for q in d.peers},
-                            torch.float64, d.device, self.group)
-        return d.unpack_positions(msgs)
+        p2p_exchange_into(self.dist, d.pack_positions(), d.recv_views(), self.group)
+        return d.finish_positions()
 
     def forces(self, local_forces):
-        torch = _torch()
         d = self.d
-        sc = d.send_counts()
-        msgs = p2p_exchange(self.dist, d.pack_forces(local_forces),
-                            {q: (sc[q], 3) for q in d.peers}, torch.float64, d.device,
-                            self.group)
+        msgs = p2p_exchange_into(self.dist, d.pack_forces(local_forces), d.force_recv_buffers(),
+                                 self.group)
         return d.unpack_forces(local_forces, msgs)
 
     def totals(self, t):
@@ -464,18 +481,16 @@ class SlabEFS:
         dev = d.device
         self._offs = torch.tensor([0, n_local], dtype=torch.int32, device=dev)
         self._types = d.local_types().contiguous()
-        self._e = torch.zeros(1, dtype=torch.float64, device=dev)
         self._f = torch.zeros((n_local, 3), dtype=torch.float64, device=dev)
-        self._s = torch.zeros((1, 9), dtype=torch.float64, device=dev)
         self._built = False
 
     def compute(self):
         x = self.t.positions()
-        self.gpu.efs_device(self._offs, self._cell, self._pbc, x, self._types, self._e, self._f,
-                            self._s, reuse_neighbors=self._built)
+        # energy and virial land in the vector that is all-reduced
+        self.gpu.efs_device(self._offs, self._cell, self._pbc, x, self._types,
+                            self.totals[0:1], self._f, self.totals[1:].view(1, 9),
+                            reuse_neighbors=self._built)
         self._built = True
         f_own = self.t.forces(self._f)
-        self.totals[0:1].copy_(self._e)
-        self.totals[1:].copy_(self._s.view(-1))
         self.t.totals(self.totals)
         return f_own, self.totals
