@@ -58,12 +58,14 @@ TRAIN_UNIT = "configs/s"
 TRAIN_WEIGHTS = (1.0, 0.01, 0.001, 1.0, 0.0, 1.0)   # E, F, S and the default powers
 EV_PER_GPA_A3 = 1.0 / 160.21766208                    # 1 GPa * 1 A^3 in eV
 
-# DRAM traffic (read + write) per atom of each kernel, from the ncu capture
-# summarised in profiles/ncu_moments_graph_config3-131k_l20.md (131,072 atoms;
-# traffic grows with the atom count, so it is scaled by atoms)
+# DRAM traffic (read + write) per atom of each kernel, from the ncu captures
+# summarised in profiles/ncu_moments_graph_config3-131k_l20.md (forward and
+# graph) and profiles/ncu_moments_rev_active_config3-md-131k_l20.md (the
+# reverse kernel's active-edge variant that the skin of the MD steps selects);
+# 131,072 atoms, scaled by atoms
 NCU_TRAFFIC_BYTES_PER_ATOM = {"k_moments<fwd>": (179.81e6 + 255.75e6) / 131072,
                               "k_dag": (310.19e6 + 263.53e6) / 131072,
-                              "k_moments<rev>": (491.38e6 + 133.67e6) / 131072}
+                              "k_moments<rev>": (671.72e6 + 178.37e6) / 131072}
 SMEM_BYTES_PER_SM_CLOCK = 128   # shared-memory bandwidth of an SM (nominal)
 
 
