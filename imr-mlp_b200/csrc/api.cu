@@ -302,19 +302,32 @@ int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offse
     // staged through their active edges; the training kernels keep the full
     // list and its degree table
     if (beyond_cutoff && nedges > 0 && ncenter > 0) {
-        int *active = c->arena.get<int>("active_edges", nedges + 1);
-        int *nact = c->arena.get<int>("active_count", ncenter + 1);
-        int *gmax = c->arena.get<int>("group_maxdeg_active", c->npad / 32 + 1);
-        if (!active || !nact || !gmax)
+        ActiveEdges act;
+        act.active = c->arena.get<int>("active_edges", nedges + 1);
+        act.nact = c->arena.get<int>("active_count", ncenter + 1);
+        act.group_maxdeg = c->arena.get<int>("group_maxdeg_active", c->npad / 32 + 1);
+        act.cx = c->arena.get<double>("active_rx", nedges + 1);
+        act.cy = c->arena.get<double>("active_ry", nedges + 1);
+        act.cz = c->arena.get<double>("active_rz", nedges + 1);
+        act.cnbr = c->arena.get<int>("active_nbr", nedges + 1);
+        act.cpair = c->arena.get<int>("active_pair", nedges + 1);
+        if (!act.active || !act.nact || !act.group_maxdeg || !act.cx || !act.cy || !act.cz ||
+            !act.cnbr || !act.cpair)
             return fail(MTPB_ERR_MEMORY, "device allocation for the active edges failed");
         NvtxRange range("mtpb:active_edges");
-        CUDA_TRY(launch_active_edges(a, active, nact, gmax, reverse ? dx : nullptr,
-                                     reverse ? dy : nullptr, reverse ? dz : nullptr, c->stream),
+        CUDA_TRY(launch_active_edges(a, act, reverse ? dx : nullptr, reverse ? dy : nullptr,
+                                     reverse ? dz : nullptr, c->stream),
                  "active edges");
         c->launches += 2;
-        a.active = active;
-        a.nact = nact;
-        a.group_maxdeg = gmax;
+        // the moment kernels stage the compacted active edges
+        a.active = act.active;
+        a.nact = act.nact;
+        a.group_maxdeg = act.group_maxdeg;
+        a.nbr = act.cnbr;
+        a.rx = act.cx;
+        a.ry = act.cy;
+        a.rz = act.cz;
+        a.pair = act.cpair;
     }
     CUDA_TRY(cudaEventRecord(c->ev[1], c->stream), "event");
     {

@@ -45,23 +45,29 @@ template <class S, bool REV> constexpr int smem_doubles(int K, int R)
     return n;
 }
 
-// Edge id of staging slot `slot` of centre `atom`: through the active-edge
-// list (ACT) or directly; false past the centre's (active) edges.  ACT is a
-// compile-time choice so that each moment kernel carries one path only (the
-// reverse kernel runs at the limit of the instruction cache).
+// Edge slot `slot` of centre `atom` in the staged arrays (the compacted
+// active edges under ACT, else the list itself); false past the centre's
+// (active) edges.  ACT is a compile-time choice so that each moment kernel
+// carries one path only (the reverse kernel runs at the limit of the
+// instruction cache).
 template <bool ACT>
 __device__ __forceinline__ bool slot_edge(const EdgeArgs &p, int atom, int slot, int &e)
 {
     const int b = __ldg(p.offsets + atom);
-    if constexpr (ACT) {
-        if (slot >= __ldg(p.nact + atom))
-            return false;
-        e = __ldg(p.active + b + slot);
-        return true;
-    } else {
-        e = b + slot;
+    e = b + slot;
+    if constexpr (ACT)
+        return slot < __ldg(p.nact + atom);
+    else
         return e < __ldg(p.offsets + atom + 1);
-    }
+}
+
+// List index of staged edge slot e (where its derivatives are stored)
+template <bool ACT> __device__ __forceinline__ int list_edge(const EdgeArgs &p, int e)
+{
+    if constexpr (ACT)
+        return __ldg(p.active + e);
+    else
+        return e;
 }
 
 struct StageView {
@@ -418,6 +424,7 @@ __device__ __forceinline__ void rev_warp(const EdgeArgs &p, const StageView &v, 
             int e;
             if (!slot_edge<ACT>(p, at, ch * KS + k, e))
                 continue;
+            e = list_edge<ACT>(p, e);
             double sx = 0.0, sy = 0.0, sz = 0.0;
 #pragma unroll
             for (int w = 0; w < NWB; ++w) {
@@ -592,14 +599,14 @@ int shape_slot(int id, int mu, int a, int b, int c)
 // ----------------------------------------------------------------------------
 // Active-edge lists: one warp per centre tests its edges against the pair
 // cutoff with the staging arithmetic (r = sqrt((x*x + y*y) + z*z), the pair's
-// rmax, atoms of type -1 and r = 0 excluded) and compacts the active edge ids
-// in list order with a ballot, so that the moment kernels stage the same
-// edges in the same order as without the list and skip only slots that would
+// rmax, atoms of type -1 and r = 0 excluded) and compacts the active edges in
+// list order with a ballot: their list ids, vectors, neighbours and species
+// pairs, so that the moment kernels stage the same edges in the same order as
+// without the list, read them contiguously, and skip only slots that would
 // add exact zeros.  Inactive edges get zero derivatives.
 // ----------------------------------------------------------------------------
-__global__ void k_active_edges(EdgeArgs p, int *__restrict__ active, int *__restrict__ nact,
-                               double *__restrict__ dx, double *__restrict__ dy,
-                               double *__restrict__ dz)
+__global__ void k_active_edges(EdgeArgs p, ActiveEdges out, double *__restrict__ dx,
+                               double *__restrict__ dy, double *__restrict__ dz)
 {
     const int lane = threadIdx.x & 31;
     const int atom = (int)(((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
@@ -611,16 +618,20 @@ __global__ void k_active_edges(EdgeArgs p, int *__restrict__ active, int *__rest
     for (int base = b; base < end; base += 32) {
         const int e = base + lane;
         bool act = false;
+        int pair = -1, j = 0;
+        double x = 0.0, y = 0.0, z = 0.0;
         if (e < end) {
-            int pair;
+            j = __ldg(p.nbr + e);
             if (p.pair) {
                 pair = __ldg(p.pair + e);
             } else {
-                const int jt = __ldg(p.types + __ldg(p.nbr + e));
+                const int jt = __ldg(p.types + j);
                 pair = (it >= 0 && jt >= 0) ? it * p.K + jt : -1;
             }
             if (pair >= 0) {
-                const double x = __ldg(p.rx + e), y = __ldg(p.ry + e), z = __ldg(p.rz + e);
+                x = __ldg(p.rx + e);
+                y = __ldg(p.ry + e);
+                z = __ldg(p.rz + e);
                 const double r2 = __dadd_rn(__dadd_rn(__dmul_rn(x, x), __dmul_rn(y, y)),
                                             __dmul_rn(z, z));
                 // the staging's test is sqrt(r2) <= rmax (sqrt correctly
@@ -640,12 +651,19 @@ __global__ void k_active_edges(EdgeArgs p, int *__restrict__ active, int *__rest
             }
         }
         const unsigned m = __ballot_sync(0xffffffffu, act);
-        if (act)
-            active[b + count + __popc(m & ((1u << lane) - 1u))] = e;
+        if (act) {
+            const int slot = b + count + __popc(m & ((1u << lane) - 1u));
+            out.active[slot] = e;
+            out.cx[slot] = x;
+            out.cy[slot] = y;
+            out.cz[slot] = z;
+            out.cnbr[slot] = j;
+            out.cpair[slot] = pair;
+        }
         count += __popc(m);
     }
     if (lane == 0)
-        nact[atom] = count;
+        out.nact[atom] = count;
 }
 
 __global__ void k_group_max_count(int natoms, const int *__restrict__ count, int *out)
@@ -659,14 +677,15 @@ __global__ void k_group_max_count(int natoms, const int *__restrict__ count, int
         out[atom >> 5] = deg;
 }
 
-cudaError_t launch_active_edges(const EdgeArgs &a, int *active, int *nact, int *group_maxdeg,
-                                double *dx, double *dy, double *dz, cudaStream_t s)
+cudaError_t launch_active_edges(const EdgeArgs &a, const ActiveEdges &out, double *dx, double *dy,
+                                double *dz, cudaStream_t s)
 {
     if (a.natoms == 0)
         return cudaSuccess;
     const long threads = 32L * a.natoms;
-    k_active_edges<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(a, active, nact, dx, dy, dz);
-    k_group_max_count<<<(a.natoms + 255) / 256, 256, 0, s>>>(a.natoms, nact, group_maxdeg);
+    k_active_edges<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(a, out, dx, dy, dz);
+    k_group_max_count<<<(a.natoms + 255) / 256, 256, 0, s>>>(a.natoms, out.nact,
+                                                             out.group_maxdeg);
     return cudaGetLastError();
 }
 

@@ -148,8 +148,10 @@ struct EdgeArgs {
     const double *rx, *ry, *rz;  // [E]
     const int *pair;             // [E] species pair it*K+jt (-1: a type is -1), or NULL
     const int *group_maxdeg;     // [ceil(natoms/32)]
-    // optional active-edge list (edges inside the pair cutoff): the k-th
-    // active edge of centre i is active[offsets[i] + k], k < nact[i]; NULL
+    // optional active edges (inside the pair cutoff): centre i has nact[i]
+    // of them, compacted in list order to slots offsets[i] .. offsets[i] +
+    // nact[i] - 1 of nbr, rx, ry, rz and pair, and active[offsets[i] + k] is
+    // the list index of its k-th (where the per-edge derivatives go); NULL
     // stages every edge of the list
     const int *active;
     const int *nact;
@@ -164,12 +166,19 @@ struct EdgeArgs {
 int moment_kernel_parts(int shape, bool rev);
 int grad_kernel_launches(int shape, bool edge);
 cudaError_t launch_moments_fwd(int shape, const EdgeArgs &a, double *basic, cudaStream_t s);
-// Active-edge list of a neighbour list whose edges may reach beyond the pair
-// cutoff (a skin or a caller's list): active/nact as in EdgeArgs, the largest
-// active count of every 32-centre group in group_maxdeg, and zero per-edge
-// derivatives dx/dy/dz (may be NULL) for the inactive edges.
-cudaError_t launch_active_edges(const EdgeArgs &a, int *active, int *nact, int *group_maxdeg,
-                                double *dx, double *dy, double *dz, cudaStream_t s);
+// Active edges of a neighbour list whose edges may reach beyond the pair
+// cutoff (a skin or a caller's list): active/nact as in EdgeArgs, the active
+// edges' vectors, neighbours and species pairs compacted into cx, cy, cz,
+// cnbr, cpair, the largest active count of every 32-centre group in
+// group_maxdeg, and zero per-edge derivatives dx/dy/dz (may be NULL) for the
+// inactive edges.
+struct ActiveEdges {
+    int *active, *nact, *group_maxdeg;
+    double *cx, *cy, *cz;
+    int *cnbr, *cpair;
+};
+cudaError_t launch_active_edges(const EdgeArgs &a, const ActiveEdges &out, double *dx, double *dy,
+                                double *dz, cudaStream_t s);
 cudaError_t launch_moments_rev(int shape, const EdgeArgs &a, const double *adjoint, double *dx,
                                double *dy, double *dz, cudaStream_t s);
 size_t dag_ring_bytes(int atoms);
