@@ -287,7 +287,7 @@ EdgeArgs edge_args(const mtpb_context *c, int ncenter, const int *types, const i
 int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offsets,
                 const int *nbr, const double *rx, const double *ry, const double *rz,
                 double *site_energy, double *dx, double *dy, double *dz, bool reverse,
-                long nedges, bool beyond_cutoff)
+                long nedges, bool beyond_cutoff, const EdgeRefresh *refresh)
 {
     c->npad = ((ncenter + 31) / 32) * 32;
     c->d_group_maxdeg = c->arena.get<int>("group_maxdeg", c->npad / 32 + 1);
@@ -301,6 +301,8 @@ int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offse
     // lists that hold pairs beyond the cutoff (a skin, a caller's list) are
     // staged through their active edges; the training kernels keep the full
     // list and its degree table
+    if (refresh && !(beyond_cutoff && nedges > 0 && ncenter > 0))
+        return fail(MTPB_ERR_STATE, "edge refresh without an active-edge pass");
     if (beyond_cutoff && nedges > 0 && ncenter > 0) {
         ActiveEdges act;
         act.active = c->arena.get<int>("active_edges", nedges + 1);
@@ -315,8 +317,8 @@ int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offse
             !act.cnbr || !act.cpair)
             return fail(MTPB_ERR_MEMORY, "device allocation for the active edges failed");
         NvtxRange range("mtpb:active_edges");
-        CUDA_TRY(launch_active_edges(a, act, reverse ? dx : nullptr, reverse ? dy : nullptr,
-                                     reverse ? dz : nullptr, c->stream),
+        CUDA_TRY(launch_active_edges(a, act, refresh, reverse ? dx : nullptr,
+                                     reverse ? dy : nullptr, reverse ? dz : nullptr, c->stream),
                  "active edges");
         c->launches += 2;
         // the moment kernels stage the compacted active edges
@@ -773,6 +775,7 @@ int mtpb_build_neighbors(mtpb_context *c, const mtpb_structures *in, int memory)
     c->have_list = true;
     c->edge_epoch++;
     c->nb_built_this_call = true;
+    c->refresh_pending = false;
     // struct ids, wrap/bin, 3 scans (2 kernels each), cell fill, sort and
     // position gather, count, fill, position packing and displacements,
     // in-edge count, fill and sort, edge species pairs
@@ -854,9 +857,12 @@ int mtpb::efs_compute(mtpb_context *c, int memory, const mtpb_efs_output *out,
                                                  : c->arena.get<double>("stress", 9 * (size_t)S + 9);
     if (!site_energy || !dx || !dy || !dz || !forces || !avir || !partials || !energy || !stress)
         return fail(MTPB_ERR_MEMORY, "device allocation failed");
-    // with a skin the list holds pairs up to r_c + skin
+    // with a skin the list holds pairs up to r_c + skin; a pending refresh
+    // of its vectors runs in the active-edge pass
+    const EdgeRefresh *refresh = c->refresh_pending ? &c->refresh : nullptr;
+    c->refresh_pending = false;
     rc = run_moments(c, N, c->d_types, c->nb.offsets, c->nb.nbr, c->nb.rx, c->nb.ry, c->nb.rz,
-                     site_energy, dx, dy, dz, forces_needed, E, c->skin > 0.0);
+                     site_energy, dx, dy, dz, forces_needed, E, c->skin > 0.0, refresh);
     if (rc)
         return rc;
     NvtxRange range_gather("mtpb:force_gather_reduce");
@@ -953,17 +959,31 @@ int mtpb_efs_structures(mtpb_context *c, const mtpb_structures *in, int memory,
         if (!unwrapped)
             return fail(MTPB_ERR_MEMORY, "device allocation failed");
         CUDA_TRY(cudaEventRecord(c->ev[0], c->stream), "event");
+        // with a skin the compute's active-edge pass recomputes the vectors
+        // while it tests them (one pass over the list instead of two)
+        const bool fused = c->skin > 0.0 && c->nedges > 0 && c->natoms > 0;
         {
             NvtxRange range("mtpb:refresh_edges");
-            CUDA_TRY(refresh_edges(N, c->d_ns, c->nb.struct_of, c->nb, c->d_x_build, x,
-                                   unwrapped, const_cast<double *>(c->nb.rx),
-                                   const_cast<double *>(c->nb.ry),
-                                   const_cast<double *>(c->nb.rz), c->stream),
-                     "refresh edge vectors");
+            if (fused)
+                CUDA_TRY(unwrap_positions(N, c->nb, c->d_x_build, x, unwrapped, c->stream),
+                         "unwrap positions");
+            else
+                CUDA_TRY(refresh_edges(N, c->d_ns, c->nb.struct_of, c->nb, c->d_x_build, x,
+                                       unwrapped, const_cast<double *>(c->nb.rx),
+                                       const_cast<double *>(c->nb.ry),
+                                       const_cast<double *>(c->nb.rz), c->stream),
+                         "refresh edge vectors");
+        }
+        if (fused) {
+            c->refresh = EdgeRefresh{c->d_ns, c->nb.struct_of, c->nb.shift, unwrapped,
+                                     const_cast<double *>(c->nb.rx),
+                                     const_cast<double *>(c->nb.ry),
+                                     const_cast<double *>(c->nb.rz)};
+            c->refresh_pending = true;
         }
         c->edge_epoch++;
         c->nb_built_this_call = true;   // ev[0] marks the refresh
-        c->pending_launches = c->nedges ? 2 : 0;
+        c->pending_launches = c->nedges ? (fused ? 1 : 2) : 0;
     }
     return mtpb_efs_compute(c, memory, out);
 }

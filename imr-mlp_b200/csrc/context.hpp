@@ -93,6 +93,10 @@ struct mtpb_context {
     bool have_efs = false;
     bool have_dedr = false;   // the last EFS call ran the reverse pass
     long edge_epoch = 0;     // advanced whenever the edge list or its vectors change
+    // a reuse step with a skin leaves the edge vectors to the active-edge pass
+    // of the next compute (one shot)
+    mtpb::EdgeRefresh refresh{};
+    bool refresh_pending = false;
     int dag_atoms_env = 0;   // MTPB_DAG_ATOMS override of the graph block width
     bool force_global_rows = false;   // MTPB_DAG_GLOBAL_ROWS=1
     // pinned staging of the per-build segment tables; stage_ev marks the end of
@@ -113,10 +117,12 @@ EdgeArgs edge_args(const mtpb_context *c, int ncenter, const int *types, const i
                    const int *nbr, const double *rx, const double *ry, const double *rz);
 // beyond_cutoff: the list may hold pairs beyond the model cutoff (a skin or a
 // caller's list), which are then skipped through an active-edge list
+// refresh (may be NULL, needs beyond_cutoff): the list's edge vectors are
+// recomputed by the active-edge pass
 int run_moments(mtpb_context *c, int ncenter, const int *types, const int *offsets,
                 const int *nbr, const double *rx, const double *ry, const double *rz,
                 double *site_energy, double *dx, double *dy, double *dz, bool reverse,
-                long nedges, bool beyond_cutoff);
+                long nedges, bool beyond_cutoff, const EdgeRefresh *refresh = nullptr);
 int efs_compute(mtpb_context *c, int memory, const mtpb_efs_output *out, bool forces_needed);
 int csr_compute(mtpb_context *c, const mtpb_csr_request *req, int memory);
 int lammps_compute(mtpb_context *c, const mtpb_lammps_request *req);

@@ -22,6 +22,7 @@
 #include "internal.hpp"
 #include "moments.cuh"
 #include "dag.cuh"
+#include "refresh.cuh"
 
 #include <algorithm>
 #include <cstdio>
@@ -603,10 +604,13 @@ int shape_slot(int id, int mu, int a, int b, int c)
 // list order with a ballot: their list ids, vectors, neighbours and species
 // pairs, so that the moment kernels stage the same edges in the same order as
 // without the list, read them contiguously, and skip only slots that would
-// add exact zeros.  Inactive edges get zero derivatives.
+// add exact zeros.  Inactive edges get zero derivatives.  With `rf`, the
+// vectors of all listed edges are first recomputed from the moved positions
+// and stored (the edge-parallel refresh pass folded into this one).
 // ----------------------------------------------------------------------------
-__global__ void k_active_edges(EdgeArgs p, ActiveEdges out, double *__restrict__ dx,
-                               double *__restrict__ dy, double *__restrict__ dz)
+__global__ void k_active_edges(EdgeArgs p, ActiveEdges out, EdgeRefresh rf,
+                               double *__restrict__ dx, double *__restrict__ dy,
+                               double *__restrict__ dz)
 {
     const int lane = threadIdx.x & 31;
     const int atom = (int)(((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
@@ -628,10 +632,18 @@ __global__ void k_active_edges(EdgeArgs p, ActiveEdges out, double *__restrict__
                 const int jt = __ldg(p.types + j);
                 pair = (it >= 0 && jt >= 0) ? it * p.K + jt : -1;
             }
-            if (pair >= 0) {
+            if (rf.unwrapped) {
+                refresh_vector(rf.structs[__ldg(rf.struct_of + atom)], atom, j,
+                               __ldg(rf.shift + e), rf.unwrapped, x, y, z);
+                rf.rx[e] = x;
+                rf.ry[e] = y;
+                rf.rz[e] = z;
+            } else if (pair >= 0) {
                 x = __ldg(p.rx + e);
                 y = __ldg(p.ry + e);
                 z = __ldg(p.rz + e);
+            }
+            if (pair >= 0) {
                 const double r2 = __dadd_rn(__dadd_rn(__dmul_rn(x, x), __dmul_rn(y, y)),
                                             __dmul_rn(z, z));
                 // the staging's test is sqrt(r2) <= rmax (sqrt correctly
@@ -677,13 +689,17 @@ __global__ void k_group_max_count(int natoms, const int *__restrict__ count, int
         out[atom >> 5] = deg;
 }
 
-cudaError_t launch_active_edges(const EdgeArgs &a, const ActiveEdges &out, double *dx, double *dy,
-                                double *dz, cudaStream_t s)
+cudaError_t launch_active_edges(const EdgeArgs &a, const ActiveEdges &out,
+                                const EdgeRefresh *refresh, double *dx, double *dy, double *dz,
+                                cudaStream_t s)
 {
     if (a.natoms == 0)
         return cudaSuccess;
+    EdgeRefresh rf{};
+    if (refresh)
+        rf = *refresh;
     const long threads = 32L * a.natoms;
-    k_active_edges<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(a, out, dx, dy, dz);
+    k_active_edges<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(a, out, rf, dx, dy, dz);
     k_group_max_count<<<(a.natoms + 255) / 256, 256, 0, s>>>(a.natoms, out.nact,
                                                              out.group_maxdeg);
     return cudaGetLastError();

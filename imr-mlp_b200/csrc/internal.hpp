@@ -177,8 +177,22 @@ struct ActiveEdges {
     double *cx, *cy, *cz;
     int *cnbr, *cpair;
 };
-cudaError_t launch_active_edges(const EdgeArgs &a, const ActiveEdges &out, double *dx, double *dy,
-                                double *dz, cudaStream_t s);
+// Edge vectors of a stored list recomputed from moved positions (refresh.cuh):
+// the structures and structure ids of the build, the packed shift of every
+// edge, the positions as [atom][4] rows relative to the build's images, and
+// the list's vector arrays, overwritten.
+struct NbStruct;
+struct EdgeRefresh {
+    const NbStruct *structs;
+    const int *struct_of;
+    const int *shift;
+    const double *unwrapped;
+    double *rx, *ry, *rz;
+};
+// refresh (may be NULL): the vectors are recomputed first, in the same pass
+cudaError_t launch_active_edges(const EdgeArgs &a, const ActiveEdges &out,
+                                const EdgeRefresh *refresh, double *dx, double *dy, double *dz,
+                                cudaStream_t s);
 cudaError_t launch_moments_rev(int shape, const EdgeArgs &a, const double *adjoint, double *dx,
                                double *dy, double *dz, cudaStream_t s);
 size_t dag_ring_bytes(int atoms);

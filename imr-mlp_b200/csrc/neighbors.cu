@@ -24,6 +24,7 @@
 // so that the output order is deterministic.
 #include "internal.hpp"
 #include "neighbors.hpp"
+#include "refresh.cuh"
 
 #include <cub/cub.cuh>
 
@@ -42,23 +43,6 @@ __device__ __forceinline__ void rowvec_mat(const double p[3], const double *M, d
     out[0] = r[0];
     out[1] = r[1];
     out[2] = r[2];
-}
-
-// Eigen Matrix3d * Vector3d: rows 0,1 (t0 + t1) + t2; row 2 t0 + (t1 + t2).
-__device__ __forceinline__ void image_translation(const NbStruct &st, int s0, int s1, int s2,
-                                                  double t[3])
-{
-    const int sh[3] = {s0, s1, s2};
-    double img[3] = {0.0, 0.0, 0.0};
-#pragma unroll
-    for (int k = 0; k < 3; ++k)
-        if (k < st.dims)
-            img[k] = (double)sh[st.axes[k]];
-#pragma unroll
-    for (int r = 0; r < 2; ++r)
-        t[r] = dadd(dadd(dmul(st.B[r][0], img[0]), dmul(st.B[r][1], img[1])),
-                    dmul(st.B[r][2], img[2]));
-    t[2] = dadd(dmul(st.B[2][0], img[0]), dadd(dmul(st.B[2][1], img[1]), dmul(st.B[2][2], img[2])));
 }
 
 __global__ void k_struct_ids(int nstruct, const int *__restrict__ atom_offsets, int natoms,
@@ -412,27 +396,11 @@ __global__ void k_refresh_edges(long nedges, const NbStruct *__restrict__ struct
     if (e >= nedges)
         return;
     const int i = center[e];
-    const int o = nbr[e];
-    const double2 *P = reinterpret_cast<const double2 *>(p);
-    const double2 i01 = P[2 * (size_t)i], i2 = P[2 * (size_t)i + 1];
-    const double2 o01 = P[2 * (size_t)o], o2 = P[2 * (size_t)o + 1];
-    const double pi[3] = {i01.x, i01.y, i2.x}, po[3] = {o01.x, o01.y, o2.x};
-    const int code = shift[e];
-    const int s0 = (code & 0xff) - 128, s1 = ((code >> 8) & 0xff) - 128,
-              s2 = ((code >> 16) & 0xff) - 128;
-    const bool zero = (s0 == 0 && s1 == 0 && s2 == 0);
-    double t[3] = {0.0, 0.0, 0.0};
-    if (!zero)
-        image_translation(structs[struct_of[i]], s0, s1, s2, t);
-    if (i <= o) {
-        rx[e] = __dsub_rn(zero ? po[0] : dadd(po[0], t[0]), pi[0]);
-        ry[e] = __dsub_rn(zero ? po[1] : dadd(po[1], t[1]), pi[1]);
-        rz[e] = __dsub_rn(zero ? po[2] : dadd(po[2], t[2]), pi[2]);
-    } else {
-        rx[e] = -__dsub_rn(zero ? pi[0] : dadd(pi[0], -t[0]), po[0]);
-        ry[e] = -__dsub_rn(zero ? pi[1] : dadd(pi[1], -t[1]), po[1]);
-        rz[e] = -__dsub_rn(zero ? pi[2] : dadd(pi[2], -t[2]), po[2]);
-    }
+    double x, y, z;
+    refresh_vector(structs[struct_of[i]], i, nbr[e], shift[e], p, x, y, z);
+    rx[e] = x;
+    ry[e] = y;
+    rz[e] = z;
 }
 
 static inline int nblk(long n, int t) { return (int)((n + t - 1) / t); }
@@ -597,6 +565,16 @@ cudaError_t refresh_edges(int natoms, const NbStruct *structs, const int *struct
     k_refresh_edges<<<nblk(nb.nedges, 256), 256, 0, s>>>(nb.nedges, structs, struct_of,
                                                          nb.center, nb.nbr, nb.shift, unwrapped,
                                                          rx, ry, rz);
+    return cudaGetLastError();
+}
+
+cudaError_t unwrap_positions(int natoms, const NbResult &nb, const double *x_build,
+                             const double *x, double *unwrapped, cudaStream_t s)
+{
+    if (natoms == 0)
+        return cudaSuccess;
+    k_unwrapped<<<nblk(natoms, 256), 256, 0, s>>>(natoms, nb.wx, nb.wy, nb.wz, x_build, x,
+                                                  unwrapped);
     return cudaGetLastError();
 }
 

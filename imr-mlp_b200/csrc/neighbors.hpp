@@ -108,6 +108,10 @@ cudaError_t build_in_edges(int ntotal, long nedges, const int *nbr, DeviceArena 
 cudaError_t refresh_edges(int natoms, const NbStruct *structs, const int *struct_of,
                           const NbResult &nb, const double *x_build, const double *x,
                           double *unwrapped, double *rx, double *ry, double *rz, cudaStream_t s);
+// the first half of refresh_edges: only the unwrapped positions (the edge
+// vectors are then recomputed by the active-edge pass, refresh.cuh)
+cudaError_t unwrap_positions(int natoms, const NbResult &nb, const double *x_build,
+                             const double *x, double *unwrapped, cudaStream_t s);
 cudaError_t edge_vectors(int ncenter, const int *offsets, const int *nbr, const double *x,
                          double *rx, double *ry, double *rz, cudaStream_t s);
 cudaError_t edge_pairs(long nedges, const int *center, const int *nbr, const int *types, int K,
