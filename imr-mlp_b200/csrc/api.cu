@@ -988,6 +988,35 @@ int mtpb_efs_structures(mtpb_context *c, const mtpb_structures *in, int memory,
     return mtpb_efs_compute(c, memory, out);
 }
 
+int mtpb_check_device_status(mtpb_context *c)
+{
+    if (!c)
+        return fail(MTPB_ERR_ARGUMENT, "ctx is NULL");
+    int rc = set_device(c);
+    if (rc)
+        return rc;
+    if (!c->d_err)
+        return MTPB_OK;   // no graph kernel has run on this context
+    CUDA_TRY(cudaStreamSynchronize(c->stream), "synchronise");
+    return check_device_error(c);
+}
+
+int mtpb_debug_flag_device_error(mtpb_context *c)
+{
+    if (!c)
+        return fail(MTPB_ERR_ARGUMENT, "ctx is NULL");
+    int rc = set_device(c);
+    if (rc)
+        return rc;
+    if (!c->d_err)
+        return fail(MTPB_ERR_STATE, "load a model first");
+    const int one = 1;
+    CUDA_TRY(cudaMemcpyAsync(c->d_err, &one, sizeof(int), cudaMemcpyHostToDevice, c->stream),
+             "set flag");
+    CUDA_TRY(cudaStreamSynchronize(c->stream), "synchronise");
+    return MTPB_OK;
+}
+
 int mtpb_last_timings(const mtpb_context *c, double *ms)
 {
     if (!c || !ms)

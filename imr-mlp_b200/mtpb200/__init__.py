@@ -333,6 +333,12 @@ class MTPGpuDirect:
         _check(self.lib.mtpb_check_training_values(self.ctx, C.byref(first)))
         return first.value
 
+    def check_device_status(self) -> None:
+        """Synchronises and raises MTPBError (status MTPB_ERR_CUDA) when a
+        graph kernel's bounded wait gave up since the last check (device-
+        memory calls do not check this themselves)."""
+        _check(self.lib.mtpb_check_device_status(self.ctx))
+
     def last_train_timings(self):
         t = np.zeros(6)
         _check(self.lib.mtpb_last_train_timings(self.ctx, _dp(t)))

@@ -129,6 +129,8 @@ SIGNATURES = [
     ("mtpb_last_timings", C.c_int, [C.c_void_p, _dp]),
     ("mtpb_last_train_timings", C.c_int, [C.c_void_p, _dp]),
     ("mtpb_check_training_values", C.c_int, [C.c_void_p, C.POINTER(C.c_long)]),
+    ("mtpb_check_device_status", C.c_int, [C.c_void_p]),
+    ("mtpb_debug_flag_device_error", C.c_int, [C.c_void_p]),
     ("mtpb_set_center_count", C.c_int, [C.c_void_p, C.c_int]),
     ("mtpb_last_launch_count", C.c_int, [C.c_void_p, _ip]),
     ("mtpb_get_site_moments", C.c_int, [C.c_void_p, _dp, _dp]),

@@ -338,6 +338,22 @@ int mtpb_loss_grad(mtpb_context *ctx, const mtpb_labels *labels, const mtpb_loss
  * returns MTPB_ERR_NONFINITE. */
 int mtpb_check_training_values(mtpb_context *ctx, long *first_nonfinite);
 
+/* Status of the device-side waits of the calls made since the last check.
+ * The graph kernels give up a wait on their record stream after a bounded
+ * number of polls and set a device flag instead of hanging (the reference
+ * reports a failed kernel through its CUDA error checks).  Host-memory calls
+ * read the flag themselves and return MTPB_ERR_CUDA; device-memory calls do
+ * not synchronise, so their caller asks here: this call synchronises the
+ * context stream and returns MTPB_ERR_CUDA, clearing the flag, when a wait
+ * gave up (the results of the calls since the last check are then invalid),
+ * else MTPB_OK. */
+int mtpb_check_device_status(mtpb_context *ctx);
+
+/* Test hook: sets the device flag as a wait that gave up would, without
+ * running any kernel, so that a caller's handling of MTPB_ERR_CUDA can be
+ * exercised. */
+int mtpb_debug_flag_device_error(mtpb_context *ctx);
+
 /* ---- diagnostics ---------------------------------------------------------- */
 
 /* Device-side timing of the last mtpb_efs_compute/mtpb_efs_structures call,
