@@ -65,7 +65,7 @@ EV_PER_GPA_A3 = 1.0 / 160.21766208                    # 1 GPa * 1 A^3 in eV
 # 131,072 atoms, scaled by atoms
 NCU_TRAFFIC_BYTES_PER_ATOM = {"k_moments<fwd>": (179.81e6 + 255.75e6) / 131072,
                               "k_dag": (310.19e6 + 263.53e6) / 131072,
-                              "k_moments<rev>": (671.72e6 + 178.37e6) / 131072}
+                              "k_moments<rev>": (672.31e6 + 180.24e6) / 131072}
 SMEM_BYTES_PER_SM_CLOCK = 128   # shared-memory bandwidth of an SM (nominal)
 
 
