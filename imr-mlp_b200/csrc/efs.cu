@@ -1028,15 +1028,20 @@ static cudaError_t launch_dag_geom(const DagPlan &plan, const DagDevRec *recs,
 {
     using G = DagGeom<ATOMS, STREAMS>;
     const int ngroups = (natoms + ATOMS - 1) / ATOMS;
-    const int blocks = GR ? std::min(ngroups, plan.grid) : ngroups;
     const size_t smem = G::ring_bytes() + (GR ? 0 : sizeof(double) * (size_t)plan.nrows * ATOMS);
     auto kern = k_dag<ATOMS, GR, STREAMS>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)smem);
     if (err == cudaSuccess && GR)   // leave the rest of the SM's memory to L1
         err = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 25);
+    // persistent blocks (as many as fit the SMs; with global rows one per SM,
+    // the scratch slices), each looping over atom groups
+    int per = 1;
+    if (err == cudaSuccess && !GR)
+        err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, G::THREADS, smem);
     if (err != cudaSuccess)
         return err;
+    const int blocks = std::min(ngroups, plan.grid * std::max(per, 1));
     kern<<<blocks, G::THREADS, smem, s>>>(recs, phase_row0, plan.n_fwd, plan.n_rev, plan.one_row,
                                           plan.zero_row, plan.nrows, nslot, natoms, npad, types,
                                           species_coeffs, basic, adjoint, site_energy, gscratch,
