@@ -478,23 +478,35 @@ __global__ void __launch_bounds__(ShapeCfg<S>::NW * 32, KCfg<S, REV>::BLOCKS)
     v.pairs = pairs;
     v.radial = radial;
     __syncthreads();
-    const int group = blockIdx.x;
-    const int atom0 = group * 32;
-    const int maxdeg = __ldg(p.group_maxdeg + group);
     const int warp = threadIdx.x >> 5;
     constexpr int NWT = NW * KCfg<S, REV>::NPART;
     constexpr int SUB = KCfg<S, REV>::SUB;
-    static_for<NW>([&](auto iw) {
-        constexpr int WL = decltype(iw)::value;
-        constexpr int W = PART * NW + WL;
-        if (warp == WL) {
-            if constexpr (REV)
-                rev_warp<S, NWT * SUB, W, SUB, NW, PART == 0, RG, ACT>(p, v, atom0, maxdeg, adjoint,
-                                                                  dx, dy, dz);
-            else
-                fwd_warp<S, NWT * SUB, W, SUB, RG, ACT>(p, v, atom0, maxdeg, basic);
-        }
-    });
+    auto run_group = [&](int group) {
+        const int atom0 = group * 32;
+        const int maxdeg = __ldg(p.group_maxdeg + group);
+        static_for<NW>([&](auto iw) {
+            constexpr int WL = decltype(iw)::value;
+            constexpr int W = PART * NW + WL;
+            if (warp == WL) {
+                if constexpr (REV)
+                    rev_warp<S, NWT * SUB, W, SUB, NW, PART == 0, RG, ACT>(p, v, atom0, maxdeg,
+                                                                      adjoint, dx, dy, dz);
+                else
+                    fwd_warp<S, NWT * SUB, W, SUB, RG, ACT>(p, v, atom0, maxdeg, basic);
+            }
+        });
+    };
+    // the forward kernel runs persistent blocks, each taking groups of 32
+    // centres in turn (the chunk loops end on a barrier, so the staging is
+    // free between groups); the reverse kernel one block per group, its code
+    // as it was (it runs at the limit of the instruction cache)
+    if constexpr (REV) {
+        run_group(blockIdx.x);
+    } else {
+        const int ngroups = (p.natoms + 31) / 32;
+        for (int group = blockIdx.x; group < ngroups; group += gridDim.x)
+            run_group(group);
+    }
 }
 
 template <class S, bool REV> static cudaError_t launch_shape(const EdgeArgs &a, double *basic,
@@ -517,8 +529,19 @@ template <class S, bool REV> static cudaError_t launch_shape(const EdgeArgs &a, 
                                  : (a.active ? k_moments<S, REV, P, false, true>
                                              : k_moments<S, REV, P, false, false>);
         err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        // persistent forward blocks (4.12 -> 4.02 ms at 1M atoms); the reverse
+        // kernel balances better with one block per group (11.0 ms against
+        // 12.1 ms persistent)
+        int per = 1, dev = 0, sms = 1;
+        if (err == cudaSuccess && !REV)
+            err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, NW * 32, smem);
+        if (err == cudaSuccess && !REV)
+            err = cudaGetDevice(&dev);
+        if (err == cudaSuccess && !REV)
+            err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (err == cudaSuccess) {
-            kern<<<groups, NW * 32, smem, s>>>(a, basic, adjoint, dx, dy, dz);
+            const int blocks = REV ? groups : std::min(groups, sms * std::max(per, 1));
+            kern<<<blocks, NW * 32, smem, s>>>(a, basic, adjoint, dx, dy, dz);
             err = cudaGetLastError();
         }
     });
