@@ -496,11 +496,13 @@ __global__ void __launch_bounds__(ShapeCfg<S>::NW * 32, KCfg<S, REV>::BLOCKS)
             }
         });
     };
-    // the forward kernel runs persistent blocks, each taking groups of 32
-    // centres in turn (the chunk loops end on a barrier, so the staging is
-    // free between groups); the reverse kernel one block per group, its code
-    // as it was (it runs at the limit of the instruction cache)
-    if constexpr (REV) {
+    // a forward kernel launched in one part runs persistent blocks, each
+    // taking groups of 32 centres in turn (the chunk loops end on a barrier,
+    // so the staging is free between groups); the reverse kernel and the
+    // multi-part forward kernels run one block per group (the reverse kernel's
+    // code as it was: it runs at the limit of the instruction cache)
+    constexpr bool PERSIST = !REV && KCfg<S, REV>::NPART == 1;
+    if constexpr (!PERSIST) {
         run_group(blockIdx.x);
     } else {
         const int ngroups = (p.natoms + 31) / 32;
@@ -529,18 +531,20 @@ template <class S, bool REV> static cudaError_t launch_shape(const EdgeArgs &a, 
                                  : (a.active ? k_moments<S, REV, P, false, true>
                                              : k_moments<S, REV, P, false, false>);
         err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        // persistent forward blocks (4.12 -> 4.02 ms at 1M atoms); the reverse
-        // kernel balances better with one block per group (11.0 ms against
-        // 12.1 ms persistent)
+        // persistent blocks for a one-part forward kernel (level 20: 4.15 ->
+        // 4.03 ms at 1M atoms); the reverse kernel balances better with one
+        // block per group (11.0 ms against 12.1 ms persistent), and so do the
+        // multi-part level-24 forward kernels (9.3 ms against 9.8 ms)
+        constexpr bool persist = !REV && KCfg<S, REV>::NPART == 1;
         int per = 1, dev = 0, sms = 1;
-        if (err == cudaSuccess && !REV)
+        if (err == cudaSuccess && persist)
             err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, NW * 32, smem);
-        if (err == cudaSuccess && !REV)
+        if (err == cudaSuccess && persist)
             err = cudaGetDevice(&dev);
-        if (err == cudaSuccess && !REV)
+        if (err == cudaSuccess && persist)
             err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (err == cudaSuccess) {
-            const int blocks = REV ? groups : std::min(groups, sms * std::max(per, 1));
+            const int blocks = persist ? std::min(groups, sms * std::max(per, 1)) : groups;
             kern<<<blocks, NW * 32, smem, s>>>(a, basic, adjoint, dx, dy, dz);
             err = cudaGetLastError();
         }
